@@ -1,0 +1,91 @@
+"""ctypes binding of libcuopx.so (the C ABI declared in include/cuopx.h).
+
+The library must exist (built by cuop_b200.build / __graft_entry__.build());
+there is no fallback of any kind: a missing or unloadable library raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+_LIB_PATH = Path(__file__).resolve().parent / "libcuopx.so"
+_lib = None
+
+# Status codes (numerically identical to cuOP's StatusCode).
+SUCCESS = 0
+NOT_IMPLEMENTED = 1001
+TIMEOUT = 1003
+CUDA_ERROR = 2000
+OUT_OF_MEMORY = 3001
+INVALID_ARGUMENT = 4001
+EXECUTION_TIMEOUT = 6002
+KERNEL_NOT_FOUND = 6005
+NOT_COMPILED = 7003
+SHAPE_MISMATCH = 10002
+UNSUPPORTED_TYPE = 11001
+
+STATUS_NAMES = {
+    0: "SUCCESS", 1001: "NOT_IMPLEMENTED", 1003: "TIMEOUT", 2000: "CUDA_ERROR", 3001: "OUT_OF_MEMORY",
+    4001: "INVALID_ARGUMENT", 6002: "EXECUTION_TIMEOUT", 6005: "KERNEL_NOT_FOUND", 7003: "NOT_COMPILED",
+    10002: "SHAPE_MISMATCH", 11001: "UNSUPPORTED_TYPE",
+}
+
+F32, F64, F16, BF16 = 0, 1, 2, 3
+
+_i64, _dbl, _vp, _sz, _int = C.c_int64, C.c_double, C.c_void_p, C.c_size_t, C.c_int
+_fp = C.c_void_p  # float* as raw address
+
+# (name, restype, argtypes) for every symbol in include/cuopx.h
+SIGNATURES = [
+    ("cuopx_version", _int, []),
+    ("cuopx_last_kernel", C.c_char_p, []),
+    ("cuopx_launch_count", _i64, []),
+    ("cuopx_get_device_error", _int, [C.POINTER(_int)]),
+    ("cuopx_clear_device_error", _int, []),
+    ("cuopx_gemm", _int, [_int, _int, _int, _i64, _i64, _i64, _dbl, _vp, _i64, _vp, _i64, _dbl, _vp, _i64, _vp]),
+    ("cuopx_gemm_strided_batched", _int,
+     [_int, _int, _int, _i64, _i64, _i64, _dbl, _vp, _i64, _i64, _vp, _i64, _i64, _dbl, _vp, _i64, _i64, _i64, _vp]),
+    ("cuopx_gemv_workspace_size", _sz, [_int, _int, _i64, _i64]),
+    ("cuopx_gemv", _int, [_int, _int, _i64, _i64, _dbl, _vp, _i64, _vp, _dbl, _vp, _vp, _sz, _vp]),
+    ("cuopx_gather_column_blocks", _int, [_int, _i64, _i64, _i64, _vp, _vp, _i64, _vp]),
+    ("cuopx_vector_workspace_size", _sz, [_i64]),
+    ("cuopx_dot", _int, [_i64, _fp, _i64, _fp, _i64, _fp, _vp, _sz, _vp]),
+    ("cuopx_axpy", _int, [_i64, C.c_float, _fp, _i64, _fp, _i64, _vp]),
+    ("cuopx_scal", _int, [_i64, C.c_float, _fp, _i64, _vp]),
+    ("cuopx_copy", _int, [_i64, _fp, _i64, _fp, _i64, _vp]),
+    ("cuopx_swap", _int, [_i64, _fp, _i64, _fp, _i64, _vp]),
+    ("cuopx_rot", _int, [_i64, _fp, _i64, _fp, _i64, C.c_float, C.c_float, _vp]),
+    ("cuopx_nrm2", _int, [_i64, _fp, _i64, _fp, _vp, _sz, _vp]),
+    ("cuopx_asum", _int, [_i64, _fp, _i64, _fp, _vp, _sz, _vp]),
+    ("cuopx_iamax", _int, [_i64, _fp, _i64, _vp, _vp, _sz, _vp]),
+    ("cuopx_iamin", _int, [_i64, _fp, _i64, _vp, _vp, _sz, _vp]),
+]
+
+
+class CuopError(RuntimeError):
+    def __init__(self, code: int, what: str):
+        super().__init__(f"{what}: {STATUS_NAMES.get(code, code)} ({code})")
+        self.code = code
+
+
+def lib_path() -> Path:
+    return _LIB_PATH
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not _LIB_PATH.exists():
+            raise ImportError(f"{_LIB_PATH} is missing: run `python -m cuop_b200.build` (no fallback path exists)")
+        handle = C.CDLL(str(_LIB_PATH))
+        for name, res, args in SIGNATURES:
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def check(code: int, what: str) -> None:
+    if code != SUCCESS:
+        raise CuopError(code, what)

@@ -1,0 +1,253 @@
+// C-ABI entry points (include/cuopx.h): argument validation, variant
+// selection, launch bookkeeping and the device error word.
+#include <atomic>
+#include <mutex>
+
+#include "common.cuh"
+#include "dispatch.h"
+
+namespace cuopx {
+
+namespace {
+thread_local const char* t_last_kernel = "none";
+std::atomic<int64_t> g_launches{0};
+int g_sm_count[64] = {0};
+
+bool overlaps(const void* a, size_t abytes, const void* b, size_t bbytes) {
+  if (!a || !b || abytes == 0 || bbytes == 0) return false;
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(a), b0 = reinterpret_cast<uintptr_t>(b);
+  return a0 < b0 + bbytes && b0 < a0 + abytes;
+}
+
+// Bytes spanned by a row-major rows x cols matrix with leading dim ld.
+size_t span_bytes(int64_t rows, int64_t cols, int64_t ld, size_t es) {
+  if (rows <= 0 || cols <= 0) return 0;
+  return static_cast<size_t>((rows - 1) * ld + cols) * es;
+}
+}  // namespace
+
+int device_sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (g_sm_count[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    g_sm_count[dev] = n;
+  }
+  return g_sm_count[dev];
+}
+
+void note_launch(const char* name) {
+  t_last_kernel = name;
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+int check_launch() { return cudaGetLastError() == cudaSuccess ? CUOPX_SUCCESS : CUOPX_CUDA_ERROR; }
+
+size_t vector_workspace_size_impl();
+int vector_reduce(int op, int64_t n, const float* x, int64_t incx, const float* y, int64_t incy, float* fres,
+                  int64_t* ires, void* workspace, size_t ws_bytes, cudaStream_t stream);
+int vector_elementwise(int op, int64_t n, float alpha, const float* x, int64_t incx, float* y, int64_t incy,
+                       float c, float s, float* xm, cudaStream_t stream);
+
+// Minimum problem size (M*N*K) for the tcgen05 path; below it the SIMT
+// kernel finishes before a persistent TMA pipeline has filled.
+constexpr double kTcMinWork = 64.0 * 64.0 * 64.0;
+
+int gemm_route(const GemmProblem& p, cudaStream_t stream) {
+  const double work = static_cast<double>(p.M) * p.N * p.K * p.batch;
+  if (p.K > 0 && work >= kTcMinWork && gemm_tc_supported(p)) return gemm_tc(p, stream);
+  if (p.K > 0 && gemm_simt_f32_supported(p)) return gemm_simt_f32(p, stream);
+  return gemm_simt_generic(p, stream);
+}
+
+int validate_gemm(const GemmProblem& p) {
+  if (dtype_size(p.dtype) == 0) return CUOPX_UNSUPPORTED_TYPE;
+  if (p.M < 0 || p.N < 0 || p.K < 0 || p.batch < 0) return CUOPX_INVALID_ARGUMENT;
+  if (p.M == 0 || p.N == 0 || p.batch == 0) return CUOPX_SUCCESS;
+  const int64_t a_rows = p.transA ? p.K : p.M, a_cols = p.transA ? p.M : p.K;
+  const int64_t b_rows = p.transB ? p.N : p.K, b_cols = p.transB ? p.K : p.N;
+  if (p.C == nullptr) return CUOPX_INVALID_ARGUMENT;
+  if (p.ldc < std::max<int64_t>(1, p.N)) return CUOPX_INVALID_ARGUMENT;
+  if (p.K > 0) {
+    if (p.A == nullptr || p.B == nullptr) return CUOPX_INVALID_ARGUMENT;
+    if (p.lda < std::max<int64_t>(1, a_cols) || p.ldb < std::max<int64_t>(1, b_cols)) return CUOPX_INVALID_ARGUMENT;
+  }
+  if (p.batch > 1 && (p.strideA < 0 || p.strideB < 0 || p.strideC < 0)) return CUOPX_INVALID_ARGUMENT;
+  const size_t es = dtype_size(p.dtype);
+  const int64_t nb = p.batch;
+  const size_t c_span = span_bytes(p.M, p.N, p.ldc, es) + (nb > 1 ? static_cast<size_t>(p.strideC) * (nb - 1) * es : 0);
+  if (p.K > 0) {
+    const size_t a_span =
+        span_bytes(a_rows, a_cols, p.lda, es) + (nb > 1 ? static_cast<size_t>(p.strideA) * (nb - 1) * es : 0);
+    const size_t b_span =
+        span_bytes(b_rows, b_cols, p.ldb, es) + (nb > 1 ? static_cast<size_t>(p.strideB) * (nb - 1) * es : 0);
+    if (overlaps(p.C, c_span, p.A, a_span) || overlaps(p.C, c_span, p.B, b_span)) return CUOPX_INVALID_ARGUMENT;
+  }
+  return -1;  // proceed
+}
+
+}  // namespace cuopx
+
+using namespace cuopx;
+
+extern "C" {
+
+int cuopx_version(void) { return 100; }
+
+const char* cuopx_last_kernel(void) { return t_last_kernel; }
+
+int64_t cuopx_launch_count(void) { return g_launches.load(); }
+
+int cuopx_get_device_error(int* code_out) {
+  if (!code_out) return CUOPX_INVALID_ARGUMENT;
+  if (cudaDeviceSynchronize() != cudaSuccess) return CUOPX_CUDA_ERROR;
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)) != cudaSuccess) return CUOPX_CUDA_ERROR;
+  *code_out = v;
+  return CUOPX_SUCCESS;
+}
+
+int cuopx_clear_device_error(void) {
+  const int zero = 0;
+  if (cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)) != cudaSuccess) return CUOPX_CUDA_ERROR;
+  return CUOPX_SUCCESS;
+}
+
+int cuopx_gemm(int dtype, int transA, int transB, int64_t M, int64_t N, int64_t K, double alpha, const void* A,
+               int64_t lda, const void* B, int64_t ldb, double beta, void* C, int64_t ldc, void* stream) {
+  GemmProblem p{dtype, transA != 0, transB != 0, M, N, K, alpha, beta, A, lda, 0, B, ldb, 0, C, ldc, 0, 1};
+  const int v = validate_gemm(p);
+  if (v >= 0) return v;
+  return gemm_route(p, static_cast<cudaStream_t>(stream));
+}
+
+int cuopx_gemm_strided_batched(int dtype, int transA, int transB, int64_t M, int64_t N, int64_t K, double alpha,
+                               const void* A, int64_t lda, int64_t strideA, const void* B, int64_t ldb,
+                               int64_t strideB, double beta, void* C, int64_t ldc, int64_t strideC, int64_t batch,
+                               void* stream) {
+  GemmProblem p{dtype, transA != 0, transB != 0, M, N, K, alpha, beta, A, lda, strideA, B, ldb, strideB,
+                C, ldc, strideC, batch};
+  const int v = validate_gemm(p);
+  if (v >= 0) return v;
+  return gemm_route(p, static_cast<cudaStream_t>(stream));
+}
+
+size_t cuopx_gemv_workspace_size(int dtype, int trans, int64_t M, int64_t N) {
+  if (M <= 0 || N <= 0) return 0;
+  return gemv_workspace_size(dtype, trans, M, N);
+}
+
+int cuopx_gemv(int dtype, int trans, int64_t M, int64_t N, double alpha, const void* A, int64_t lda, const void* x,
+               double beta, void* y, void* workspace, size_t workspace_bytes, void* stream) {
+  if (dtype_size(dtype) == 0) return CUOPX_UNSUPPORTED_TYPE;
+  if (M < 0 || N < 0) return CUOPX_INVALID_ARGUMENT;
+  if (M == 0) return CUOPX_SUCCESS;
+  if (y == nullptr) return CUOPX_INVALID_ARGUMENT;
+  if (N > 0) {
+    if (A == nullptr || x == nullptr) return CUOPX_INVALID_ARGUMENT;
+    if (lda < (trans ? M : N)) return CUOPX_INVALID_ARGUMENT;
+    const size_t es = dtype_size(dtype);
+    const size_t a_span = trans ? span_bytes(N, M, lda, es) : span_bytes(M, N, lda, es);
+    if (overlaps(y, M * es, A, a_span) || overlaps(y, M * es, x, N * es)) return CUOPX_INVALID_ARGUMENT;
+  }
+  return gemv_dispatch(dtype, trans, M, N, alpha, A, lda, x, beta, y, workspace, workspace_bytes,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int cuopx_gather_column_blocks(int dtype, int64_t G, int64_t M, int64_t Nb, const void* blocks, void* out,
+                               int64_t ldo, void* stream) {
+  if (dtype_size(dtype) == 0) return CUOPX_UNSUPPORTED_TYPE;
+  if (G < 0 || M < 0 || Nb < 0) return CUOPX_INVALID_ARGUMENT;
+  if (G * M * Nb == 0) return CUOPX_SUCCESS;
+  if (!blocks || !out || ldo < G * Nb) return CUOPX_INVALID_ARGUMENT;
+  return gather_column_blocks(dtype, G, M, Nb, blocks, out, ldo, static_cast<cudaStream_t>(stream));
+}
+
+size_t cuopx_vector_workspace_size(int64_t n) {
+  (void)n;
+  return vector_workspace_size_impl();
+}
+
+static int vec_args_ok(int64_t n, const void* x, int64_t incx, const void* y, int64_t incy, bool need_y) {
+  if (n < 0) return CUOPX_INVALID_ARGUMENT;
+  if (n == 0) return CUOPX_SUCCESS;
+  if (!x || incx == 0) return CUOPX_INVALID_ARGUMENT;
+  if (need_y && (!y || incy == 0)) return CUOPX_INVALID_ARGUMENT;
+  return -1;
+}
+
+int cuopx_dot(int64_t n, const float* x, int64_t incx, const float* y, int64_t incy, float* result,
+              void* workspace, size_t workspace_bytes, void* stream) {
+  if (!result || n < 0) return CUOPX_INVALID_ARGUMENT;
+  if (n > 0) {
+    const int v = vec_args_ok(n, x, incx, y, incy, true);
+    if (v >= 0) return v;
+  }
+  return vector_reduce(0, n, x, incx, y, incy, result, nullptr, workspace, workspace_bytes,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int cuopx_asum(int64_t n, const float* x, int64_t incx, float* result, void* workspace, size_t workspace_bytes,
+               void* stream) {
+  if (!result || n < 0) return CUOPX_INVALID_ARGUMENT;
+  if (n > 0 && (!x || incx == 0)) return CUOPX_INVALID_ARGUMENT;
+  return vector_reduce(1, n, x, incx, nullptr, 1, result, nullptr, workspace, workspace_bytes,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int cuopx_nrm2(int64_t n, const float* x, int64_t incx, float* result, void* workspace, size_t workspace_bytes,
+               void* stream) {
+  if (!result || n < 0) return CUOPX_INVALID_ARGUMENT;
+  if (n > 0 && (!x || incx == 0)) return CUOPX_INVALID_ARGUMENT;
+  return vector_reduce(2, n, x, incx, nullptr, 1, result, nullptr, workspace, workspace_bytes,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int cuopx_iamax(int64_t n, const float* x, int64_t incx, int64_t* result, void* workspace, size_t workspace_bytes,
+                void* stream) {
+  if (!result || n < 0) return CUOPX_INVALID_ARGUMENT;
+  if (n > 0 && (!x || incx == 0)) return CUOPX_INVALID_ARGUMENT;
+  return vector_reduce(3, n, x, incx, nullptr, 1, nullptr, result, workspace, workspace_bytes,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int cuopx_iamin(int64_t n, const float* x, int64_t incx, int64_t* result, void* workspace, size_t workspace_bytes,
+                void* stream) {
+  if (!result || n < 0) return CUOPX_INVALID_ARGUMENT;
+  if (n > 0 && (!x || incx == 0)) return CUOPX_INVALID_ARGUMENT;
+  return vector_reduce(4, n, x, incx, nullptr, 1, nullptr, result, workspace, workspace_bytes,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int cuopx_axpy(int64_t n, float alpha, const float* x, int64_t incx, float* y, int64_t incy, void* stream) {
+  const int v = vec_args_ok(n, x, incx, y, incy, true);
+  if (v >= 0) return v;
+  return vector_elementwise(0, n, alpha, x, incx, y, incy, 0.f, 0.f, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+int cuopx_scal(int64_t n, float alpha, float* x, int64_t incx, void* stream) {
+  const int v = vec_args_ok(n, x, incx, nullptr, 1, false);
+  if (v >= 0) return v;
+  return vector_elementwise(1, n, alpha, nullptr, incx, nullptr, 1, 0.f, 0.f, x, static_cast<cudaStream_t>(stream));
+}
+
+int cuopx_copy(int64_t n, const float* x, int64_t incx, float* y, int64_t incy, void* stream) {
+  const int v = vec_args_ok(n, x, incx, y, incy, true);
+  if (v >= 0) return v;
+  return vector_elementwise(2, n, 0.f, x, incx, y, incy, 0.f, 0.f, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+int cuopx_swap(int64_t n, float* x, int64_t incx, float* y, int64_t incy, void* stream) {
+  const int v = vec_args_ok(n, x, incx, y, incy, true);
+  if (v >= 0) return v;
+  return vector_elementwise(3, n, 0.f, nullptr, incx, y, incy, 0.f, 0.f, x, static_cast<cudaStream_t>(stream));
+}
+
+int cuopx_rot(int64_t n, float* x, int64_t incx, float* y, int64_t incy, float c, float s, void* stream) {
+  const int v = vec_args_ok(n, x, incx, y, incy, true);
+  if (v >= 0) return v;
+  return vector_elementwise(4, n, 0.f, nullptr, incx, y, incy, c, s, x, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

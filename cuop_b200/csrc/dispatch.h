@@ -1,0 +1,68 @@
+// Internal host-side interfaces between the C-ABI layer (capi.cu) and the
+// kernel translation units.  Not installed; the public surface is cuopx.h.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+#include <algorithm>
+
+#include "cuopx.h"
+
+namespace cuopx {
+
+// SM count of the current device (cached per device).
+int device_sm_count();
+
+// Record the kernel variant name for cuopx_last_kernel() and bump the
+// process-wide launch counter.
+void note_launch(const char* name);
+
+// cudaGetLastError -> CUOPX_SUCCESS / CUOPX_CUDA_ERROR.
+int check_launch();
+
+// ---- GEMV (gemv.cu) ----
+size_t gemv_workspace_size(int dtype, int trans, int64_t M, int64_t N);
+int gemv_dispatch(int dtype, int trans, int64_t M, int64_t N, double alpha, const void* A, int64_t lda,
+                  const void* x, double beta, void* y, void* ws, size_t ws_bytes, cudaStream_t stream);
+
+// ---- GEMM problem descriptor shared by all GEMM back-ends ----
+struct GemmProblem {
+  int dtype;
+  bool transA, transB;
+  int64_t M, N, K;
+  double alpha, beta;
+  const void* A;
+  int64_t lda, strideA;
+  const void* B;
+  int64_t ldb, strideB;
+  void* C;
+  int64_t ldc, strideC;
+  int64_t batch;
+};
+
+// SIMT back-ends (gemm_simt.cu): generic any-dtype/any-layout kernel and
+// the register-blocked fp32 kernel.
+int gemm_simt_generic(const GemmProblem& p, cudaStream_t stream);
+bool gemm_simt_f32_supported(const GemmProblem& p);
+int gemm_simt_f32(const GemmProblem& p, cudaStream_t stream);
+
+// tcgen05/TMA back-end (gemm_tc.cu) for fp16/bf16.
+bool gemm_tc_supported(const GemmProblem& p);
+int gemm_tc(const GemmProblem& p, cudaStream_t stream);
+
+// Column-block gather (vector_ops.cu).
+int gather_column_blocks(int dtype, int64_t G, int64_t M, int64_t Nb, const void* blocks, void* out, int64_t ldo,
+                         cudaStream_t stream);
+
+inline size_t dtype_size(int dtype) {
+  switch (dtype) {
+    case CUOPX_F32: return 4;
+    case CUOPX_F64: return 8;
+    case CUOPX_F16: return 2;
+    case CUOPX_BF16: return 2;
+    default: return 0;
+  }
+}
+
+}  // namespace cuopx

@@ -1,0 +1,268 @@
+"""Torch-tensor front end over the C ABI (include/cuopx.h).
+
+Tensors only carry device memory and streams here: every call passes raw
+device pointers to libcuopx.so, which launches the sm_100a kernels.  Shapes
+and argument meaning follow cuOP's operators:
+
+  gemm(A, B)        C = alpha * op(A) op(B) + beta * C   (Gemm<T>::Forward,
+                    src/cuda_op/detail/cuBlas/gemm.cu:417-511)
+  gemv(A, x)        y = alpha * op(A) x + beta * y        (Gemv<T>::Forward,
+                    src/cuda_op/detail/cuBlas/gemv.cu:209-256)
+  batched_gemm(A,B) C_b = alpha * A_b B_b + beta * C_b    (BatchMatMul<T>::Forward,
+                    src/cuda_op/detail/cuDNN/batchmatmul.cu:52-94)
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Optional
+
+import torch
+
+from . import _native as N
+
+_DT = {torch.float32: N.F32, torch.float64: N.F64, torch.float16: N.F16, torch.bfloat16: N.BF16}
+
+_ws_cache: dict = {}
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise N.CuopError(N.UNSUPPORTED_TYPE, f"dtype {t.dtype}") from None
+
+
+def _require_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if not t.is_cuda:
+            raise N.CuopError(N.INVALID_ARGUMENT, "tensor is not on a CUDA device (no CPU path exists)")
+
+
+def _row_ld(t: torch.Tensor) -> int:
+    """Leading dimension of a row-major 2-D view (unit column stride)."""
+    if t.dim() != 2 or (t.stride(1) != 1 and t.size(1) > 1):
+        raise N.CuopError(N.INVALID_ARGUMENT, "expected a row-major 2-D tensor with unit column stride")
+    return max(t.stride(0), t.size(1), 1)
+
+
+def _stream(stream) -> int:
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, torch.cuda.Stream):
+        return stream.cuda_stream
+    return int(stream)
+
+
+def workspace(nbytes: int, device: torch.device, tag: str = "ws") -> tuple[int, int]:
+    """Per-device scratch (zeroed once at allocation); returns (ptr, bytes)."""
+    if nbytes == 0:
+        return 0, 0
+    key = (tag, device.index if device.index is not None else torch.cuda.current_device())
+    buf = _ws_cache.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _ws_cache[key] = buf
+    return buf.data_ptr(), buf.numel()
+
+
+def gemm(A: torch.Tensor, B: torch.Tensor, C: Optional[torch.Tensor] = None, *, transA: bool = False,
+         transB: bool = False, alpha: float = 1.0, beta: float = 0.0, stream=None) -> torch.Tensor:
+    """C = alpha * op(A) op(B) + beta * C for row-major 2-D tensors."""
+    _require_cuda(A, B)
+    M = A.size(1) if transA else A.size(0)
+    K = A.size(0) if transA else A.size(1)
+    Kb = B.size(1) if transB else B.size(0)
+    Nn = B.size(0) if transB else B.size(1)
+    if Kb != K:
+        raise N.CuopError(N.SHAPE_MISMATCH, f"gemm: op(A) is {M}x{K}, op(B) is {Kb}x{Nn}")
+    if A.dtype != B.dtype:
+        raise N.CuopError(N.UNSUPPORTED_TYPE, "gemm: A and B must share a dtype")
+    if C is None:
+        C = torch.empty((M, Nn), dtype=A.dtype, device=A.device)
+        beta = 0.0
+    _require_cuda(C)
+    if tuple(C.shape) != (M, Nn) or C.dtype != A.dtype:
+        raise N.CuopError(N.SHAPE_MISMATCH, f"gemm: C must be {M}x{Nn} {A.dtype}")
+    rc = N.lib().cuopx_gemm(_dtype_code(A), int(transA), int(transB), M, Nn, K, float(alpha), A.data_ptr(),
+                            _row_ld(A), B.data_ptr(), _row_ld(B), float(beta), C.data_ptr(), _row_ld(C),
+                            _stream(stream))
+    N.check(rc, "cuopx_gemm")
+    return C
+
+
+def batched_gemm(A: torch.Tensor, B: torch.Tensor, C: Optional[torch.Tensor] = None, *, transA: bool = False,
+                 transB: bool = False, alpha: float = 1.0, beta: float = 0.0, stream=None) -> torch.Tensor:
+    """Strided batched GEMM over contiguous [batch, rows, cols] tensors."""
+    _require_cuda(A, B)
+    if A.dim() != 3 or B.dim() != 3:
+        raise N.CuopError(N.SHAPE_MISMATCH, "batched_gemm expects 3-D tensors")
+    A = A if A.is_contiguous() else A.contiguous()
+    B = B if B.is_contiguous() else B.contiguous()
+    batch = A.size(0)
+    M = A.size(2) if transA else A.size(1)
+    K = A.size(1) if transA else A.size(2)
+    Kb = B.size(2) if transB else B.size(1)
+    Nn = B.size(1) if transB else B.size(2)
+    if Kb != K or B.size(0) != batch:
+        raise N.CuopError(N.SHAPE_MISMATCH, "batched_gemm: shape mismatch")
+    if C is None:
+        C = torch.empty((batch, M, Nn), dtype=A.dtype, device=A.device)
+        beta = 0.0
+    if tuple(C.shape) != (batch, M, Nn) or not C.is_contiguous():
+        raise N.CuopError(N.SHAPE_MISMATCH, "batched_gemm: bad C")
+    rc = N.lib().cuopx_gemm_strided_batched(
+        _dtype_code(A), int(transA), int(transB), M, Nn, K, float(alpha), A.data_ptr(), A.size(2),
+        A.size(1) * A.size(2), B.data_ptr(), B.size(2), B.size(1) * B.size(2), float(beta), C.data_ptr(), Nn,
+        M * Nn, batch, _stream(stream))
+    N.check(rc, "cuopx_gemm_strided_batched")
+    return C
+
+
+def gemv(A: torch.Tensor, x: torch.Tensor, y: Optional[torch.Tensor] = None, *, trans: bool = False,
+         alpha: float = 1.0, beta: float = 0.0, stream=None) -> torch.Tensor:
+    """y = alpha * op(A) x + beta * y.
+
+    trans=False: A is M x N, x has N entries, y has M.
+    trans=True:  A is N x M (the reference reads A[col*m+row]); y = A^T x has M.
+    """
+    _require_cuda(A, x)
+    if trans:
+        Nn, M = A.size(0), A.size(1)
+    else:
+        M, Nn = A.size(0), A.size(1)
+    if x.numel() != Nn:
+        raise N.CuopError(N.SHAPE_MISMATCH, f"gemv: x has {x.numel()} entries, expected {Nn}")
+    if y is None:
+        y = torch.empty(M, dtype=A.dtype, device=A.device)
+        beta = 0.0
+    if y.numel() != M:
+        raise N.CuopError(N.SHAPE_MISMATCH, f"gemv: y has {y.numel()} entries, expected {M}")
+    dt = _dtype_code(A)
+    need = N.lib().cuopx_gemv_workspace_size(dt, int(trans), M, Nn)
+    ws, wsb = workspace(need, A.device)
+    rc = N.lib().cuopx_gemv(dt, int(trans), M, Nn, float(alpha), A.data_ptr(), _row_ld(A), x.data_ptr(),
+                            float(beta), y.data_ptr(), ws, wsb, _stream(stream))
+    N.check(rc, "cuopx_gemv")
+    return y
+
+
+def gather_column_blocks(blocks: torch.Tensor, out: torch.Tensor, stream=None) -> torch.Tensor:
+    """blocks: [G, M, Nb] contiguous -> out: [M, G*Nb] row-major."""
+    G, M, Nb = blocks.shape
+    rc = N.lib().cuopx_gather_column_blocks(_dtype_code(blocks), G, M, Nb, blocks.data_ptr(), out.data_ptr(),
+                                            _row_ld(out), _stream(stream))
+    N.check(rc, "cuopx_gather_column_blocks")
+    return out
+
+
+# ----------------------------------------------------------------- level 1
+def _vws(x: torch.Tensor) -> tuple[int, int]:
+    return workspace(N.lib().cuopx_vector_workspace_size(x.numel()), x.device, tag="vec")
+
+
+def _f32(*ts):
+    for t in ts:
+        if t.dtype != torch.float32:
+            raise N.CuopError(N.UNSUPPORTED_TYPE, "vector ops are fp32")
+    _require_cuda(*ts)
+
+
+def dot(x, y, n=None, incx=1, incy=1, stream=None) -> torch.Tensor:
+    _f32(x, y)
+    n = x.numel() if n is None else n
+    out = torch.empty(1, dtype=torch.float32, device=x.device)
+    ws, wsb = _vws(x)
+    N.check(N.lib().cuopx_dot(n, x.data_ptr(), incx, y.data_ptr(), incy, out.data_ptr(), ws, wsb, _stream(stream)),
+            "cuopx_dot")
+    return out
+
+
+def nrm2(x, n=None, incx=1, stream=None) -> torch.Tensor:
+    _f32(x)
+    n = x.numel() if n is None else n
+    out = torch.empty(1, dtype=torch.float32, device=x.device)
+    ws, wsb = _vws(x)
+    N.check(N.lib().cuopx_nrm2(n, x.data_ptr(), incx, out.data_ptr(), ws, wsb, _stream(stream)), "cuopx_nrm2")
+    return out
+
+
+def asum(x, n=None, incx=1, stream=None) -> torch.Tensor:
+    _f32(x)
+    n = x.numel() if n is None else n
+    out = torch.empty(1, dtype=torch.float32, device=x.device)
+    ws, wsb = _vws(x)
+    N.check(N.lib().cuopx_asum(n, x.data_ptr(), incx, out.data_ptr(), ws, wsb, _stream(stream)), "cuopx_asum")
+    return out
+
+
+def iamax(x, n=None, incx=1, stream=None) -> torch.Tensor:
+    _f32(x)
+    n = x.numel() if n is None else n
+    out = torch.empty(1, dtype=torch.int64, device=x.device)
+    ws, wsb = _vws(x)
+    N.check(N.lib().cuopx_iamax(n, x.data_ptr(), incx, out.data_ptr(), ws, wsb, _stream(stream)), "cuopx_iamax")
+    return out
+
+
+def iamin(x, n=None, incx=1, stream=None) -> torch.Tensor:
+    _f32(x)
+    n = x.numel() if n is None else n
+    out = torch.empty(1, dtype=torch.int64, device=x.device)
+    ws, wsb = _vws(x)
+    N.check(N.lib().cuopx_iamin(n, x.data_ptr(), incx, out.data_ptr(), ws, wsb, _stream(stream)), "cuopx_iamin")
+    return out
+
+
+def axpy(alpha, x, y, n=None, incx=1, incy=1, stream=None):
+    _f32(x, y)
+    n = x.numel() if n is None else n
+    N.check(N.lib().cuopx_axpy(n, float(alpha), x.data_ptr(), incx, y.data_ptr(), incy, _stream(stream)), "cuopx_axpy")
+    return y
+
+
+def scal(alpha, x, n=None, incx=1, stream=None):
+    _f32(x)
+    n = x.numel() if n is None else n
+    N.check(N.lib().cuopx_scal(n, float(alpha), x.data_ptr(), incx, _stream(stream)), "cuopx_scal")
+    return x
+
+
+def copy(x, y, n=None, incx=1, incy=1, stream=None):
+    _f32(x, y)
+    n = x.numel() if n is None else n
+    N.check(N.lib().cuopx_copy(n, x.data_ptr(), incx, y.data_ptr(), incy, _stream(stream)), "cuopx_copy")
+    return y
+
+
+def swap(x, y, n=None, incx=1, incy=1, stream=None):
+    _f32(x, y)
+    n = x.numel() if n is None else n
+    N.check(N.lib().cuopx_swap(n, x.data_ptr(), incx, y.data_ptr(), incy, _stream(stream)), "cuopx_swap")
+    return x, y
+
+
+def rot(x, y, c, s, n=None, incx=1, incy=1, stream=None):
+    _f32(x, y)
+    n = x.numel() if n is None else n
+    N.check(N.lib().cuopx_rot(n, x.data_ptr(), incx, y.data_ptr(), incy, float(c), float(s), _stream(stream)),
+            "cuopx_rot")
+    return x, y
+
+
+# ----------------------------------------------------------------- diagnostics
+def last_kernel() -> str:
+    return N.lib().cuopx_last_kernel().decode()
+
+
+def launch_count() -> int:
+    return int(N.lib().cuopx_launch_count())
+
+
+def device_error() -> int:
+    v = C.c_int(0)
+    N.check(N.lib().cuopx_get_device_error(C.byref(v)), "cuopx_get_device_error")
+    return v.value
+
+
+def clear_device_error() -> None:
+    N.check(N.lib().cuopx_clear_device_error(), "cuopx_clear_device_error")

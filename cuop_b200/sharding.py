@@ -1,0 +1,95 @@
+"""Multi-GPU sharding of the GEMM paths (one process per GPU).
+
+The reference is single-GPU; these two strategies are what the batched and
+large-GEMM paths need on one 8-GPU box:
+
+* Batch sharding (strided batched GEMM): rank r owns batches
+  [r*B/G, (r+1)*B/G) of contiguous A/B/C and runs one local batched call.
+  There is no data-path collective.
+* Column sharding (large GEMM / linear layer): rank r holds the weight column
+  block W[:, r*N/G:(r+1)*N/G] as its own contiguous [K, N/G] matrix and
+  computes Y_r = X W_r.  Only when the caller wants the full Y on every rank
+  is there an exchange: an NCCL all-gather of the [M, N/G] blocks into a
+  [G, M, N/G] staging buffer, issued per M-chunk right after that chunk's GEMM
+  so the transfer of chunk c overlaps the GEMM of chunk c+1, followed by the
+  column-block gather kernel that writes row-major [M, N].
+
+torch.distributed (NCCL over NVLink/NVSwitch) is plumbing only; every GEMM and
+the gather run through libcuopx.so.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from . import ops
+
+
+def shard_range(total: int, rank: int, world: int) -> tuple[int, int]:
+    """Balanced contiguous split: the first (total % world) ranks get one extra."""
+    if world <= 0 or not (0 <= rank < world):
+        raise ValueError(f"bad rank {rank} of {world}")
+    base, extra = divmod(total, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def batch_sharded_gemm(A: torch.Tensor, B: torch.Tensor, rank: int, world: int,
+                       C: Optional[torch.Tensor] = None, **kw) -> torch.Tensor:
+    """Local part of a batch-sharded strided batched GEMM.
+
+    A, B are either the full [batch, ...] tensors (the local slice is taken as
+    a view) or already-local slices when `C` is given with the local shape."""
+    b0, b1 = shard_range(A.size(0), rank, world)
+    return ops.batched_gemm(A[b0:b1], B[b0:b1], None if C is None else C[b0:b1], **kw)
+
+
+@dataclass
+class ColumnShardedGemm:
+    """Y = X @ W with W split by columns over `world` ranks.
+
+    w_local: this rank's contiguous [K, N/G] column block (N divisible by G).
+    """
+
+    w_local: torch.Tensor
+    world: int
+    group: Optional[dist.ProcessGroup] = None
+    chunks: int = 4
+
+    def local(self, X: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """This rank's [M, N/G] output block (no communication)."""
+        return ops.gemm(X, self.w_local, out)
+
+    def forward(self, X: torch.Tensor, gather: bool = True, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if not gather or self.world == 1:
+            return self.local(X, out)
+        M, nb = X.size(0), self.w_local.size(1)
+        G = self.world
+        if out is None:
+            out = torch.empty((M, G * nb), dtype=X.dtype, device=X.device)
+        chunks = max(1, min(self.chunks, M))
+        local_blk = torch.empty((M, nb), dtype=X.dtype, device=X.device)
+        pending = []
+        # Each chunk's all-gather is queued as soon as its rows are computed;
+        # NCCL runs it on its own stream while the next chunk's GEMM runs.
+        for c in range(chunks):
+            r0, r1 = shard_range(M, c, chunks)
+            if r1 <= r0:
+                continue
+            ops.gemm(X[r0:r1], self.w_local, local_blk[r0:r1])
+            recv = torch.empty((G, r1 - r0, nb), dtype=X.dtype, device=X.device)
+            h = dist.all_gather_into_tensor(recv, local_blk[r0:r1], group=self.group, async_op=True)
+            pending.append((r0, r1, recv, h))
+        for r0, r1, recv, h in pending:
+            h.wait()  # the current stream waits for this chunk's collective
+            ops.gather_column_blocks(recv, out[r0:r1])
+        return out
+
+
+def split_columns(W: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """Contiguous copy of this rank's column block of a row-major [K, N] W."""
+    n0, n1 = shard_range(W.size(1), rank, world)
+    return W[:, n0:n1].contiguous()

@@ -1,0 +1,138 @@
+/*
+ * cuopx.h — C ABI of the B200 (sm_100a) dense BLAS hot path.
+ *
+ * Plain pointers and sizes only: every matrix/vector argument is a DEVICE
+ * pointer, every size is int64_t, every call is asynchronous on the given
+ * cudaStream_t (passed as void*, NULL = legacy default stream) and returns
+ * a cuOP StatusCode integer (same numeric values as the reference's
+ * `enum class StatusCode`, include/util/status_code.hpp:28-161).  No call
+ * allocates device memory; scratch is passed in by the caller.
+ *
+ * Layout convention: row-major, like the reference operators
+ * (src/cuda_op/detail/cuBlas/gemm.cu:14-42, gemv.cu:10-23).
+ */
+#ifndef CUOPX_H_
+#define CUOPX_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (numerically identical to cu_op_mem::StatusCode) ---- */
+#define CUOPX_SUCCESS 0
+#define CUOPX_NOT_IMPLEMENTED 1001
+#define CUOPX_TIMEOUT 1003
+#define CUOPX_CUDA_ERROR 2000
+#define CUOPX_OUT_OF_MEMORY 3001
+#define CUOPX_INVALID_ARGUMENT 4001
+#define CUOPX_EXECUTION_TIMEOUT 6002
+#define CUOPX_KERNEL_NOT_FOUND 6005
+#define CUOPX_NOT_COMPILED 7003
+#define CUOPX_SHAPE_MISMATCH 10002
+#define CUOPX_UNSUPPORTED_TYPE 11001
+
+/* ---- element types ---- */
+#define CUOPX_F32 0
+#define CUOPX_F64 1
+#define CUOPX_F16 2
+#define CUOPX_BF16 3
+
+/* ---- library ---- */
+int cuopx_version(void);
+/* Name of the kernel variant the last successful call on this host thread
+ * launched (e.g. "gemm_tc_128x256", "gemv_t_splitk").  Never NULL. */
+const char* cuopx_last_kernel(void);
+/* Number of cuopx kernels launched by this process so far. */
+int64_t cuopx_launch_count(void);
+/* First error code recorded by a device-side bounded wait (0 = none).
+ * Synchronises the current device. */
+int cuopx_get_device_error(int* code_out);
+int cuopx_clear_device_error(void);
+
+/*
+ * GEMM: C = alpha * op(A) * op(B) + beta * C, all row-major.
+ *   op(A) is M x K: A is M x K (lda >= K) or, if transA, K x M (lda >= M).
+ *   op(B) is K x N: B is K x N (ldb >= N) or, if transB, N x K (ldb >= K).
+ *   C is M x N (ldc >= N).  beta == 0 never reads C.
+ * dtype F32/F64: alpha, beta and accumulation in that type.
+ * dtype F16/BF16: inputs and C in that type, fp32 accumulate, alpha/beta
+ *   applied in fp32, one rounding of the result.
+ * Replaces Gemm<T>::Forward (src/cuda_op/detail/cuBlas/gemm.cu:417-511)
+ * and GemmJITPlugin::Execute (src/jit/Blas/gemm_jit_plugin.cu:147-265).
+ */
+int cuopx_gemm(int dtype, int transA, int transB, int64_t M, int64_t N, int64_t K, double alpha, const void* A,
+               int64_t lda, const void* B, int64_t ldb, double beta, void* C, int64_t ldc, void* stream);
+
+/*
+ * Strided batched GEMM: for b in [0, batch):
+ *   C_b = alpha * op(A_b) * op(B_b) + beta * C_b,
+ *   X_b = X + b * strideX (element strides; strideB may be 0 to share B).
+ * Replaces BatchMatMul<T>::Forward (src/cuda_op/detail/cuDNN/batchmatmul.cu:52-94,
+ * alpha=1, beta=0) and GemmBatchedJITPlugin::Execute
+ * (src/jit/Blas/gemm_batched_jit_plugin.cu:113-188).
+ */
+int cuopx_gemm_strided_batched(int dtype, int transA, int transB, int64_t M, int64_t N, int64_t K,
+                               double alpha, const void* A, int64_t lda, int64_t strideA, const void* B,
+                               int64_t ldb, int64_t strideB, double beta, void* C, int64_t ldc, int64_t strideC,
+                               int64_t batch, void* stream);
+
+/*
+ * GEMV: y[M] = alpha * op(A) * x[N] + beta * y[M].
+ *   trans == 0: A is M x N row-major (lda >= N), y_i = sum_j A[i*lda+j] x_j.
+ *   trans != 0: A is N x M row-major (lda >= M), y_i = sum_j A[j*lda+i] x_j
+ *   (the reference's transA indexing A[col*m+row], gemv.cu:17).
+ * `workspace` (device, 256-byte aligned) holds split-K partial sums and
+ * arrival counters; size from cuopx_gemv_workspace_size().  With too
+ * little workspace a single-pass variant runs instead (same result
+ * bits are NOT guaranteed between the two variants; both meet tolerance).
+ * Counters are left zeroed on return; a fresh workspace must be zeroed once.
+ * Replaces Gemv<T>::Forward (src/cuda_op/detail/cuBlas/gemv.cu:209-256)
+ * and GemvJITPlugin::Execute (src/jit/Blas/gemv_jit_plugin.cu:126-200).
+ */
+size_t cuopx_gemv_workspace_size(int dtype, int trans, int64_t M, int64_t N);
+int cuopx_gemv(int dtype, int trans, int64_t M, int64_t N, double alpha, const void* A, int64_t lda,
+               const void* x, double beta, void* y, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Column-block gather for N-sharded GEMM: `blocks` is G contiguous
+ * [M][Nb] row-major blocks (as an all-gather leaves them); writes the
+ * row-major [M][G*Nb] matrix `out` (ldo >= G*Nb).  Element size from dtype.
+ * No reference counterpart (the reference has no multi-GPU path); used
+ * after ncclAllGather of per-rank GEMM outputs.
+ */
+int cuopx_gather_column_blocks(int dtype, int64_t G, int64_t M, int64_t Nb, const void* blocks, void* out,
+                               int64_t ldo, void* stream);
+
+/*
+ * Level-1 vector operations (fp32), replacing VectorOpsJITPlugin::Execute
+ * (src/jit/Blas/vector_ops_jit_plugin.cu:113-181) with standard BLAS
+ * semantics.  Scalar results are written to DEVICE memory (`result`).
+ * Reductions use `workspace` (cuopx_vector_workspace_size bytes, zeroed
+ * once; counters are left zeroed on return).  Index results are 1-based
+ * BLAS indices of the FIRST maximal / minimal |x_i| (0 when n <= 0).
+ */
+size_t cuopx_vector_workspace_size(int64_t n);
+int cuopx_dot(int64_t n, const float* x, int64_t incx, const float* y, int64_t incy, float* result,
+              void* workspace, size_t workspace_bytes, void* stream);
+int cuopx_axpy(int64_t n, float alpha, const float* x, int64_t incx, float* y, int64_t incy, void* stream);
+int cuopx_scal(int64_t n, float alpha, float* x, int64_t incx, void* stream);
+int cuopx_copy(int64_t n, const float* x, int64_t incx, float* y, int64_t incy, void* stream);
+int cuopx_swap(int64_t n, float* x, int64_t incx, float* y, int64_t incy, void* stream);
+int cuopx_rot(int64_t n, float* x, int64_t incx, float* y, int64_t incy, float c, float s, void* stream);
+int cuopx_nrm2(int64_t n, const float* x, int64_t incx, float* result, void* workspace, size_t workspace_bytes,
+               void* stream);
+int cuopx_asum(int64_t n, const float* x, int64_t incx, float* result, void* workspace, size_t workspace_bytes,
+               void* stream);
+int cuopx_iamax(int64_t n, const float* x, int64_t incx, int64_t* result, void* workspace,
+                size_t workspace_bytes, void* stream);
+int cuopx_iamin(int64_t n, const float* x, int64_t incx, int64_t* result, void* workspace,
+                size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CUOPX_H_ */

@@ -1,0 +1,43 @@
+import os
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+sys.path.insert(0, str(ROOT))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA (B200, sm_100a) device")
+
+
+def pytest_collection_modifyitems(config, items):
+    import torch
+
+    if torch.cuda.is_available():
+        return
+    skip = pytest.mark.skip(reason="no CUDA device in this process")
+    for item in items:
+        if "gpu" in item.keywords:
+            item.add_marker(skip)
+
+
+@pytest.fixture(scope="session")
+def dev():
+    import torch
+
+    return torch.device("cuda", 0)
+
+
+@pytest.fixture(autouse=True)
+def _no_device_error(request):
+    """Every GPU test must leave the device error word clean."""
+    yield
+    if "gpu" in request.keywords:
+        import cuop_b200 as cx
+
+        code = cx.device_error()
+        if code:
+            cx.clear_device_error()
+        assert code == 0, f"device-side error word set: {code}"

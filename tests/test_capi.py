@@ -1,0 +1,97 @@
+"""CPU tests of the C ABI: the library loads, exports exactly what
+include/cuopx.h declares, and rejects bad arguments before touching a GPU."""
+import ctypes as C
+import re
+from pathlib import Path
+
+import pytest
+
+import cuop_b200 as cx
+from cuop_b200 import _native as N
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def declared_symbols():
+    text = (ROOT / "include" / "cuopx.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(cuopx_\w+)\s*\(", text)))
+
+
+def test_library_loads_from_tree():
+    L = cx.lib()
+    assert Path(L._name).resolve() == (ROOT / "cuop_b200" / "libcuopx.so").resolve()
+    assert L.cuopx_version() == 100
+
+
+def test_every_declared_symbol_is_exported_and_bound():
+    L = cx.lib()
+    decl = declared_symbols()
+    assert len(decl) >= 20
+    bound = {name for name, _, _ in N.SIGNATURES}
+    assert set(decl) == bound, set(decl) ^ bound
+    for name in decl:
+        assert hasattr(L, name), name
+
+
+def test_status_codes_match_reference_enum():
+    # include/util/status_code.hpp:28-161 of the reference
+    assert (N.SUCCESS, N.NOT_IMPLEMENTED, N.TIMEOUT, N.CUDA_ERROR, N.OUT_OF_MEMORY) == (0, 1001, 1003, 2000, 3001)
+    assert (N.INVALID_ARGUMENT, N.EXECUTION_TIMEOUT, N.KERNEL_NOT_FOUND, N.NOT_COMPILED) == (4001, 6002, 6005, 7003)
+    assert (N.SHAPE_MISMATCH, N.UNSUPPORTED_TYPE) == (10002, 11001)
+
+
+def test_header_status_macros_agree():
+    text = (ROOT / "include" / "cuopx.h").read_text()
+    macros = dict(re.findall(r"#define CUOPX_(\w+) (\d+)", text))
+    for name in ("SUCCESS", "CUDA_ERROR", "INVALID_ARGUMENT", "SHAPE_MISMATCH", "UNSUPPORTED_TYPE"):
+        assert int(macros[name]) == getattr(N, name)
+
+
+def test_argument_validation_without_gpu():
+    L = cx.lib()
+    # negative sizes
+    assert L.cuopx_gemm(N.F32, 0, 0, -1, 4, 4, 1.0, 16, 4, 16, 4, 0.0, 16, 4, None) == N.INVALID_ARGUMENT
+    # unknown dtype
+    assert L.cuopx_gemm(99, 0, 0, 4, 4, 4, 1.0, 16, 4, 16, 4, 0.0, 16, 4, None) == N.UNSUPPORTED_TYPE
+    # empty problems are no-ops
+    assert L.cuopx_gemm(N.F32, 0, 0, 0, 4, 4, 1.0, None, 4, None, 4, 0.0, None, 4, None) == N.SUCCESS
+    assert L.cuopx_gemv(N.F32, 0, 0, 5, 1.0, None, 5, None, 0.0, None, None, 0, None) == N.SUCCESS
+    # null operands with real sizes
+    assert L.cuopx_gemm(N.F32, 0, 0, 4, 4, 4, 1.0, None, 4, 16, 4, 0.0, 64, 4, None) == N.INVALID_ARGUMENT
+    # leading dimension too small
+    assert L.cuopx_gemm(N.F32, 0, 0, 4, 4, 8, 1.0, 4096, 4, 8192, 4, 0.0, 16384, 4, None) == N.INVALID_ARGUMENT
+    # transposed A needs lda >= M
+    assert L.cuopx_gemm(N.F32, 1, 0, 8, 4, 4, 1.0, 4096, 4, 8192, 4, 0.0, 16384, 4, None) == N.INVALID_ARGUMENT
+    # C overlapping A
+    assert L.cuopx_gemm(N.F32, 0, 0, 4, 4, 4, 1.0, 4096, 4, 8192, 4, 0.0, 4096 + 16, 4, None) == N.INVALID_ARGUMENT
+    # gemv: lda < N, y overlapping x
+    assert L.cuopx_gemv(N.F32, 0, 4, 8, 1.0, 4096, 4, 8192, 0.0, 16384, None, 0, None) == N.INVALID_ARGUMENT
+    assert L.cuopx_gemv(N.F32, 0, 4, 4, 1.0, 4096, 4, 8192, 0.0, 8192, None, 0, None) == N.INVALID_ARGUMENT
+    # vector ops
+    assert L.cuopx_axpy(-1, 1.0, 16, 1, 32, 1, None) == N.INVALID_ARGUMENT
+    assert L.cuopx_axpy(4, 1.0, 16, 0, 32, 1, None) == N.INVALID_ARGUMENT
+    assert L.cuopx_gather_column_blocks(N.F16, 2, 4, 4, 16, 64, 7, None) == N.INVALID_ARGUMENT
+
+
+def test_workspace_sizing_is_host_only():
+    L = cx.lib()
+    assert L.cuopx_gemv_workspace_size(N.F32, 0, 0, 100) == 0
+    # transposed 8192^2 needs split-K partials; sizes are 256-byte multiples
+    ws = L.cuopx_gemv_workspace_size(N.F32, 1, 8192, 8192)
+    assert ws > 0 and ws % 256 == 0
+    assert L.cuopx_vector_workspace_size(1 << 20) >= 1024 * 16
+
+
+def test_last_kernel_defaults():
+    assert isinstance(cx.last_kernel(), str)
+    assert cx.launch_count() >= 0
+
+
+def test_ops_refuse_cpu_tensors():
+    import torch
+
+    with pytest.raises(cx.CuopError):
+        cx.gemm(torch.zeros(4, 4), torch.zeros(4, 4))
+    with pytest.raises(cx.CuopError):
+        cx.gemv(torch.zeros(4, 4), torch.zeros(4))

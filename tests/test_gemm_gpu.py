@@ -1,0 +1,193 @@
+"""GEMM parity through the C ABI.
+
+fp32 / fp64 (SIMT kernels): every output is the same ascending-k fma chain as
+the CPU oracle, so results must be BIT-IDENTICAL to it; the bound
+||C-R||_F/||R||_F <= 1e-5*sqrt(K) is checked against an fp64 product too.
+fp16 / bf16 (tcgen05 kernels): max|C-R| / max|R| <= 1e-2 against the oracle
+(fp32 products and sums, one rounding)."""
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import cuop_b200 as cx
+import oracle as O
+from helpers import TDT, fp32_reference_gpu, lowp_bits, to_dev_f32, to_dev_lowp
+
+pytestmark = pytest.mark.gpu
+GOLD = json.loads((Path(__file__).parent / "golden" / "known_answers.json").read_text())
+LOWP_TOL = 1e-2
+
+
+def test_known_answer_all_dtypes(dev):
+    g = GOLD["gemm_2x3x4"]  # test/cuBlas/test_gemm/test_gemm.cpp:19-43
+    A = np.array(g["A"], np.float32).reshape(2, 3)
+    B = np.array(g["B"], np.float32).reshape(3, 4)
+    for dtype in (torch.float32, torch.float64, torch.float16, torch.bfloat16):
+        C = cx.gemm(torch.from_numpy(A).to(dev, dtype), torch.from_numpy(B).to(dev, dtype))
+        np.testing.assert_allclose(C.double().cpu().numpy().ravel(), g["expected"], atol=g["tol"])
+
+
+F32_CASES = [
+    (1, 1, 1, False, False), (2, 3, 4, False, False), (33, 17, 65, False, False), (33, 17, 65, True, False),
+    (33, 17, 65, False, True), (33, 17, 65, True, True), (128, 128, 128, False, False), (200, 300, 64, False, False),
+    (257, 129, 1000, False, False), (64, 64, 3, False, False), (512, 96, 77, True, True),
+]
+
+
+@pytest.mark.parametrize("M,N,K,tA,tB", F32_CASES)
+def test_f32_bit_exact_vs_oracle(dev, M, N, K, tA, tB):
+    A = O.uniform((K, M) if tA else (M, K), seed=M + 1)
+    B = O.uniform((N, K) if tB else (K, N), seed=N + 2)
+    C0 = O.uniform((M, N), seed=3)
+    ref = O.gemm_f32(A, B, C0, transA=tA, transB=tB, alpha=0.5, beta=2.0)
+    C = cx.gemm(to_dev_f32(A, dev), to_dev_f32(B, dev), to_dev_f32(C0, dev), transA=tA, transB=tB, alpha=0.5,
+                beta=2.0)
+    got = C.cpu().numpy()
+    np.testing.assert_array_equal(got, ref, err_msg=cx.last_kernel())
+    exact = 0.5 * ((A.T if tA else A).astype(np.float64) @ (B.T if tB else B).astype(np.float64)) + 2.0 * C0
+    assert O.rel_frobenius(got, exact) <= 1e-5 * np.sqrt(K)
+
+
+def test_f32_fast_kernel_selected(dev):
+    A = to_dev_f32(O.uniform((512, 512), seed=1), dev)
+    B = to_dev_f32(O.uniform((512, 512), seed=2), dev)
+    cx.gemm(A, B)
+    assert cx.last_kernel().startswith("gemm_f32_")
+
+
+def test_f64_bit_exact_vs_oracle(dev):
+    A = np.asarray(O.uniform((70, 90), seed=4), np.float64)
+    B = np.asarray(O.uniform((90, 50), seed=5), np.float64)
+    C = cx.gemm(torch.from_numpy(A).to(dev), torch.from_numpy(B).to(dev))
+    np.testing.assert_array_equal(C.cpu().numpy(), O.gemm_f64(A, B))
+
+
+def test_c1_fp32_1024_vs_oracle_and_reference_operator(dev):
+    """C1: fp32 1024^3, A,B ~ U[-1,1) seeds 0/1, C zero, alpha=1 beta=0."""
+    n = 1024
+    A32 = O.uniform((n, n), seed=0)
+    B32 = O.uniform((n, n), seed=1)
+    A, B = to_dev_f32(A32, dev), to_dev_f32(B32, dev)
+    C = cx.gemm(A, B)
+    cpu = O.gemm_f32(A32, B32)
+    np.testing.assert_array_equal(C.cpu().numpy(), cpu)
+    exact = A32.astype(np.float64) @ B32.astype(np.float64)
+    assert O.rel_frobenius(cpu, exact) <= 1e-5 * np.sqrt(n)
+    if O.ref_available():
+        Cr = torch.zeros(n, n, device=dev)
+        torch.cuda.synchronize()
+        assert O.ref_lib().ref_gemm_f32(0, 0, n, n, n, 1.0, A.data_ptr(), B.data_ptr(), 0.0, Cr.data_ptr()) == 0
+        ref_gpu = Cr.cpu().numpy()
+        assert O.rel_frobenius(ref_gpu, exact) <= 1e-5 * np.sqrt(n)
+        # The reference's blocked kernel is the same ascending-k fma chain.
+        assert O.rel_frobenius(C.cpu().numpy(), ref_gpu) <= 1e-6
+
+
+LOWP_CASES = [
+    (128, 256, 64, False, False), (256, 512, 128, False, False), (300, 504, 200, False, False),
+    (129, 264, 72, False, False), (1000, 1000, 1000, False, False), (512, 384, 4096, False, False),
+    (256, 384, 192, True, False), (256, 384, 192, False, True), (256, 384, 192, True, True),
+    (384, 136, 320, True, True), (64, 128, 64, False, False), (2048, 2048, 512, False, False),
+]
+
+
+@pytest.mark.parametrize("dt", [O.F16, O.BF16])
+@pytest.mark.parametrize("M,N,K,tA,tB", LOWP_CASES)
+def test_lowp_tcgen05_vs_oracle(dev, dt, M, N, K, tA, tB):
+    A = O.to_lowp(O.normal((K, M) if tA else (M, K), seed=M) / np.sqrt(K), dt)
+    B = O.to_lowp(O.normal((N, K) if tB else (K, N), seed=N + 7), dt)
+    ref = O.gemm_lowp(dt, A, B, transA=tA, transB=tB)
+    C = cx.gemm(to_dev_lowp(A, dt, dev), to_dev_lowp(B, dt, dev), transA=tA, transB=tB)
+    assert cx.last_kernel().startswith("gemm_tc_"), cx.last_kernel()
+    err = O.max_relative(O.from_lowp(lowp_bits(C), dt), O.from_lowp(ref, dt))
+    assert err <= LOWP_TOL, (err, cx.last_kernel())
+
+
+@pytest.mark.parametrize("dt", [O.F16, O.BF16])
+def test_lowp_alpha_beta(dev, dt):
+    M, N, K = 320, 640, 256
+    A = O.to_lowp(O.normal((M, K), seed=1) / np.sqrt(K), dt)
+    B = O.to_lowp(O.normal((K, N), seed=2), dt)
+    C0 = O.to_lowp(O.normal((M, N), seed=3), dt)
+    ref = O.gemm_lowp(dt, A, B, C0, alpha=0.75, beta=-1.25)
+    Cd = to_dev_lowp(C0, dt, dev)
+    cx.gemm(to_dev_lowp(A, dt, dev), to_dev_lowp(B, dt, dev), Cd, alpha=0.75, beta=-1.25)
+    assert cx.last_kernel().startswith("gemm_tc_")
+    assert O.max_relative(O.from_lowp(lowp_bits(Cd), dt), O.from_lowp(ref, dt)) <= LOWP_TOL
+
+
+def test_lowp_strided_leading_dims(dev):
+    """Row-major views with padded leading dimensions (multiples of 8)."""
+    dt = O.BF16
+    M, N, K = 200, 192, 136
+    Ab = O.to_lowp(O.normal((M, K + 24), seed=4), dt)
+    Bb = O.to_lowp(O.normal((K, N + 8), seed=5), dt)
+    A = to_dev_lowp(Ab, dt, dev)[:, :K]
+    B = to_dev_lowp(Bb, dt, dev)[:, :N]
+    Cbig = torch.zeros(M, N + 16, device=dev, dtype=torch.bfloat16)
+    C = Cbig[:, :N]
+    cx.gemm(A, B, C)
+    assert cx.last_kernel().startswith("gemm_tc_")
+    ref = O.gemm_lowp(dt, np.ascontiguousarray(Ab[:, :K]), np.ascontiguousarray(Bb[:, :N]))
+    assert O.max_relative(O.from_lowp(lowp_bits(C.contiguous()), dt), O.from_lowp(ref, dt)) <= LOWP_TOL
+    assert torch.count_nonzero(Cbig[:, N:]) == 0  # padding columns untouched
+
+
+def test_lowp_unaligned_uses_generic(dev):
+    dt = O.F16
+    A = O.to_lowp(O.normal((50, 37), seed=1), dt)
+    B = O.to_lowp(O.normal((37, 45), seed=2), dt)
+    C = cx.gemm(to_dev_lowp(A, dt, dev), to_dev_lowp(B, dt, dev))
+    assert cx.last_kernel() == "gemm_simt_generic"
+    ref = O.gemm_lowp(dt, A, B)
+    assert O.max_relative(O.from_lowp(lowp_bits(C), dt), O.from_lowp(ref, dt)) <= LOWP_TOL
+
+
+def _sampled_check(C, A32, B32, rows, cols, tol):
+    ref = O.gemm_sample_f64(A32, B32, rows, cols)
+    got = C[rows][:, cols].float().cpu().numpy()
+    return O.max_relative(got, ref)
+
+
+def test_c3_fp16_8192_full(dev):
+    """C3: fp16 8192^3, A,B ~ N(0,1)/sqrt(K), fp32 accumulate, fp16 out."""
+    n = 8192
+    dt = O.F16
+    A16 = O.to_lowp(O.normal((n, n), seed=0) / np.sqrt(n), dt)
+    B16 = O.to_lowp(O.normal((n, n), seed=1) / np.sqrt(n), dt)
+    A, B = to_dev_lowp(A16, dt, dev), to_dev_lowp(B16, dt, dev)
+    C = cx.gemm(A, B)
+    assert cx.last_kernel() == "gemm_tc_128x256"
+    full = fp32_reference_gpu(A, B)
+    assert O.max_relative(C.float().cpu().numpy(), full.cpu().numpy()) <= LOWP_TOL
+    rng = np.random.default_rng(0)
+    rows = np.sort(rng.choice(n, 8, replace=False))
+    cols = np.sort(rng.choice(n, 256, replace=False))
+    assert _sampled_check(C, O.from_lowp(A16, dt), O.from_lowp(B16, dt), rows, cols, LOWP_TOL) <= LOWP_TOL
+
+
+def test_c5_bf16_linear_full(dev):
+    """C5: X 4096x8192 ~ N(0,1), W 8192x28672 ~ N(0,0.02), bf16 out."""
+    M, K, N = 4096, 8192, 28672
+    dt = O.BF16
+    X16 = O.to_lowp(O.normal((M, K), seed=0), dt)
+    W16 = O.to_lowp(O.normal((K, N), seed=1, std=0.02), dt)
+    X, W = to_dev_lowp(X16, dt, dev), to_dev_lowp(W16, dt, dev)
+    Y = cx.gemm(X, W)
+    full = fp32_reference_gpu(X, W)
+    assert O.max_relative(Y.float().cpu().numpy(), full.cpu().numpy()) <= LOWP_TOL
+    del full
+    rng = np.random.default_rng(1)
+    rows = np.sort(rng.choice(M, 4, replace=False))
+    cols = np.sort(rng.choice(N, 128, replace=False))
+    assert _sampled_check(Y, O.from_lowp(X16, dt), O.from_lowp(W16, dt), rows, cols, LOWP_TOL) <= LOWP_TOL
+
+
+def test_deterministic_lowp(dev):
+    dt = O.BF16
+    A = to_dev_lowp(O.to_lowp(O.normal((1024, 2048), seed=1), dt), dt, dev)
+    B = to_dev_lowp(O.to_lowp(O.normal((2048, 1536), seed=2), dt), dt, dev)
+    assert torch.equal(cx.gemm(A, B), cx.gemm(A, B))
