@@ -2,6 +2,7 @@
 // module-wide device error word (cuopx::g_device_error) and every kernel
 // live in one CUDA module without relocatable-device-code linking.
 #include "capi.cu"
+#include "gemv_stream.cu"
 #include "gemv.cu"
 #include "gemm_simt.cu"
 #include "gemm_tc.cu"

@@ -12,6 +12,9 @@
 //  * gemv_t_splitk — transposed: each thread owns 16 bytes of adjacent
 //                    output columns and walks rows (coalesced 16-byte loads),
 //                    rows split over CTAs, same last-CTA reduction.
+// The streaming kernels in gemv_stream.cu take precedence whenever rows are
+// 16-byte aligned (and, for y = A x, x fits eight vectors per lane); these
+// kernels cover every other shape.
 //
 // Math follows the reference kernels: y_i = alpha * sum_j A_ij x_j + beta * y_i
 // (src/cuda_op/detail/cuBlas/gemv.cu:10-23; transposed indexing A[col*m+row]
@@ -349,6 +352,11 @@ int launch_gemv(int trans, int64_t M, int64_t N, double alpha_d, const void* A_,
   const T* x = static_cast<const T*>(x_);
   T* y = static_cast<T*>(y_);
   const Acc alpha = static_cast<Acc>(alpha_d), beta = static_cast<Acc>(beta_d);
+  // Streaming kernels (gemv_stream.cu) first; the kernels below cover the
+  // shapes and alignments they do not take.
+  const int rs = launch_gemv_stream<T>(trans, M, N, alpha_d, A_, lda, x_, beta_d, y_, ws, ws_bytes, kCounterBytes,
+                                       stream);
+  if (rs >= 0) return rs;
   GemvPlan p = plan_gemv<T>(trans, M, N, lda, A_, x_, device_sm_count());
   const size_t need = p.partial_bytes + p.counter_bytes;
   if (p.splits > 1 && (ws == nullptr || ws_bytes < need || (reinterpret_cast<uintptr_t>(ws) % kAlign) != 0)) {
@@ -408,7 +416,8 @@ size_t gemv_workspace_size(int dtype, int trans, int64_t M, int64_t N) {
     case CUOPX_BF16: p = plan_gemv<__nv_bfloat16>(trans, M, N, trans ? M : N, al, al, sms); break;
     default: return 0;
   }
-  return p.partial_bytes + p.counter_bytes;
+  const size_t stream_ws = gemv_stream_workspace(dtype, trans, M, N);
+  return std::max(p.partial_bytes + p.counter_bytes, stream_ws ? stream_ws + kCounterBytes : size_t(0));
 }
 
 int gemv_dispatch(int dtype, int trans, int64_t M, int64_t N, double alpha, const void* A, int64_t lda,

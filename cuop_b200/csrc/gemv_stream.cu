@@ -1,0 +1,354 @@
+// Streaming GEMV kernels sized for B200 HBM3e.
+//
+// Measured on this part (1 GiB read probe): plain 16-byte loads from two
+// 256..1024-thread CTAs per SM with 4-16 loads in flight per thread sustain
+// ~6.3 TB/s, while TMA bulk copies of 8 KB stall near 4.8 TB/s and 32 KB
+// bulk copies whose slots are then read back from shared memory reach ~6.0.
+// Both kernels below therefore stream A with ld.global.nc (L1 no-allocate)
+// and keep 16 loads of 16 bytes in flight per thread, two 256-thread CTAs
+// per SM.
+//
+// gemv_n_xreg (y = A x): CTA c owns rows [c*R, (c+1)*R); warp w owns the fixed
+//   column slice [w*32*KV, (w+1)*32*KV) vectors, so its slice of x lives in
+//   registers for the whole kernel.  Each warp reduces its slice of two rows
+//   at a time (fma chains per lane, then a butterfly shuffle); the 8 warp
+//   partials of each row are added in warp order from shared memory.
+// gemv_t_lsu (y = A^T x, A is N x M): the grid is (column strips) x (row
+//   splits); thread t owns the 16-byte column group t of its strip and walks
+//   the split's rows 16 at a time.  Split partials go to the workspace and
+//   the last CTA of a strip adds them in split order, issuing the partial
+//   loads in independent batches so the tail is not one long latency chain.
+// Both are deterministic: summation order depends only on the shape.
+//
+// Math: y_i = alpha * sum_j op(A)_ij x_j + beta * y_i (the reference's gemv
+// kernels, src/cuda_op/detail/cuBlas/gemv.cu:10-23; transposed indexing
+// A[col*m+row], gemv.cu:17), fp32 accumulation (fp64 for double).
+#include "common.cuh"
+#include "dispatch.h"
+
+namespace cuopx {
+
+namespace {
+
+constexpr int GS_THREADS = 256;
+constexpr int GS_WARPS = GS_THREADS / 32;
+constexpr int GS_ROWS_MAX = 64;  // rows per CTA in gemv_n_xreg
+constexpr int GS_T_UNROLL = 16;  // rows in flight per thread in gemv_t_lsu
+constexpr int GS_T_RED_BATCH = 8;  // partial loads issued together in the final reduction
+
+__device__ __forceinline__ uint4 ld_nc16(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack_v(const uint4& v, typename AccOf<T>::type* out) {
+  const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+  for (int i = 0; i < 16 / (int)sizeof(T); ++i) out[i] = to_acc<T>(e[i]);
+}
+
+template <typename Acc>
+__device__ __forceinline__ Acc warp_allsum(Acc v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// ---------------------------------------------------------------------------
+template <typename T, int KV>
+__global__ void __launch_bounds__(GS_THREADS, 2)
+    gemv_n_xreg(int64_t M, int64_t N, typename AccOf<T>::type alpha, const T* __restrict__ A, int64_t lda,
+                const T* __restrict__ x, typename AccOf<T>::type beta, T* __restrict__ y, int rows_per_cta) {
+  using Acc = typename AccOf<T>::type;
+  constexpr int V = 16 / sizeof(T);
+  __shared__ Acc part[GS_ROWS_MAX][GS_WARPS];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t nvec = N / V;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_cta;
+  const int64_t r1 = min(M, r0 + rows_per_cta);
+  if (r0 >= r1) return;
+
+  Acc xr[KV][V];
+  bool valid[KV];
+#pragma unroll
+  for (int k = 0; k < KV; ++k) {
+    const int64_t vi = static_cast<int64_t>(warp) * 32 * KV + k * 32 + lane;
+    valid[k] = vi < nvec;
+    if (valid[k]) {
+      unpack_v<T>(__ldg(reinterpret_cast<const uint4*>(x) + vi), xr[k]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < V; ++i) xr[k][i] = 0;
+    }
+  }
+  const int64_t vbase = static_cast<int64_t>(warp) * 32 * KV + lane;
+
+  int64_t r = r0;
+  for (; r + 1 < r1; r += 2) {
+    const uint4* a0 = reinterpret_cast<const uint4*>(A + r * lda) + vbase;
+    const uint4* a1 = reinterpret_cast<const uint4*>(A + (r + 1) * lda) + vbase;
+    uint4 v0[KV], v1[KV];
+#pragma unroll
+    for (int k = 0; k < KV; ++k) {
+      v0[k] = valid[k] ? ld_nc16(a0 + k * 32) : make_uint4(0, 0, 0, 0);
+      v1[k] = valid[k] ? ld_nc16(a1 + k * 32) : make_uint4(0, 0, 0, 0);
+    }
+    Acc s0 = 0, s1 = 0;
+#pragma unroll
+    for (int k = 0; k < KV; ++k) {
+      Acc f0[V], f1[V];
+      unpack_v<T>(v0[k], f0);
+      unpack_v<T>(v1[k], f1);
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        s0 = fma(f0[i], xr[k][i], s0);
+        s1 = fma(f1[i], xr[k][i], s1);
+      }
+    }
+    s0 = warp_allsum(s0);
+    s1 = warp_allsum(s1);
+    if (lane == 0) {
+      part[r - r0][warp] = s0;
+      part[r + 1 - r0][warp] = s1;
+    }
+  }
+  if (r < r1) {
+    const uint4* a0 = reinterpret_cast<const uint4*>(A + r * lda) + vbase;
+    uint4 v0[KV];
+#pragma unroll
+    for (int k = 0; k < KV; ++k) v0[k] = valid[k] ? ld_nc16(a0 + k * 32) : make_uint4(0, 0, 0, 0);
+    Acc s0 = 0;
+#pragma unroll
+    for (int k = 0; k < KV; ++k) {
+      Acc f0[V];
+      unpack_v<T>(v0[k], f0);
+#pragma unroll
+      for (int i = 0; i < V; ++i) s0 = fma(f0[i], xr[k][i], s0);
+    }
+    s0 = warp_allsum(s0);
+    if (lane == 0) part[r - r0][warp] = s0;
+  }
+  __syncthreads();
+  for (int64_t rr = threadIdx.x; rr < r1 - r0; rr += GS_THREADS) {
+    Acc s = part[rr][0];
+#pragma unroll
+    for (int w = 1; w < GS_WARPS; ++w) s += part[rr][w];
+    Acc res = alpha * s;
+    if (beta != Acc(0)) res += beta * to_acc<T>(y[r0 + rr]);
+    y[r0 + rr] = from_acc<T>(res);
+  }
+}
+
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(GS_THREADS, 2)
+    gemv_t_lsu(int64_t M, int64_t N, typename AccOf<T>::type alpha, const T* __restrict__ A, int64_t lda,
+               const T* __restrict__ x, typename AccOf<T>::type beta, T* __restrict__ y, int64_t rows_per_split,
+               typename AccOf<T>::type* __restrict__ partials, unsigned int* __restrict__ counters) {
+  using Acc = typename AccOf<T>::type;
+  constexpr int V = 16 / sizeof(T);
+  constexpr int U = GS_T_UNROLL;
+  constexpr int64_t STRIP = static_cast<int64_t>(GS_THREADS) * V;  // columns per strip
+  __shared__ unsigned int s_last;
+  const int tid = threadIdx.x;
+  const int64_t col = static_cast<int64_t>(blockIdx.x) * STRIP + static_cast<int64_t>(tid) * V;
+  const bool has = col < M;  // M % V == 0: the group is all in or all out
+  const int64_t j0 = static_cast<int64_t>(blockIdx.y) * rows_per_split;
+  const int64_t j1 = min(N, j0 + rows_per_split);
+  const unsigned int splits = gridDim.y;
+
+  Acc acc[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) acc[i] = 0;
+
+  if (has) {
+    const T* ap = A + col;
+    int64_t j = j0;
+    for (; j + U <= j1; j += U) {
+      uint4 v[U];
+      Acc xv[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) v[u] = ld_nc16(ap + (j + u) * lda);
+#pragma unroll
+      for (int u = 0; u < U; ++u) xv[u] = to_acc<T>(__ldg(x + j + u));
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        Acc f[V];
+        unpack_v<T>(v[u], f);
+#pragma unroll
+        for (int i = 0; i < V; ++i) acc[i] = fma(f[i], xv[u], acc[i]);
+      }
+    }
+    for (; j < j1; ++j) {
+      const Acc xj = to_acc<T>(__ldg(x + j));
+      Acc f[V];
+      unpack_v<T>(ld_nc16(ap + j * lda), f);
+#pragma unroll
+      for (int i = 0; i < V; ++i) acc[i] = fma(f[i], xj, acc[i]);
+    }
+  }
+
+  if (splits == 1) {
+    if (has) {
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        Acc res = alpha * acc[i];
+        if (beta != Acc(0)) res += beta * to_acc<T>(y[col + i]);
+        y[col + i] = from_acc<T>(res);
+      }
+    }
+    return;
+  }
+  if (has) {
+    Acc* dst = partials + static_cast<int64_t>(blockIdx.y) * M + col;
+#pragma unroll
+    for (int i = 0; i < V; ++i) dst[i] = acc[i];
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned int prev = atomicAdd(&counters[blockIdx.x], 1u);
+    if (prev >= splits) record_device_error(kDevErrSplitReduce);
+    s_last = (prev == splits - 1) ? 1u : 0u;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if (has) {
+    Acc sum[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) sum[i] = 0;
+    // Split order 0..splits-1; loads issued GS_T_RED_BATCH at a time.
+    for (unsigned int k0 = 0; k0 < splits; k0 += GS_T_RED_BATCH) {
+      Acc pv[GS_T_RED_BATCH][V];
+#pragma unroll
+      for (int b = 0; b < GS_T_RED_BATCH; ++b) {
+        const unsigned int k = k0 + b;
+#pragma unroll
+        for (int i = 0; i < V; ++i)
+          pv[b][i] = (k < splits) ? __ldcg(partials + static_cast<int64_t>(k) * M + col + i) : Acc(0);
+      }
+#pragma unroll
+      for (int b = 0; b < GS_T_RED_BATCH; ++b)
+        if (k0 + b < splits)
+#pragma unroll
+          for (int i = 0; i < V; ++i) sum[i] += pv[b][i];
+    }
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      Acc res = alpha * sum[i];
+      if (beta != Acc(0)) res += beta * to_acc<T>(y[col + i]);
+      y[col + i] = from_acc<T>(res);
+    }
+  }
+  if (tid == 0) counters[blockIdx.x] = 0u;
+}
+
+}  // namespace
+
+struct GemvStreamPlan {
+  bool ok = false;
+  bool trans = false;
+  int kv = 0;                 // gemv_n_xreg vectors per lane
+  int64_t grid = 0;           // gemv_n_xreg CTAs
+  int rows_per_cta = 0;
+  int64_t strips = 0, splits = 0, rows_per_split = 0;  // gemv_t_lsu
+  size_t partial_bytes = 0;
+};
+
+template <typename T>
+GemvStreamPlan plan_gemv_stream(int trans, int64_t M, int64_t N, int64_t lda, const void* A, const void* x,
+                                int sms) {
+  GemvStreamPlan p;
+  using Acc = typename AccOf<T>::type;
+  constexpr int V = 16 / sizeof(T);
+  const bool a_al = (reinterpret_cast<uintptr_t>(A) % 16 == 0) && ((lda * (int64_t)sizeof(T)) % 16 == 0);
+  if (!a_al || M <= 0 || N <= 0) return p;
+  const int64_t ctas_full = 2LL * sms;  // two resident CTAs per SM
+  if (!trans) {
+    if (N % V || reinterpret_cast<uintptr_t>(x) % 16) return p;
+    const int64_t nvec = N / V;
+    if (nvec > 8 * 32 * GS_WARPS) return p;  // x slice must fit 8 vectors per lane
+    if (M < sms) return p;                    // short-wide shapes: split-K kernel
+    int kv = 1;
+    while (kv * 32 * GS_WARPS < nvec) kv *= 2;
+    p.kv = kv;
+    int64_t rows = (M + ctas_full - 1) / ctas_full;
+    rows = std::min<int64_t>(std::max<int64_t>(rows, 1), GS_ROWS_MAX);
+    p.rows_per_cta = static_cast<int>(rows);
+    p.grid = (M + rows - 1) / rows;
+    p.ok = true;
+  } else {
+    if (M % V || N < 16) return p;
+    const int64_t strip = static_cast<int64_t>(GS_THREADS) * V;
+    p.strips = (M + strip - 1) / strip;
+    if (p.strips > 4096) return p;
+    int64_t splits = std::max<int64_t>(1, ctas_full / p.strips);
+    splits = std::min<int64_t>(splits, std::max<int64_t>(1, N / GS_T_UNROLL));
+    splits = std::min<int64_t>(splits, 65535);
+    p.rows_per_split = (N + splits - 1) / splits;
+    p.splits = (N + p.rows_per_split - 1) / p.rows_per_split;
+    if (p.splits > 1) p.partial_bytes = (static_cast<size_t>(p.splits) * M * sizeof(Acc) + 255) / 256 * 256;
+    p.trans = true;
+    p.ok = true;
+  }
+  return p;
+}
+
+// Returns -1 when these kernels do not apply (caller falls back), else a
+// status.  Workspace layout matches gemv.cu: [counters][partials].
+template <typename T>
+int launch_gemv_stream(int trans, int64_t M, int64_t N, double alpha_d, const void* A_, int64_t lda,
+                       const void* x_, double beta_d, void* y_, void* ws, size_t ws_bytes, size_t counter_bytes,
+                       cudaStream_t stream) {
+  using Acc = typename AccOf<T>::type;
+  const int sms = device_sm_count();
+  const GemvStreamPlan p = plan_gemv_stream<T>(trans, M, N, lda, A_, x_, sms);
+  if (!p.ok) return -1;
+  if (p.trans && p.splits > 1 &&
+      (ws == nullptr || ws_bytes < counter_bytes + p.partial_bytes || reinterpret_cast<uintptr_t>(ws) % 256))
+    return -1;
+  const T* A = static_cast<const T*>(A_);
+  const T* x = static_cast<const T*>(x_);
+  T* y = static_cast<T*>(y_);
+  const Acc alpha = static_cast<Acc>(alpha_d), beta = static_cast<Acc>(beta_d);
+  if (!p.trans) {
+    const dim3 grid(static_cast<unsigned>(p.grid));
+    switch (p.kv) {
+      case 1: gemv_n_xreg<T, 1><<<grid, GS_THREADS, 0, stream>>>(M, N, alpha, A, lda, x, beta, y, p.rows_per_cta); break;
+      case 2: gemv_n_xreg<T, 2><<<grid, GS_THREADS, 0, stream>>>(M, N, alpha, A, lda, x, beta, y, p.rows_per_cta); break;
+      case 4: gemv_n_xreg<T, 4><<<grid, GS_THREADS, 0, stream>>>(M, N, alpha, A, lda, x, beta, y, p.rows_per_cta); break;
+      default: gemv_n_xreg<T, 8><<<grid, GS_THREADS, 0, stream>>>(M, N, alpha, A, lda, x, beta, y, p.rows_per_cta); break;
+    }
+    note_launch("gemv_n_xreg");
+  } else {
+    unsigned int* counters = reinterpret_cast<unsigned int*>(ws);
+    Acc* partials = reinterpret_cast<Acc*>(static_cast<char*>(ws) + counter_bytes);
+    const dim3 grid(static_cast<unsigned>(p.strips), static_cast<unsigned>(p.splits));
+    gemv_t_lsu<T><<<grid, GS_THREADS, 0, stream>>>(M, N, alpha, A, lda, x, beta, y, p.rows_per_split, partials,
+                                                  counters);
+    note_launch("gemv_t_lsu");
+  }
+  return check_launch();
+}
+
+size_t gemv_stream_workspace(int dtype, int trans, int64_t M, int64_t N) {
+  const void* al = reinterpret_cast<const void*>(static_cast<uintptr_t>(256));
+  const int sms = device_sm_count();
+  GemvStreamPlan p;
+  const int64_t lda = trans ? M : N;
+  switch (dtype) {
+    case CUOPX_F32: p = plan_gemv_stream<float>(trans, M, N, lda, al, al, sms); break;
+    case CUOPX_F64: p = plan_gemv_stream<double>(trans, M, N, lda, al, al, sms); break;
+    case CUOPX_F16: p = plan_gemv_stream<__half>(trans, M, N, lda, al, al, sms); break;
+    case CUOPX_BF16: p = plan_gemv_stream<__nv_bfloat16>(trans, M, N, lda, al, al, sms); break;
+    default: return 0;
+  }
+  return p.ok ? p.partial_bytes : 0;
+}
+
+}  // namespace cuopx

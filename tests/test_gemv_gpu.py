@@ -102,7 +102,7 @@ def test_benchmark_size_vs_cpu_and_reference_operator(dev, trans):
     x32 = O.uniform(N_, seed=1)
     A, x = to_dev_f32(A32, dev), to_dev_f32(x32, dev)
     y = cx.gemv(A, x, trans=trans)
-    assert cx.last_kernel() == ("gemv_t_splitk" if trans else "gemv_n_rows")
+    assert cx.last_kernel() == ("gemv_t_lsu" if trans else "gemv_n_xreg")
     cpu = O.gemv_f32(A32, x32, trans=trans)
     exact = O.gemv_f64acc(A32, x32, trans=trans)
     tol = 1e-5 * np.sqrt(N_)
