@@ -15,6 +15,7 @@ _lib = None
 SUCCESS = 0
 NOT_IMPLEMENTED = 1001
 TIMEOUT = 1003
+RESOURCE_UNAVAILABLE = 1005
 CUDA_ERROR = 2000
 OUT_OF_MEMORY = 3001
 INVALID_ARGUMENT = 4001
@@ -25,7 +26,7 @@ SHAPE_MISMATCH = 10002
 UNSUPPORTED_TYPE = 11001
 
 STATUS_NAMES = {
-    0: "SUCCESS", 1001: "NOT_IMPLEMENTED", 1003: "TIMEOUT", 2000: "CUDA_ERROR", 3001: "OUT_OF_MEMORY",
+    0: "SUCCESS", 1001: "NOT_IMPLEMENTED", 1003: "TIMEOUT", 1005: "RESOURCE_UNAVAILABLE", 2000: "CUDA_ERROR", 3001: "OUT_OF_MEMORY",
     4001: "INVALID_ARGUMENT", 6002: "EXECUTION_TIMEOUT", 6005: "KERNEL_NOT_FOUND", 7003: "NOT_COMPILED",
     10002: "SHAPE_MISMATCH", 11001: "UNSUPPORTED_TYPE",
 }
@@ -47,6 +48,7 @@ SIGNATURES = [
      [_int, _int, _int, _i64, _i64, _i64, _dbl, _vp, _i64, _i64, _vp, _i64, _i64, _dbl, _vp, _i64, _i64, _i64, _vp]),
     ("cuopx_gemv_workspace_size", _sz, [_int, _int, _i64, _i64]),
     ("cuopx_gemv", _int, [_int, _int, _i64, _i64, _dbl, _vp, _i64, _vp, _dbl, _vp, _vp, _sz, _vp]),
+    ("cuopx_gemv_noalloc", _int, [_int, _int, _i64, _i64, _dbl, _vp, _i64, _vp, _dbl, _vp, _vp]),
     ("cuopx_gather_column_blocks", _int, [_int, _i64, _i64, _i64, _vp, _vp, _i64, _vp]),
     ("cuopx_vector_workspace_size", _sz, [_i64]),
     ("cuopx_dot", _int, [_i64, _fp, _i64, _fp, _i64, _fp, _vp, _sz, _vp]),

@@ -4,6 +4,7 @@
 #include "capi.cu"
 #include "gemv_stream.cu"
 #include "gemv.cu"
+#include "gemv_noalloc.cu"
 #include "gemm_simt.cu"
 #include "gemm_tc.cu"
 #include "vector_ops.cu"

@@ -25,6 +25,7 @@ extern "C" {
 #define CUOPX_SUCCESS 0
 #define CUOPX_NOT_IMPLEMENTED 1001
 #define CUOPX_TIMEOUT 1003
+#define CUOPX_RESOURCE_UNAVAILABLE 1005
 #define CUOPX_CUDA_ERROR 2000
 #define CUOPX_OUT_OF_MEMORY 3001
 #define CUOPX_INVALID_ARGUMENT 4001
@@ -95,6 +96,23 @@ int cuopx_gemm_strided_batched(int dtype, int transA, int transB, int64_t M, int
 size_t cuopx_gemv_workspace_size(int dtype, int trans, int64_t M, int64_t N);
 int cuopx_gemv(int dtype, int trans, int64_t M, int64_t N, double alpha, const void* A, int64_t lda,
                const void* x, double beta, void* y, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * GEMV that allocates nothing: same arguments and result as cuopx_gemv, but
+ * the split-K scratch comes from a fixed 2 MiB array inside the library
+ * (per device, held until exit) instead of a caller-provided workspace.
+ * For callers that may not allocate device memory while running (plugin
+ * hosts that own all device memory, latency-bound serving loops where an
+ * allocation can stall or fail).  No counterpart in the reference.
+ * Returns CUOPX_RESOURCE_UNAVAILABLE when the kernel chosen for the call
+ * needs more than 2 MiB of scratch (fp32/fp64 with 16-byte-aligned rows
+ * never do; fp16/bf16 transposed GEMV of large matrices does).  The first call on a device resolves the array's
+ * device address; make it before any stream capture.  Calls share the array:
+ * calls that overlap on the GPU race, so order them on one stream.  Each call
+ * zeroes the array's counter block on `stream` before its kernels run.
+ */
+int cuopx_gemv_noalloc(int dtype, int trans, int64_t M, int64_t N, double alpha, const void* A, int64_t lda,
+                       const void* x, double beta, void* y, void* stream);
 
 /*
  * Column-block gather for N-sharded GEMM: `blocks` is G contiguous
