@@ -286,21 +286,25 @@ ORACLE_API void oracle_gemv_f32(int trans, int64_t M, int64_t N, float alpha, co
       y[i] = r;
     }
   } else {
-    /* Column sums walk rows of A (contiguous) and keep M running fma chains;
-     * each output's chain still runs j = 0..N-1 in order.                   */
+    /* Each thread owns a contiguous range of outputs and walks every row of A
+     * over that range; each output's fma chain still runs j = 0..N-1 in order. */
     float* acc = (float*)calloc((size_t)(M > 0 ? M : 1), sizeof(float));
 #pragma omp parallel num_threads(nthreads)
     {
-#pragma omp for schedule(static)
-      for (int64_t i = 0; i < M; ++i) acc[i] = 0.0f;
+#ifdef _OPENMP
+      const int64_t nt = omp_get_num_threads(), t = omp_get_thread_num();
+#else
+      const int64_t nt = 1, t = 0;
+#endif
+      const int64_t chunk = ((M + nt - 1) / nt + 15) / 16 * 16;
+      const int64_t i0 = t * chunk < M ? t * chunk : M;
+      const int64_t i1 = i0 + chunk < M ? i0 + chunk : M;
       for (int64_t j = 0; j < N; ++j) {
         const float* arow = A + j * lda;
         const float xj = x[j];
-#pragma omp for schedule(static)
-        for (int64_t i = 0; i < M; ++i) acc[i] = fmaf(arow[i], xj, acc[i]);
+        for (int64_t i = i0; i < i1; ++i) acc[i] = fmaf(arow[i], xj, acc[i]);
       }
-#pragma omp for schedule(static)
-      for (int64_t i = 0; i < M; ++i) {
+      for (int64_t i = i0; i < i1; ++i) {
         float r = alpha * acc[i];
         if (beta != 0.0f) r = r + beta * y[i];
         y[i] = r;
