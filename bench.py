@@ -147,8 +147,50 @@ def max_over_ranks(v: float, world: int) -> float:
     return float(t.item())
 
 
+def capture_graph(fn, n):
+    """CUDA graph of fn(0..n-1).  The launches inside are the library's own
+    kernels through its public API; replaying the graph removes the host's
+    per-call Python/ctypes overhead from the device timeline.  Returns the
+    graph and the number of cuopx kernels it holds."""
+    import torch
+    import cuop_b200 as cx
+
+    fn(0)  # lazy per-device set-up (function attributes, workspaces) outside capture
+    torch.cuda.synchronize()
+    c0 = cx.launch_count()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(n):
+            fn(i)
+    torch.cuda.synchronize()
+    return g, cx.launch_count() - c0
+
+
+def time_graph(fn, steps, warmup, world):
+    """Device time (ms per call) of `steps` calls of fn replayed as one CUDA
+    graph after `warmup` eager calls; max over ranks."""
+    import torch
+
+    for i in range(warmup):
+        fn(i)
+    g, _ = capture_graph(fn, steps)
+    g.replay()  # first replay uploads the graph
+    barrier(world)
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    g.replay()
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    barrier(world)
+    del g
+    return max_over_ranks(ms, world)
+
+
 def time_loop(fn, steps, warmup, world, stream=None):
-    """Device time (ms per call) of `fn` over `steps` calls, max over ranks."""
+    """Eager device time (ms per call) of `steps` calls, max over ranks (used
+    where a step holds NCCL collectives, which stay out of graphs)."""
     import torch
 
     for _ in range(warmup):
@@ -199,33 +241,28 @@ def run_gemv(args, rank, world, local_rank):
     barrier(world)
 
     K = args.steps
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
-    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    n_launch0 = cx.launch_count()
+    # The timed region replays one CUDA graph of K steps (2K kernels).
+    g_step, launches = capture_graph(step, K)
     kn = kt = None
+    cx.gemv(An[0], x, yn)
+    kn = cx.last_kernel()
+    cx.gemv(At[0], x, yt, trans=True)
+    kt = cx.last_kernel()
+    g_step.replay()
+    barrier(world)
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clk:
         e_start.record(stream)
-        for i in range(K):
-            ev = evs[i]
-            ev[0].record(stream)
-            cx.gemv(An[i % sets], x, yn)
-            if i == 0:
-                kn = cx.last_kernel()
-            ev[1].record(stream)
-            cx.gemv(At[i % sets], x, yt, trans=True)
-            if i == 0:
-                kt = cx.last_kernel()
-            ev[2].record(stream)
+        g_step.replay()
         e_end.record(stream)
         torch.cuda.synchronize()
-    launches = cx.launch_count() - n_launch0
     ms_local = e_start.elapsed_time(e_end) / K
-    t_n = statistics.mean(ev[0].elapsed_time(ev[1]) for ev in evs)
-    t_t = statistics.mean(ev[1].elapsed_time(ev[2]) for ev in evs)
+    del g_step
     barrier(world)
     ms = max_over_ranks(ms_local, world)
-    t_n = max_over_ranks(t_n, world)
-    t_t = max_over_ranks(t_t, world)
+    # Per-kernel device time: each kernel alone, back to back, same rotation.
+    t_n = time_graph(lambda i: cx.gemv(An[i % sets], x, yn), K, 2, world)
+    t_t = time_graph(lambda i: cx.gemv(At[i % sets], x, yt, trans=True), K, 2, world)
 
     hbm, bf16, bf16_sus, peak_src = load_peaks()
     value = world * 2 * GEMV_BYTES / (ms * 1e-3) / 1e9
@@ -253,6 +290,7 @@ def run_gemv(args, rank, world, local_rank):
                      "algorithmic_bytes": GEMV_BYTES},
         "kernels": kernels,
         "gpu_launches": launches,
+        "timing": "timed region = one CUDA graph replay of K steps; per-kernel times from graphs of K launches",
         "clocks": clk.summary(),
         "e2e": e2e,
     }
@@ -336,7 +374,7 @@ def run_configs(args, rank, world, local_rank):
     A = torch.rand(n, n, device=dev, generator=g) * 2 - 1
     B = torch.rand(n, n, device=dev, generator=g) * 2 - 1
     C = torch.empty(n, n, device=dev)
-    ms = time_loop(lambda i: cx.gemm(A, B, C), steps * 4, 5, world)
+    ms = time_graph(lambda i: cx.gemm(A, B, C), steps * 4, 5, world)
     tf = 2 * n ** 3 / (ms * 1e-3) / 1e12
     out["c1_fp32_gemm_1024"] = {"tflops_total": round(world * tf, 3), "ms": round(ms, 5), "kernel": cx.last_kernel(),
                                 "frac_fp32_simt_nominal": round(tf / FP32_SIMT_NOMINAL_TFLOPS, 4),
@@ -350,7 +388,7 @@ def run_configs(args, rank, world, local_rank):
     Wl = (torch.randn(n, Wfull_cols, device=dev, generator=g) / math.sqrt(n)).half()
     if world == 1:
         C = torch.empty(n, n, device=dev, dtype=torch.half)
-        ms = time_loop(lambda i: cx.gemm(A, Wl, C), steps, 3, world)
+        ms = time_graph(lambda i: cx.gemm(A, Wl, C), steps, 3, world)
         kname = cx.last_kernel()
         ms_local = ms
     else:
@@ -358,7 +396,7 @@ def run_configs(args, rank, world, local_rank):
         Cfull = torch.empty(n, n, device=dev, dtype=torch.half)
         ms = time_loop(lambda i: sg.forward(A, out=Cfull), steps, 3, world)
         Cl = torch.empty(n, Wfull_cols, device=dev, dtype=torch.half)
-        ms_local = time_loop(lambda i: cx.gemm(A, Wl, Cl), steps, 3, world)
+        ms_local = time_graph(lambda i: cx.gemm(A, Wl, Cl), steps, 3, world)
         kname = cx.last_kernel()
     tf_local = 2 * n * n * Wfull_cols / (ms_local * 1e-3) / 1e12
     out["c3_fp16_gemm_8192"] = {
@@ -378,7 +416,7 @@ def run_configs(args, rank, world, local_rank):
     As = [torch.randn(lb, M, K, device=dev, generator=g).bfloat16() for _ in range(sets)]
     Bs = [torch.randn(lb, K, N_, device=dev, generator=g).bfloat16() for _ in range(sets)]
     Cs = [torch.empty(lb, M, N_, device=dev, dtype=torch.bfloat16) for _ in range(sets)]
-    ms = time_loop(lambda i: cx.batched_gemm(As[i % sets], Bs[i % sets], Cs[i % sets]), steps * 4, 5, world)
+    ms = time_graph(lambda i: cx.batched_gemm(As[i % sets], Bs[i % sets], Cs[i % sets]), steps * 4, 5, world)
     bytes_total = batch * (M * K + K * N_ + M * N_) * 2
     gbs_local = lb * (M * K + K * N_ + M * N_) * 2 / (ms * 1e-3) / 1e9
     out["c4_bf16_batched_4096x128x128x64"] = {
@@ -395,7 +433,7 @@ def run_configs(args, rank, world, local_rank):
     nl = N_ // world
     Wl = (torch.randn(K, nl, device=dev, generator=g) * 0.02).bfloat16()
     Yl = torch.empty(M, nl, device=dev, dtype=torch.bfloat16)
-    ms_local = time_loop(lambda i: cx.gemm(X, Wl, Yl), steps, 3, world)
+    ms_local = time_graph(lambda i: cx.gemm(X, Wl, Yl), steps, 3, world)
     kname = cx.last_kernel()
     if world > 1:
         sg = sharding.ColumnShardedGemm(Wl, world)
