@@ -9,10 +9,10 @@ large-GEMM paths need on one 8-GPU box:
 * Column sharding (large GEMM / linear layer): rank r holds the weight column
   block W[:, r*N/G:(r+1)*N/G] as its own contiguous [K, N/G] matrix and
   computes Y_r = X W_r.  Only when the caller wants the full Y on every rank
-  is there an exchange: an NCCL all-gather of the [M, N/G] blocks into a
-  [G, M, N/G] staging buffer, issued per M-chunk right after that chunk's GEMM
-  so the transfer of chunk c overlaps the GEMM of chunk c+1, followed by the
-  column-block gather kernel that writes row-major [M, N].
+  is there an exchange: per M-chunk, an NCCL all-gather of that chunk's
+  [rows, N/G] blocks into a [G, rows, N/G] receive buffer, issued right after
+  the chunk's GEMM so the transfer of chunk c overlaps the GEMM of chunk c+1,
+  then the column-block gather kernel writes those rows of row-major [M, N].
 
 torch.distributed (NCCL over NVLink/NVSwitch) is plumbing only; every GEMM and
 the gather run through libcuopx.so.
@@ -20,7 +20,7 @@ the gather run through libcuopx.so.
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import Optional
+from typing import Callable, Optional
 
 import torch
 import torch.distributed as dist
@@ -52,16 +52,26 @@ class ColumnShardedGemm:
     """Y = X @ W with W split by columns over `world` ranks.
 
     w_local: this rank's contiguous [K, N/G] column block (N divisible by G).
+    gemm_fn / gather_fn default to the library's kernels; tests of the host
+    logic on CPU ranks substitute plain torch equivalents.
     """
 
     w_local: torch.Tensor
     world: int
     group: Optional[dist.ProcessGroup] = None
     chunks: int = 4
+    gemm_fn: Optional[Callable] = None
+    gather_fn: Optional[Callable] = None
+
+    def _gemm(self, X, W, out):
+        return (self.gemm_fn or ops.gemm)(X, W, out)
+
+    def _gather(self, blocks, out):
+        return (self.gather_fn or ops.gather_column_blocks)(blocks, out)
 
     def local(self, X: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """This rank's [M, N/G] output block (no communication)."""
-        return ops.gemm(X, self.w_local, out)
+        return self._gemm(X, self.w_local, out)
 
     def forward(self, X: torch.Tensor, gather: bool = True, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         if not gather or self.world == 1:
@@ -79,13 +89,13 @@ class ColumnShardedGemm:
             r0, r1 = shard_range(M, c, chunks)
             if r1 <= r0:
                 continue
-            ops.gemm(X[r0:r1], self.w_local, local_blk[r0:r1])
-            recv = torch.empty((G, r1 - r0, nb), dtype=X.dtype, device=X.device)
+            self._gemm(X[r0:r1], self.w_local, local_blk[r0:r1])
+            recv = torch.empty((G * (r1 - r0), nb), dtype=X.dtype, device=X.device)
             h = dist.all_gather_into_tensor(recv, local_blk[r0:r1], group=self.group, async_op=True)
-            pending.append((r0, r1, recv, h))
+            pending.append((r0, r1, recv.view(G, r1 - r0, nb), h))
         for r0, r1, recv, h in pending:
             h.wait()  # the current stream waits for this chunk's collective
-            ops.gather_column_blocks(recv, out[r0:r1])
+            self._gather(recv, out[r0:r1])
         return out
 
 
