@@ -21,7 +21,8 @@ LIB = PKG / "libcuopx.so"
 BUILD_DIR = PKG / "_build"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", f"-I{ROOT / 'include'}", f"-I{CSRC}"]
+COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", f"-I{ROOT / 'include'}",
+          f"-I{ROOT / 'include' / 'cuop'}", f"-I{CSRC}"]
 
 # Device code is one translation unit (see csrc/cuopx_unity.cu); the C++17
 # operator/plugin facade is plain host code compiled by nvcc's host compiler.

@@ -1,0 +1,468 @@
+// C++ tests of the cuOP-compatible facade over libcuopx.so, written the way
+// the reference's GTest suites are (test/cuBlas/test_gemm/test_gemm.cpp,
+// test/cuBlas/test_gemv/test_gemv.cpp, test/cuDNN/test_matmul/test_matmul.cpp):
+// known-answer cases first, then seeded cases checked against the oracle's
+// CPU restatement (oracle/cpu_ref.c, linked as liboracle.so).
+//
+// Usage: test_facade [--host-only] [filter-substring]
+//   --host-only runs only the tests that need no GPU.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <functional>
+#include <string>
+#include <vector>
+
+#include "cuda_op/detail/cuBlas/gemm.hpp"
+#include "cuda_op/detail/cuBlas/gemm_batched.hpp"
+#include "cuda_op/detail/cuBlas/gemv.hpp"
+#include "cuda_op/detail/cuDNN/batchmatmul.hpp"
+#include "cuda_op/detail/cuDNN/matmul.hpp"
+#include "cuopx.h"
+#include "jit/Blas/blas_jit_plugins.hpp"
+#include "jit/global_jit_manager.hpp"
+#include "jit/jit_wrapper.hpp"
+
+extern "C" {
+void oracle_fill_uniform_f32(float* out, int64_t n, uint64_t seed, float lo, float hi);
+void oracle_gemm_f32(int transA, int transB, int64_t M, int64_t N, int64_t K, float alpha, const float* A,
+                     int64_t lda, const float* B, int64_t ldb, float beta, float* C, int64_t ldc, int nthreads);
+void oracle_gemv_f32(int trans, int64_t M, int64_t N, float alpha, const float* A, int64_t lda, const float* x,
+                     float beta, float* y, int nthreads);
+}
+
+using namespace cu_op_mem;
+
+// ------------------------------------------------------------------ harness
+struct TestCase {
+  const char* name;
+  bool needs_gpu;
+  std::function<void()> fn;
+};
+static std::vector<TestCase>& registry() {
+  static std::vector<TestCase> r;
+  return r;
+}
+static int g_failures = 0;
+struct Reg {
+  Reg(const char* n, bool gpu, std::function<void()> f) { registry().push_back({n, gpu, f}); }
+};
+#define TEST_HOST(name) static void name(); static Reg reg_##name(#name, false, name); static void name()
+#define TEST_GPU(name) static void name(); static Reg reg_##name(#name, true, name); static void name()
+#define EXPECT_TRUE(c)                                                                     \
+  do {                                                                                     \
+    if (!(c)) {                                                                            \
+      std::printf("    FAILED %s:%d: %s\n", __FILE__, __LINE__, #c);                       \
+      ++g_failures;                                                                        \
+    }                                                                                      \
+  } while (0)
+#define EXPECT_EQ(a, b) EXPECT_TRUE((a) == (b))
+#define EXPECT_NEAR(a, b, tol)                                                                       \
+  do {                                                                                               \
+    const double va_ = (a), vb_ = (b);                                                               \
+    if (!(std::fabs(va_ - vb_) <= (tol))) {                                                          \
+      std::printf("    FAILED %s:%d: %s=%g vs %s=%g (tol %g)\n", __FILE__, __LINE__, #a, va_, #b, vb_, \
+                  (double)(tol));                                                                    \
+      ++g_failures;                                                                                  \
+    }                                                                                                \
+  } while (0)
+
+template <typename T>
+static std::vector<T> to_host(const Tensor<T>& t) {
+  std::vector<T> h(t.numel());
+  t.copy_to_host(h.data());
+  return h;
+}
+
+static double rel_frobenius(const std::vector<float>& c, const std::vector<float>& r) {
+  double num = 0, den = 0;
+  for (size_t i = 0; i < c.size(); ++i) {
+    num += (double(c[i]) - r[i]) * (double(c[i]) - r[i]);
+    den += double(r[i]) * r[i];
+  }
+  return std::sqrt(num) / (den > 0 ? std::sqrt(den) : 1.0);
+}
+
+// ------------------------------------------------------------------ host-only
+TEST_HOST(StatusCodesMatchReferenceValues) {
+  EXPECT_EQ(static_cast<int>(StatusCode::SUCCESS), 0);
+  EXPECT_EQ(static_cast<int>(StatusCode::CUDA_ERROR), 2000);
+  EXPECT_EQ(static_cast<int>(StatusCode::INVALID_ARGUMENT), 4001);
+  EXPECT_EQ(static_cast<int>(StatusCode::SHAPE_MISMATCH), 10002);
+  EXPECT_EQ(static_cast<int>(StatusCode::UNSUPPORTED_TYPE), 11001);
+  EXPECT_EQ(static_cast<int>(StatusCode::NOT_COMPILED), 7003);
+  EXPECT_EQ(static_cast<int>(StatusCode::KERNEL_NOT_FOUND), 6005);
+  EXPECT_EQ(static_cast<int>(StatusCode::RESOURCE_UNAVAILABLE), CUOPX_RESOURCE_UNAVAILABLE);
+  EXPECT_TRUE(GetErrorCategory(StatusCode::OUT_OF_MEMORY) == ErrorCategory::MEMORY);
+  EXPECT_TRUE(GetErrorCategory(StatusCode::PLUGIN_NOT_FOUND) == ErrorCategory::PLUGIN);
+  EXPECT_TRUE(std::string(StatusCodeToString(StatusCode::TENSOR_SHAPE_MISMATCH)) == "TENSOR_SHAPE_MISMATCH");
+  Status s(StatusCode::INVALID_ARGUMENT, "bad lda", "Forward");
+  EXPECT_TRUE(s.IsError() && !s);
+  EXPECT_TRUE(s.ToString().find("INVALID_ARGUMENT") != std::string::npos);
+}
+
+TEST_HOST(BlasPluginManagerRegistersEveryOperatorName) {
+  RegisterBlasJITPlugins();
+  for (const char* n : {"gemm", "Gemm", "gemv", "Gemv", "gemm_batched", "GemmBatched", "batched_gemm",
+                        "BatchedGemm", "dot", "Dot", "axpy", "nrm2", "iamax", "Iamin", "rot", "swap", "scal",
+                        "copy", "asum"})
+    EXPECT_TRUE(IsBlasOperatorSupported(n));
+  EXPECT_TRUE(!IsBlasOperatorSupported("trsm_not_here"));
+  auto p = CreateBlasJITPlugin("gemm_batched");
+  EXPECT_TRUE(p != nullptr);
+  if (p) EXPECT_TRUE(p->GetPluginName() == "gemm_batched_jit");
+  auto v = CreateBlasJITPlugin("Iamax");
+  auto* vp = dynamic_cast<VectorOpsJITPlugin*>(v.get());
+  EXPECT_TRUE(vp && vp->GetOperationType() == VectorOpType::IAMAX);
+  EXPECT_TRUE(CreateBlasJITPlugin("unknown") == nullptr);
+}
+
+TEST_HOST(PluginRegistrarKnowsJitWrapperKeys) {
+  auto& r = PluginRegistrar::Instance();
+  for (const char* k : {"gemm", "gemm_jit", "gemv", "gemv_jit", "gemm_batched", "gemm_batched_jit", "vector_ops"})
+    EXPECT_TRUE(r.CreatePlugin(k) != nullptr);
+  EXPECT_TRUE(r.IsOperatorSupported("Gemm") && r.IsOperatorSupported("dot"));
+}
+
+TEST_HOST(CompileRequiresInitializeAndKnownKernelType) {
+  GemmJITPlugin p;
+  EXPECT_TRUE(p.Compile(JITConfig()) == StatusCode::NOT_INITIALIZED);
+  std::vector<Tensor<float>> in, out;
+  EXPECT_TRUE(p.Execute(in, out) == StatusCode::NOT_COMPILED);
+}
+
+TEST_HOST(MemoryPoolSizeClasses) {
+  EXPECT_EQ(CudaMemoryPool::SizeClass(1), 256u);
+  EXPECT_EQ(CudaMemoryPool::SizeClass(257), 512u);
+  EXPECT_EQ(CudaMemoryPool::SizeClass(1 << 20), 1u << 20);
+  EXPECT_EQ(CudaMemoryPool::SizeClass((1 << 20) + 1), 2u << 20);
+  EXPECT_EQ(CudaMemoryPool::SizeClass((5u << 20) + 3), 6u << 20);
+}
+
+TEST_HOST(OperatorConfigPersistence) {
+  auto& g = GlobalJITManager::Instance();
+  JITConfig c;
+  c.kernel_type = "tcgen05";
+  c.tile_size = 256;
+  c.num_stages = 4;
+  g.SetOperatorConfig("gemm", c);
+  g.SaveCacheToFile("/tmp/cuopx_opcfg.txt");
+  g.Cleanup();
+  EXPECT_TRUE(g.GetOperatorConfig("gemm").kernel_type == "default");
+  g.LoadCacheFromFile("/tmp/cuopx_opcfg.txt");
+  EXPECT_TRUE(g.GetOperatorConfig("gemm").kernel_type == "tcgen05");
+  EXPECT_EQ(g.GetOperatorConfig("gemm").num_stages, 4);
+}
+
+// ------------------------------------------------------------------ GPU: reference known answers
+TEST_GPU(GemmForwardFloatNoTranspose) {  // test/cuBlas/test_gemm/test_gemm.cpp:19-43
+  float h_input[6] = {1, 2, 3, 4, 5, 6};
+  float h_weight[12] = {1, 0, 0, 0, 0, 1, 0, 0, 0, 0, 1, 0};
+  Tensor<float> input({2, 3}), weight({3, 4}), output({2, 4});
+  input.copy_from_host(h_input);
+  weight.copy_from_host(h_weight);
+  output.zero();
+  Gemm<float> gemm(false, false, 1.0f, 0.0f);
+  gemm.SetWeight(weight);
+  EXPECT_TRUE(gemm.Forward(input, output) == StatusCode::SUCCESS);
+  const float expected[8] = {1, 2, 3, 0, 4, 5, 6, 0};
+  auto h = to_host(output);
+  for (int i = 0; i < 8; ++i) EXPECT_NEAR(h[i], expected[i], 1e-5);
+}
+
+TEST_GPU(GemvForwardFloatNoTranspose) {  // test/cuBlas/test_gemv/test_gemv.cpp:19-44
+  float h_input[6] = {1, 2, 3, 4, 5, 6}, h_weight[3] = {1, 2, 3};
+  Tensor<float> input({2, 3}), weight({3}), output({2});
+  input.copy_from_host(h_input);
+  weight.copy_from_host(h_weight);
+  output.zero();
+  Gemv<float> gemv(false, 1.0f, 0.0f);
+  gemv.SetWeight(weight);
+  EXPECT_TRUE(gemv.Forward(input, output) == StatusCode::SUCCESS);
+  auto h = to_host(output);
+  EXPECT_NEAR(h[0], 14, 1e-5);
+  EXPECT_NEAR(h[1], 32, 1e-5);
+}
+
+TEST_GPU(MatMulForward2DAndBatch3D) {  // test/cuDNN/test_matmul/test_matmul.cpp:21-67
+  float h_A[6] = {1, 2, 3, 4, 5, 6}, h_B[12] = {1, 0, 0, 0, 0, 1, 0, 0, 0, 0, 1, 0};
+  Tensor<float> A({2, 3}), B({3, 4}), C({2, 4});
+  A.copy_from_host(h_A);
+  B.copy_from_host(h_B);
+  MatMul<float> mm;
+  EXPECT_TRUE(mm.Forward(A, B, C, -1) == StatusCode::SUCCESS);
+  const float e2[8] = {1, 2, 3, 0, 4, 5, 6, 0};
+  auto h = to_host(C);
+  for (int i = 0; i < 8; ++i) EXPECT_NEAR(h[i], e2[i], 1e-5);
+
+  float h_A3[12] = {1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12};
+  float h_B3[24] = {1, 0, 0, 0, 0, 1, 0, 0, 0, 0, 1, 0, 2, 0, 0, 0, 0, 2, 0, 0, 0, 0, 2, 0};
+  Tensor<float> A3({2, 2, 3}), B3({2, 3, 4}), C3;
+  A3.copy_from_host(h_A3);
+  B3.copy_from_host(h_B3);
+  EXPECT_TRUE(mm.Forward(A3, B3, C3, -1) == StatusCode::SUCCESS);
+  const float e3[16] = {1, 2, 3, 0, 4, 5, 6, 0, 14, 16, 18, 0, 20, 22, 24, 0};
+  auto h3 = to_host(C3);
+  EXPECT_EQ(h3.size(), 16u);
+  for (int i = 0; i < 16 && i < (int)h3.size(); ++i) EXPECT_NEAR(h3[i], e3[i], 1e-5);
+
+  BatchMatMul<float> bmm;
+  Tensor<float> C4;
+  EXPECT_TRUE(bmm.Forward(A3, B3, C4, 0) == StatusCode::SUCCESS);
+  auto h4 = to_host(C4);
+  for (int i = 0; i < 16 && i < (int)h4.size(); ++i) EXPECT_NEAR(h4[i], e3[i], 1e-5);
+  Tensor<float> dummy;
+  EXPECT_TRUE(bmm.Forward(A3, dummy) == StatusCode::UNSUPPORTED_TYPE);
+}
+
+TEST_GPU(ShapeMismatchIsReported) {
+  Tensor<float> A({4, 5}), W({6, 7}), C({4, 7});
+  Gemm<float> g;
+  g.SetWeight(W);
+  EXPECT_TRUE(g.Forward(A, C) == StatusCode::SHAPE_MISMATCH);
+  Gemv<float> v;
+  Tensor<float> x({3}), y({4});
+  v.SetWeight(x);
+  EXPECT_TRUE(v.Forward(A, y) == StatusCode::SHAPE_MISMATCH);
+}
+
+// ------------------------------------------------------------------ GPU: seeded parity vs oracle
+TEST_GPU(GemmSeededMatchesOracleBitExact) {
+  for (int t = 0; t < 4; ++t) {
+    const bool tA = t & 1, tB = t & 2;
+    const int M = 257, N = 129, K = 300;
+    std::vector<float> a(size_t(M) * K), w(size_t(K) * N), c0(size_t(M) * N), ref;
+    oracle_fill_uniform_f32(a.data(), a.size(), 11, -1.f, 1.f);
+    oracle_fill_uniform_f32(w.data(), w.size(), 12, -1.f, 1.f);
+    oracle_fill_uniform_f32(c0.data(), c0.size(), 13, -1.f, 1.f);
+    ref = c0;
+    oracle_gemm_f32(tA, tB, M, N, K, 0.5f, a.data(), tA ? M : K, w.data(), tB ? K : N, 1.5f, ref.data(), N, 4);
+    Tensor<float> A(tA ? std::vector<size_t>{size_t(K), size_t(M)} : std::vector<size_t>{size_t(M), size_t(K)});
+    Tensor<float> W(tB ? std::vector<size_t>{size_t(N), size_t(K)} : std::vector<size_t>{size_t(K), size_t(N)});
+    Tensor<float> C({size_t(M), size_t(N)});
+    A.copy_from_host(a.data());
+    W.copy_from_host(w.data());
+    C.copy_from_host(c0.data());
+    Gemm<float> g(tA, tB, 0.5f, 1.5f);
+    g.SetWeight(W);
+    EXPECT_TRUE(g.Forward(A, C) == StatusCode::SUCCESS);
+    auto h = to_host(C);
+    EXPECT_TRUE(std::memcmp(h.data(), ref.data(), h.size() * sizeof(float)) == 0);
+  }
+}
+
+TEST_GPU(GemvSeededMatchesOracle) {
+  for (int trans = 0; trans < 2; ++trans) {
+    const int m = 4096, n = 3072;
+    std::vector<float> a(size_t(m) * n), x(n), y(m, 0.f);
+    oracle_fill_uniform_f32(a.data(), a.size(), 21, -1.f, 1.f);
+    oracle_fill_uniform_f32(x.data(), n, 22, -1.f, 1.f);
+    // Tensor shape [m, n]; transposed reads A[col*m + row] (n rows of m)
+    oracle_gemv_f32(trans, m, n, 1.f, a.data(), trans ? m : n, x.data(), 0.f, y.data(), 4);
+    Tensor<float> A({size_t(m), size_t(n)}), X({size_t(n)}), Y({size_t(m)});
+    A.copy_from_host(a.data());
+    X.copy_from_host(x.data());
+    Gemv<float> g(trans != 0, 1.f, 0.f);
+    g.SetWeight(X);
+    EXPECT_TRUE(g.Forward(A, Y) == StatusCode::SUCCESS);
+    EXPECT_TRUE(rel_frobenius(to_host(Y), y) <= 1e-5 * std::sqrt(double(n)));
+  }
+}
+
+TEST_GPU(Bf16GemmAndBatchedRunOnTensorCores) {
+  const int M = 256, N = 384, K = 192, batch = 3;
+  std::vector<float> a(size_t(batch) * M * K), b(size_t(batch) * K * N);
+  oracle_fill_uniform_f32(a.data(), a.size(), 31, -1.f, 1.f);
+  oracle_fill_uniform_f32(b.data(), b.size(), 32, -1.f, 1.f);
+  std::vector<__nv_bfloat16> ah(a.size()), bh(b.size());
+  for (size_t i = 0; i < a.size(); ++i) ah[i] = __float2bfloat16(a[i]);
+  for (size_t i = 0; i < b.size(); ++i) bh[i] = __float2bfloat16(b[i]);
+  Tensor<__nv_bfloat16> A({size_t(batch), size_t(M), size_t(K)}), B({size_t(batch), size_t(K), size_t(N)});
+  Tensor<__nv_bfloat16> C({size_t(batch), size_t(M), size_t(N)});
+  A.copy_from_host(ah.data());
+  B.copy_from_host(bh.data());
+  GemmBatched<__nv_bfloat16> gb;
+  EXPECT_TRUE(gb.Forward(A, B, C) == StatusCode::SUCCESS);
+  EXPECT_TRUE(std::string(cuopx_last_kernel()).rfind("gemm_tc_", 0) == 0);
+  auto h = to_host(C);
+  // fp32 reference of the widened inputs, batch 1
+  double maxref = 0, maxerr = 0;
+  for (int i = 0; i < M; ++i)
+    for (int j = 0; j < N; ++j) {
+      double s = 0;
+      for (int k = 0; k < K; ++k)
+        s += double(__bfloat162float(ah[size_t(M) * K + size_t(i) * K + k])) *
+             double(__bfloat162float(bh[size_t(K) * N + size_t(k) * N + j]));
+      maxref = std::max(maxref, std::fabs(s));
+      maxerr = std::max(maxerr, std::fabs(s - double(__bfloat162float(h[size_t(M) * N + size_t(i) * N + j]))));
+    }
+  EXPECT_TRUE(maxerr / maxref <= 1e-2);
+}
+
+// ------------------------------------------------------------------ GPU: plugins and wrapper
+TEST_GPU(GemmPluginExecute) {
+  auto plugin = CreateBlasJITPlugin("gemm");
+  auto* g = dynamic_cast<GemmJITPlugin*>(plugin.get());
+  EXPECT_TRUE(g != nullptr);
+  if (!g) return;
+  EXPECT_TRUE(g->Initialize() == StatusCode::SUCCESS);
+  JITConfig cfg;
+  cfg.kernel_type = "tensor_core";
+  EXPECT_TRUE(g->Compile(cfg) == StatusCode::SUCCESS);
+  float h_input[6] = {1, 2, 3, 4, 5, 6}, h_weight[12] = {1, 0, 0, 0, 0, 1, 0, 0, 0, 0, 1, 0};
+  Tensor<float> W({3, 4});
+  W.copy_from_host(h_weight);
+  g->SetGemmParams(false, false, 2.0f, 0.0f);
+  g->SetWeight(W);
+  std::vector<Tensor<float>> in, out;
+  in.emplace_back(std::vector<size_t>{2, 3});
+  in[0].copy_from_host(h_input);
+  out.emplace_back();  // empty: the plugin allocates [2, 4]
+  EXPECT_TRUE(g->Execute(in, out) == StatusCode::SUCCESS);
+  const float expected[8] = {2, 4, 6, 0, 8, 10, 12, 0};
+  auto h = to_host(out[0]);
+  for (int i = 0; i < 8; ++i) EXPECT_NEAR(h[i], expected[i], 1e-5);
+  EXPECT_TRUE(!g->GetPerformanceProfile().kernel_name.empty());
+}
+
+TEST_GPU(BatchedAndGemvAndVectorPlugins) {
+  // batched: 2 x (2x3 * 3x4) with the known-answer data, registered under "gemm_batched"
+  auto pb = CreateBlasJITPlugin("gemm_batched");
+  auto* b = dynamic_cast<GemmBatchedJITPlugin*>(pb.get());
+  EXPECT_TRUE(b && b->Initialize() == StatusCode::SUCCESS && b->Compile(JITConfig()) == StatusCode::SUCCESS);
+  float h_A[12] = {1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12};
+  float h_B[24] = {1, 0, 0, 0, 0, 1, 0, 0, 0, 0, 1, 0, 2, 0, 0, 0, 0, 2, 0, 0, 0, 0, 2, 0};
+  std::vector<Tensor<float>> in, out;
+  in.emplace_back(std::vector<size_t>{2, 2, 3});
+  in.emplace_back(std::vector<size_t>{2, 3, 4});
+  in[0].copy_from_host(h_A);
+  in[1].copy_from_host(h_B);
+  out.emplace_back(std::vector<size_t>{2, 2, 4});
+  b->SetBatchSize(2);
+  b->SetMatrixDimensions(2, 4, 3);
+  EXPECT_TRUE(b->Execute(in, out) == StatusCode::SUCCESS);
+  const float e3[16] = {1, 2, 3, 0, 4, 5, 6, 0, 14, 16, 18, 0, 20, 22, 24, 0};
+  auto h = to_host(out[0]);
+  for (int i = 0; i < 16; ++i) EXPECT_NEAR(h[i], e3[i], 1e-5);
+
+  // gemv plugin: weight = A [2,3], input x, output y
+  auto pv = CreateBlasJITPlugin("Gemv");
+  auto* v = dynamic_cast<GemvJITPlugin*>(pv.get());
+  EXPECT_TRUE(v && v->Initialize() == StatusCode::SUCCESS && v->Compile(JITConfig()) == StatusCode::SUCCESS);
+  Tensor<float> A({2, 3});
+  A.copy_from_host(h_A);
+  v->SetWeight(A);
+  std::vector<Tensor<float>> vin, vout;
+  vin.emplace_back(std::vector<size_t>{3});
+  float x[3] = {1, 2, 3};
+  vin[0].copy_from_host(x);
+  vout.emplace_back(std::vector<size_t>{2});
+  EXPECT_TRUE(v->Execute(vin, vout) == StatusCode::SUCCESS);
+  auto hy = to_host(vout[0]);
+  EXPECT_NEAR(hy[0], 14, 1e-5);
+  EXPECT_NEAR(hy[1], 32, 1e-5);
+
+  // vector ops: dot, nrm2, iamax (1-based), axpy
+  auto pd = CreateBlasJITPlugin("dot");
+  auto* d = dynamic_cast<VectorOpsJITPlugin*>(pd.get());
+  EXPECT_TRUE(d && d->Initialize() == StatusCode::SUCCESS && d->Compile(JITConfig()) == StatusCode::SUCCESS);
+  float hx[4] = {1, -7, 3, 2}, hy2[4] = {2, 1, 0, 1};
+  std::vector<Tensor<float>> din, dout;
+  din.emplace_back(std::vector<size_t>{4});
+  din.emplace_back(std::vector<size_t>{4});
+  din[0].copy_from_host(hx);
+  din[1].copy_from_host(hy2);
+  dout.emplace_back();
+  EXPECT_TRUE(d->Execute(din, dout) == StatusCode::SUCCESS);
+  EXPECT_NEAR(to_host(dout[0])[0], 2 - 7 + 0 + 2, 1e-6);
+  d->SetOperationType(VectorOpType::NRM2);
+  EXPECT_TRUE(d->Execute(din, dout) == StatusCode::SUCCESS);
+  EXPECT_NEAR(to_host(dout[0])[0], std::sqrt(1 + 49 + 9 + 4.0), 1e-5);
+  d->SetOperationType(VectorOpType::IAMAX);
+  EXPECT_TRUE(d->Execute(din, dout) == StatusCode::SUCCESS);
+  EXPECT_NEAR(to_host(dout[0])[0], 2, 0);
+  d->SetOperationType(VectorOpType::AXPY);
+  d->SetAlpha(2.f);
+  std::vector<Tensor<float>> ain, aout;
+  ain.emplace_back(din[0].data(), din[0].shape());
+  aout.emplace_back(din[1].data(), din[1].shape());
+  EXPECT_TRUE(d->Execute(ain, aout) == StatusCode::SUCCESS);
+  auto ha = to_host(din[1]);
+  for (int i = 0; i < 4; ++i) EXPECT_NEAR(ha[i], 2 * hx[i] + hy2[i], 1e-6);
+}
+
+TEST_GPU(JitWrapperRoutesGemmThroughPlugin) {
+  // test/JIT_test/test_jit_system.cpp:99-141 style: original vs wrapper on the same inputs
+  const int n = 512;
+  std::vector<float> a(size_t(n) * n), w(size_t(n) * n);
+  oracle_fill_uniform_f32(a.data(), a.size(), 41, -1.f, 1.f);
+  oracle_fill_uniform_f32(w.data(), w.size(), 42, -1.f, 1.f);
+  Tensor<float> A({size_t(n), size_t(n)}), W({size_t(n), size_t(n)}), C1({size_t(n), size_t(n)}),
+      C2({size_t(n), size_t(n)});
+  A.copy_from_host(a.data());
+  W.copy_from_host(w.data());
+  Gemm<float> g(false, false, 1.f, 0.f);
+  g.SetWeight(W);
+  EXPECT_TRUE(g.Forward(A, C1) == StatusCode::SUCCESS);
+  JITWrapper<Gemm<float>> wrapped(std::move(g));
+  wrapped.EnableJIT(true);
+  EXPECT_TRUE(wrapped.IsJITCompiled());
+  EXPECT_TRUE(wrapped(A, C2) == StatusCode::SUCCESS);
+  EXPECT_TRUE(!wrapped.GetPerformanceProfile().kernel_name.empty());  // the plugin ran, not the fallback
+  auto h1 = to_host(C1), h2 = to_host(C2);
+  EXPECT_TRUE(std::memcmp(h1.data(), h2.data(), h1.size() * sizeof(float)) == 0);
+}
+
+TEST_GPU(MemoryPoolReusesAndLimits) {
+  auto& pool = CudaMemoryPool::Instance();
+  pool.ResetStats();
+  void* p = pool.Alloc(3000);
+  EXPECT_TRUE(p != nullptr);
+  pool.Free(p, 3000);
+  void* q = pool.Alloc(4000);  // same 4 KiB class, same stream: cached block comes back
+  EXPECT_TRUE(q == p);
+  EXPECT_TRUE(pool.GetStats().cache_hits >= 1);
+  pool.Free(q, 4000);
+  const auto reserved = pool.GetStats().bytes_reserved;
+  pool.SetMemoryLimit(reserved + (1 << 20));
+  EXPECT_TRUE(pool.Alloc(size_t(64) << 20) == nullptr);  // over the limit: refused on the host
+  EXPECT_TRUE(pool.GetStats().failed_allocs >= 1);
+  bool threw = false;
+  try {
+    Tensor<float> big({size_t(32) << 20});
+  } catch (const std::runtime_error&) {
+    threw = true;
+  }
+  EXPECT_TRUE(threw);
+  pool.SetMemoryLimit(0);
+  Tensor<float> ok({size_t(32) << 20});
+  EXPECT_TRUE(ok.data() != nullptr);
+}
+
+int main(int argc, char** argv) {
+  bool host_only = false;
+  std::string filter;
+  for (int i = 1; i < argc; ++i) {
+    if (std::string(argv[i]) == "--host-only") host_only = true;
+    else filter = argv[i];
+  }
+  int run = 0;
+  for (auto& t : registry()) {
+    if (host_only && t.needs_gpu) continue;
+    if (!filter.empty() && std::string(t.name).find(filter) == std::string::npos) continue;
+    const int before = g_failures;
+    std::printf("[ RUN  ] %s\n", t.name);
+    t.fn();
+    std::printf("[ %s ] %s\n", g_failures == before ? " OK " : "FAIL", t.name);
+    ++run;
+  }
+  if (!host_only) {
+    int code = 0;
+    if (cuopx_get_device_error(&code) != 0 || code != 0) {
+      std::printf("device error word: %d\n", code);
+      ++g_failures;
+    }
+  }
+  std::printf("%d tests, %d failures\n", run, g_failures);
+  return g_failures == 0 && run > 0 ? 0 : 1;
+}
