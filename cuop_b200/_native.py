@@ -32,6 +32,7 @@ STATUS_NAMES = {
 }
 
 F32, F64, F16, BF16 = 0, 1, 2, 3
+FP32_AUTO, FP32_FFMA, FP32_TF32X3 = 0, 1, 2
 
 _i64, _dbl, _vp, _sz, _int = C.c_int64, C.c_double, C.c_void_p, C.c_size_t, C.c_int
 _fp = C.c_void_p  # float* as raw address
@@ -39,6 +40,8 @@ _fp = C.c_void_p  # float* as raw address
 # (name, restype, argtypes) for every symbol in include/cuopx.h
 SIGNATURES = [
     ("cuopx_version", _int, []),
+    ("cuopx_set_fp32_gemm_mode", _int, [_int]),
+    ("cuopx_get_fp32_gemm_mode", _int, []),
     ("cuopx_last_kernel", C.c_char_p, []),
     ("cuopx_launch_count", _i64, []),
     ("cuopx_get_device_error", _int, [C.POINTER(_int)]),

@@ -53,10 +53,18 @@ int vector_elementwise(int op, int64_t n, float alpha, const float* x, int64_t i
 // Minimum problem size (M*N*K) for the tcgen05 path; below it the SIMT
 // kernel finishes before a persistent TMA pipeline has filled.
 constexpr double kTcMinWork = 64.0 * 64.0 * 64.0;
+// fp32 problems at least this large go to 3xTF32 on the tensor cores
+// (unless the FFMA mode is selected).
+constexpr double kTf32x3MinWork = 256.0 * 256.0 * 256.0;
+std::atomic<int> g_fp32_mode{CUOPX_FP32_AUTO};
 
 int gemm_route(const GemmProblem& p, cudaStream_t stream) {
   const double work = static_cast<double>(p.M) * p.N * p.K * p.batch;
   if (p.K > 0 && work >= kTcMinWork && gemm_tc_supported(p)) return gemm_tc(p, stream);
+  const int mode = g_fp32_mode.load(std::memory_order_relaxed);
+  if (p.K > 0 && ((mode == CUOPX_FP32_AUTO && work >= kTf32x3MinWork) || mode == CUOPX_FP32_TF32X3) &&
+      gemm_tf32x3_supported(p))
+    return gemm_tf32x3(p, stream);
   if (p.K > 0 && gemm_simt_f32_supported(p)) return gemm_simt_f32(p, stream);
   return gemm_simt_generic(p, stream);
 }
@@ -94,6 +102,15 @@ using namespace cuopx;
 extern "C" {
 
 int cuopx_version(void) { return 100; }
+
+int cuopx_set_fp32_gemm_mode(int mode) {
+  if (mode != CUOPX_FP32_AUTO && mode != CUOPX_FP32_FFMA && mode != CUOPX_FP32_TF32X3)
+    return CUOPX_INVALID_ARGUMENT;
+  g_fp32_mode.store(mode);
+  return CUOPX_SUCCESS;
+}
+
+int cuopx_get_fp32_gemm_mode(void) { return g_fp32_mode.load(); }
 
 const char* cuopx_last_kernel(void) { return t_last_kernel; }
 

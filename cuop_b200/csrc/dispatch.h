@@ -51,6 +51,10 @@ int gemm_simt_f32(const GemmProblem& p, cudaStream_t stream);
 bool gemm_tc_supported(const GemmProblem& p);
 int gemm_tc(const GemmProblem& p, cudaStream_t stream);
 
+// 3xTF32 tcgen05 back-end (gemm_tf32x3.cu) for fp32.
+bool gemm_tf32x3_supported(const GemmProblem& p);
+int gemm_tf32x3(const GemmProblem& p, cudaStream_t stream);
+
 // Column-block gather (vector_ops.cu).
 int gather_column_blocks(int dtype, int64_t G, int64_t M, int64_t Nb, const void* blocks, void* out, int64_t ldo,
                          cudaStream_t stream);

@@ -348,22 +348,29 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
-// 3-D tiled map over a row-major [batch][rows][inner] 16-bit tensor with
-// row stride `ld` and batch stride `bstride` (elements), 128-byte swizzle.
-bool make_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base, int64_t inner, int64_t rows,
-              int64_t batch, int64_t ld, int64_t bstride, int box_inner, int box_rows) {
+// 3-D tiled map over a row-major [batch][rows][inner] tensor of `es`-byte
+// elements with row stride `ld` and batch stride `bstride` (elements),
+// 128-byte swizzle.
+bool make_map_es(CUtensorMap* map, CUtensorMapDataType dt, int es, const void* base, int64_t inner, int64_t rows,
+                 int64_t batch, int64_t ld, int64_t bstride, int box_inner, int box_rows,
+                 CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto enc = get_encode_fn();
   if (!enc) return false;
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows),
                         static_cast<cuuint64_t>(batch)};
-  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld * 2),
-                           static_cast<cuuint64_t>((batch > 1 ? bstride : ld * rows) * 2)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld * es),
+                           static_cast<cuuint64_t>((batch > 1 ? bstride : ld * rows) * es)};
   cuuint32_t box[3] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_rows), 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+bool make_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base, int64_t inner, int64_t rows,
+              int64_t batch, int64_t ld, int64_t bstride, int box_inner, int box_rows) {
+  return make_map_es(map, dt, 2, base, inner, rows, batch, ld, bstride, box_inner, box_rows);
 }
 
 template <typename T, int BN, int STAGES, bool A_MN, bool B_MN>

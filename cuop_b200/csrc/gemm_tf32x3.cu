@@ -1,0 +1,432 @@
+// fp32 GEMM on the tensor cores with 3xTF32 (tcgen05.mma kind::tf32).
+//
+// Each fp32 operand x is split in shared memory into hi = tf32(x) (round to
+// nearest) and lo = x - hi (exact in fp32, read by the MMA as tf32), and the
+// product is accumulated in fp32 TMEM as hi*hi + hi*lo + lo*hi.  The dropped
+// lo*lo term and the tf32 truncation of lo bound the per-product error near
+// 2^-21 relative, far inside the fp32 path's ||C-R||_F/||R||_F <= 1e-5*sqrt(K);
+// there is no silent single-pass TF32.  Summation order differs from the
+// reference's FFMA chain (gemm.cu:14-42), so results match within that
+// tolerance, not bit for bit (the FFMA kernels in gemm_simt.cu are exact).
+//
+// One persistent CTA per SM, 10 warps:
+//   warp 0      TMA producer: fp32 A (128 x 32) and B (BN x 32) tiles into the
+//               "hi" buffers of a STAGES-deep ring: 128-byte swizzle for
+//               K-major operands, 128-byte swizzle with 32-byte atoms for
+//               MN-major ones (the only MN-major layout tf32 MMAs accept).
+//   warps 6..9  converters: wait for a landed stage, rewrite hi in place and
+//               write lo next to it (same swizzled layout: the split is
+//               elementwise), fence the async proxy, signal the MMA warp.
+//   warp 1      TMEM allocator + MMA issuer: 3 x (BK/8) MMAs (M=128, N=BN,
+//               K=8) per stage, commit frees the stage / hands off the tile.
+//   warps 2..5  epilogue: tcgen05.ld, alpha/beta, swizzled staging, TMA store.
+// No TMA multicast.
+#include "common.cuh"
+#include "dispatch.h"
+
+namespace cuopx {
+
+namespace {
+
+constexpr int X3_BM = 128;
+constexpr int X3_BK = 32;  // 32 fp32 = 128 bytes = one swizzle row
+constexpr int X3_THREADS = 320;
+constexpr int X3_EPI_WARPS = 4;
+constexpr int X3_CONV_WARPS = 4;
+constexpr int X3_CHUNK = 32;  // epilogue columns per TMA store (32 fp32 = 128 bytes)
+
+struct X3Params {
+  int M, N, K, batch;
+  int tiles_m, tiles_n, num_tiles, k_blocks;
+  float alpha, beta;
+  const float* C_in;
+  int64_t ldc, strideC;
+};
+
+template <int BN, int STAGES>
+struct X3Smem {
+  static constexpr int A_BYTES = X3_BM * X3_BK * 4;  // 16 KB
+  static constexpr int B_BYTES = BN * X3_BK * 4;
+  static constexpr int STAGE = 2 * (A_BYTES + B_BYTES);  // A_hi, A_lo, B_hi, B_lo
+  static constexpr int C_STAGE = 32 * X3_CHUNK * 4;       // 4 KB
+  static constexpr int OFF_C = STAGES * STAGE;
+  static constexpr int OFF_BAR = OFF_C + X3_EPI_WARPS * 2 * C_STAGE;
+  // full[S], conv[S], empty[S], acc_full[2], acc_empty[2], drain
+  static constexpr int NUM_BARS = 3 * STAGES + 5;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr int ALLOC = OFF_MISC + 16 + 1024;
+  static_assert(ALLOC <= 232448, "shared memory budget exceeded");
+  static constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulator buffers
+  static_assert(TMEM_COLS == 128 || TMEM_COLS == 256, "TMEM allocation must be a power of two >= 32");
+  __device__ static unsigned char* a_hi(unsigned char* s, int st) { return s + st * STAGE; }
+  __device__ static unsigned char* a_lo(unsigned char* s, int st) { return s + st * STAGE + A_BYTES; }
+  __device__ static unsigned char* b_hi(unsigned char* s, int st) { return s + st * STAGE + 2 * A_BYTES; }
+  __device__ static unsigned char* b_lo(unsigned char* s, int st) { return s + st * STAGE + 2 * A_BYTES + B_BYTES; }
+};
+
+__device__ __forceinline__ void x3_tile_coords(int t, const X3Params& p, int& b, int& mt, int& nt) {
+  constexpr int G = 8;
+  const int per_batch = p.tiles_m * p.tiles_n;
+  b = t / per_batch;
+  const int r = t - b * per_batch;
+  const int span = G * p.tiles_n;
+  const int g = r / span;
+  const int first_m = g * G;
+  const int gsize = min(G, p.tiles_m - first_m);
+  const int rr = r - g * span;
+  mt = first_m + rr % gsize;
+  nt = rr / gsize;
+}
+
+__device__ __forceinline__ uint32_t to_tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+// hi/lo split of `bytes` bytes at `hi` (in place) and `lo`, by `nthreads` threads.
+__device__ __forceinline__ void split_tf32(unsigned char* hi, unsigned char* lo, int bytes, int tid, int nthreads) {
+  for (int off = tid * 16; off < bytes; off += nthreads * 16) {
+    float4 v = *reinterpret_cast<const float4*>(hi + off);
+    float4 h, l;
+    h.x = __uint_as_float(to_tf32_rna(v.x));
+    h.y = __uint_as_float(to_tf32_rna(v.y));
+    h.z = __uint_as_float(to_tf32_rna(v.z));
+    h.w = __uint_as_float(to_tf32_rna(v.w));
+    l.x = __fsub_rn(v.x, h.x);
+    l.y = __fsub_rn(v.y, h.y);
+    l.z = __fsub_rn(v.z, h.z);
+    l.w = __fsub_rn(v.w, h.w);
+    *reinterpret_cast<float4*>(hi + off) = h;
+    *reinterpret_cast<float4*>(lo + off) = l;
+  }
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(X3_THREADS, 1)
+    gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                       const __grid_constant__ CUtensorMap tmC, const X3Params p) {
+  using L = X3Smem<BN, STAGES>;
+  constexpr uint32_t STAGE_TX = static_cast<uint32_t>(L::A_BYTES + L::B_BYTES);
+  constexpr uint32_t IDESC = make_idesc(2u /*tf32*/, A_MN, B_MN, X3_BM, BN);
+  constexpr uint32_t CHUNK_BYTES = 32 * X3_BK * 4;  // one 32 x 32 fp32 box = 4 KB
+
+  extern __shared__ __align__(1024) unsigned char x3_smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(x3_smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* full = bars;
+  uint64_t* conv = bars + STAGES;
+  uint64_t* empty = bars + 2 * STAGES;
+  uint64_t* acc_full = bars + 3 * STAGES;
+  uint64_t* acc_empty = bars + 3 * STAGES + 2;
+  uint64_t* drain = bars + 3 * STAGES + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&conv[s], X3_CONV_WARPS);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], X3_EPI_WARPS);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    prefetch_tmap(&tmC);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, L::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool issued_any[STAGES];
+      uint32_t last_phase[STAGES];
+      for (int s = 0; s < STAGES; ++s) issued_any[s] = false, last_phase[s] = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        int b, mt, nt;
+        x3_tile_coords(t, p, b, mt, nt);
+        const int m0 = mt * X3_BM, n0 = nt * BN;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, kDevErrWaitTimeoutEmpty, abort_flag)) {
+            ok = false;
+            break;
+          }
+          unsigned char* sa = L::a_hi(smem, stage);
+          unsigned char* sb = L::b_hi(smem, stage);
+          mbar_arrive_expect_tx(&full[stage], STAGE_TX);
+          const int k0 = kb * X3_BK;
+          if constexpr (A_MN) {
+#pragma unroll
+            for (int j = 0; j < X3_BM / 32; ++j)
+              tma_load_3d(sa + j * CHUNK_BYTES, &tmA, &full[stage], m0 + 32 * j, k0, b);
+          } else {
+            tma_load_3d(sa, &tmA, &full[stage], k0, m0, b);
+          }
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 32; ++j)
+              tma_load_3d(sb + j * CHUNK_BYTES, &tmB, &full[stage], n0 + 32 * j, k0, b);
+          } else {
+            tma_load_3d(sb, &tmB, &full[stage], k0, n0, b);
+          }
+          issued_any[stage] = true;
+          last_phase[stage] = phase;
+          if (++stage == STAGES) stage = 0, phase ^= 1u;
+        }
+      }
+      if (!ok) {
+        for (int s = 0; s < STAGES; ++s) {
+          if (!issued_any[s]) continue;
+          const uint32_t addr = smem_u32(&full[s]);
+          const unsigned long long t0 = global_timer_ns();
+          while (!mbar_try_wait(addr, last_phase[s])) {
+            if (global_timer_ns() - t0 > kWaitLimitNs) {
+              record_device_error(kDevErrAbortDrain);
+              break;
+            }
+          }
+        }
+      }
+    }
+  } else if (warp >= 6) {
+    // ------------------------------------------------------------ converters
+    const int ctid = threadIdx.x - 6 * 32;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      for (int kb = 0; kb < p.k_blocks; ++kb) {
+        if (!mbar_wait_bounded(&full[stage], phase, kDevErrWaitTimeoutFull, abort_flag)) {
+          ok = false;
+          break;
+        }
+        split_tf32(L::a_hi(smem, stage), L::a_lo(smem, stage), L::A_BYTES, ctid, X3_CONV_WARPS * 32);
+        split_tf32(L::b_hi(smem, stage), L::b_lo(smem, stage), L::B_BYTES, ctid, X3_CONV_WARPS * 32);
+        fence_proxy_async_shared();  // generic-proxy writes -> visible to the tensor cores
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv[stage]);
+        if (++stage == STAGES) stage = 0, phase ^= 1u;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true, issued = false;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1u, kDevErrWaitTimeoutAccEmpty, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after_sync();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait_bounded(&conv[stage], phase, kDevErrWaitTimeoutFull, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after_sync();
+          const uint32_t ah = smem_u32(L::a_hi(smem, stage)), al = smem_u32(L::a_lo(smem, stage));
+          const uint32_t bh = smem_u32(L::b_hi(smem, stage)), bl = smem_u32(L::b_lo(smem, stage));
+#pragma unroll
+          for (int kk = 0; kk < X3_BK / 8; ++kk) {
+            // K=8 per MMA: K-major advances 32 bytes in the swizzled row;
+            // MN-major advances one 8-row group = 1024 bytes.
+            const uint32_t ao = A_MN ? kk * 1024 : kk * 32, bo = B_MN ? kk * 1024 : kk * 32;
+            // MN-major tf32 operands use the 32-byte-atom swizzle: 4-row
+            // (512-byte) atoms, 32-element chunks CHUNK_BYTES apart.
+            const uint64_t dah = A_MN ? make_smem_desc_sw128_32b(ah + ao, CHUNK_BYTES, 512)
+                                      : make_smem_desc_sw128(ah + ao, 16, 1024);
+            const uint64_t dal = A_MN ? make_smem_desc_sw128_32b(al + ao, CHUNK_BYTES, 512)
+                                      : make_smem_desc_sw128(al + ao, 16, 1024);
+            const uint64_t dbh = B_MN ? make_smem_desc_sw128_32b(bh + bo, CHUNK_BYTES, 512)
+                                      : make_smem_desc_sw128(bh + bo, 16, 1024);
+            const uint64_t dbl = B_MN ? make_smem_desc_sw128_32b(bl + bo, CHUNK_BYTES, 512)
+                                      : make_smem_desc_sw128(bl + bo, 16, 1024);
+            umma_tf32(d_tmem, dal, dbh, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);  // small terms first
+            umma_tf32(d_tmem, dah, dbl, IDESC, 1u);
+            umma_tf32(d_tmem, dah, dbh, IDESC, 1u);
+          }
+          issued = true;
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) stage = 0, phase ^= 1u;
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[acc]);
+        if (++acc == 2) acc = 0, acc_phase ^= 1u;
+      }
+      if (!ok && issued) {
+        umma_commit(drain);
+        const uint32_t addr = smem_u32(drain);
+        const unsigned long long t0 = global_timer_ns();
+        while (!mbar_try_wait(addr, 0)) {
+          if (global_timer_ns() - t0 > kWaitLimitNs) {
+            record_device_error(kDevErrAbortDrain);
+            break;
+          }
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..5)
+    const int q = warp & 3;
+    const int row_in_tile = 32 * q + lane;
+    unsigned char* stage_buf[2] = {smem + L::OFF_C + ((warp - 2) * 2 + 0) * L::C_STAGE,
+                                   smem + L::OFF_C + ((warp - 2) * 2 + 1) * L::C_STAGE};
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int sbuf = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+      int b, mt, nt;
+      x3_tile_coords(t, p, b, mt, nt);
+      const int m0 = mt * X3_BM, n0 = nt * BN;
+      if (!mbar_wait_bounded(&acc_full[acc], acc_phase, kDevErrWaitTimeoutAccFull, abort_flag)) break;
+      tc_fence_after_sync();
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(acc * BN);
+      const int64_t grow = static_cast<int64_t>(m0) + row_in_tile;
+#pragma unroll 1
+      for (int ch = 0; ch < BN / X3_CHUNK; ++ch) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + ch * X3_CHUNK, r);
+        tmem_wait_ld();
+        if (ch == BN / X3_CHUNK - 1) {
+          tc_fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        }
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __fmul_rn(p.alpha, __uint_as_float(r[i]));
+        if (p.beta != 0.f && grow < p.M) {
+          const int64_t gcol0 = static_cast<int64_t>(n0) + ch * X3_CHUNK;
+          const float* crow = p.C_in + static_cast<int64_t>(b) * p.strideC + grow * p.ldc;
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (gcol0 + i < p.N) v[i] = __fadd_rn(v[i], __fmul_rn(p.beta, crow[gcol0 + i]));
+        }
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+        unsigned char* sbase = stage_buf[sbuf];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          *reinterpret_cast<float4*>(sbase + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+              make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_3d(&tmC, sbase, n0 + ch * X3_CHUNK, m0 + 32 * q, b);
+          bulk_commit_group();
+        }
+        sbuf ^= 1;
+      }
+      if (++acc == 2) acc = 0, acc_phase ^= 1u;
+    }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem_base, L::TMEM_COLS);
+  }
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN>
+int launch_x3(const GemmProblem& p, cudaStream_t stream, const char* name) {
+  using L = X3Smem<BN, STAGES>;
+  const auto dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  CUtensorMap mA, mB, mC;
+  bool ok = true;
+  constexpr auto kMN = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;  // MN-major tf32 layout
+  if (A_MN) ok &= make_map_es(&mA, dt, 4, p.A, p.M, p.K, p.batch, p.lda, p.strideA, 32, X3_BK, kMN);
+  else ok &= make_map_es(&mA, dt, 4, p.A, p.K, p.M, p.batch, p.lda, p.strideA, X3_BK, X3_BM);
+  if (B_MN) ok &= make_map_es(&mB, dt, 4, p.B, p.N, p.K, p.batch, p.ldb, p.strideB, 32, X3_BK, kMN);
+  else ok &= make_map_es(&mB, dt, 4, p.B, p.K, p.N, p.batch, p.ldb, p.strideB, X3_BK, BN);
+  ok &= make_map_es(&mC, dt, 4, p.C, p.N, p.M, p.batch, p.ldc, p.strideC, X3_CHUNK, 32);
+  if (!ok) return CUOPX_CUDA_ERROR;
+  X3Params prm;
+  prm.M = static_cast<int>(p.M);
+  prm.N = static_cast<int>(p.N);
+  prm.K = static_cast<int>(p.K);
+  prm.batch = static_cast<int>(p.batch);
+  prm.tiles_m = static_cast<int>((p.M + X3_BM - 1) / X3_BM);
+  prm.tiles_n = static_cast<int>((p.N + BN - 1) / BN);
+  prm.num_tiles = prm.tiles_m * prm.tiles_n * prm.batch;
+  prm.k_blocks = static_cast<int>((p.K + X3_BK - 1) / X3_BK);
+  prm.alpha = static_cast<float>(p.alpha);
+  prm.beta = static_cast<float>(p.beta);
+  prm.C_in = static_cast<const float*>(p.C);
+  prm.ldc = p.ldc;
+  prm.strideC = p.strideC;
+  auto kern = gemm_tf32x3_kernel<BN, STAGES, A_MN, B_MN>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return CUOPX_CUDA_ERROR;
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) != cudaSuccess)
+      return CUOPX_CUDA_ERROR;
+    attr_set[dev] = true;
+  }
+  const int grid = std::min(prm.num_tiles, device_sm_count());
+  kern<<<grid, X3_THREADS, L::ALLOC, stream>>>(mA, mB, mC, prm);
+  note_launch(name);
+  return check_launch();
+}
+
+template <int BN, int STAGES>
+int launch_x3_layout(const GemmProblem& p, cudaStream_t stream, const char* name) {
+  const bool a_mn = p.transA, b_mn = !p.transB;
+  if (!a_mn && b_mn) return launch_x3<BN, STAGES, false, true>(p, stream, name);
+  if (!a_mn && !b_mn) return launch_x3<BN, STAGES, false, false>(p, stream, name);
+  if (a_mn && b_mn) return launch_x3<BN, STAGES, true, true>(p, stream, name);
+  return launch_x3<BN, STAGES, true, false>(p, stream, name);
+}
+
+}  // namespace
+
+bool gemm_tf32x3_supported(const GemmProblem& p) {
+  if (p.dtype != CUOPX_F32) return false;
+  if (p.M <= 0 || p.N <= 0 || p.K <= 0 || p.batch <= 0) return false;
+  if (p.M > INT32_MAX || p.N > INT32_MAX || p.K > INT32_MAX || p.batch > 65535) return false;
+  auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) % 16) == 0; };
+  if (!al16(p.A) || !al16(p.B) || !al16(p.C)) return false;
+  if (p.lda % 4 || p.ldb % 4 || p.ldc % 4) return false;
+  if (p.batch > 1 && (p.strideA % 4 || p.strideB % 4 || p.strideC % 4 || p.strideA == 0 || p.strideB == 0 ||
+                      p.strideC == 0))
+    return false;
+  return true;
+}
+
+int gemm_tf32x3(const GemmProblem& p, cudaStream_t stream) {
+  const int sms = device_sm_count();
+  const int64_t tiles128 = ((p.M + X3_BM - 1) / X3_BM) * ((p.N + 127) / 128) * p.batch;
+  if (p.N > 64 && tiles128 >= sms) return launch_x3_layout<128, 3>(p, stream, "gemm_tf32x3_128x128");
+  return launch_x3_layout<64, 4>(p, stream, "gemm_tf32x3_128x64");
+}
+
+}  // namespace cuopx

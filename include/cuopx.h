@@ -54,6 +54,24 @@ int cuopx_get_device_error(int* code_out);
 int cuopx_clear_device_error(void);
 
 /*
+ * fp32 GEMM arithmetic, process-wide:
+ *   CUOPX_FP32_AUTO (default): problems of 256^3 and up with 16-byte-aligned
+ *     rows run 3xTF32 on the tensor cores (hi*hi + hi*lo + lo*hi, fp32
+ *     accumulate; meets ||C-R||_F/||R||_F <= 1e-5*sqrt(K), not bit-identical
+ *     to an FFMA loop); the rest run FFMA.
+ *   CUOPX_FP32_FFMA: always FFMA, one fma chain per output in ascending k —
+ *     the summation order of the reference's kernels (gemm.cu:23-41), so
+ *     results reproduce a CPU loop in that order bit for bit.
+ *   CUOPX_FP32_TF32X3: 3xTF32 at every size it supports.
+ * No reference counterpart (the reference has only FFMA kernels).
+ */
+#define CUOPX_FP32_AUTO 0
+#define CUOPX_FP32_FFMA 1
+#define CUOPX_FP32_TF32X3 2
+int cuopx_set_fp32_gemm_mode(int mode);
+int cuopx_get_fp32_gemm_mode(void);
+
+/*
  * GEMM: C = alpha * op(A) * op(B) + beta * C, all row-major.
  *   op(A) is M x K: A is M x K (lda >= K) or, if transA, K x M (lda >= M).
  *   op(B) is K x N: B is K x N (ldb >= N) or, if transB, N x K (ldb >= K).

@@ -41,3 +41,14 @@ def _no_device_error(request):
         if code:
             cx.clear_device_error()
         assert code == 0, f"device-side error word set: {code}"
+
+
+@pytest.fixture
+def fp32_ffma():
+    """Run a test with fp32 GEMM forced onto the FFMA kernels (bit-reproducible
+    ascending-k order); restores the default mode afterwards."""
+    from cuop_b200 import _native as N
+
+    assert N.lib().cuopx_set_fp32_gemm_mode(N.FP32_FFMA) == 0
+    yield
+    assert N.lib().cuopx_set_fp32_gemm_mode(N.FP32_AUTO) == 0

@@ -23,7 +23,7 @@ def test_known_answer_batch3d(dev):
 
 
 @pytest.mark.parametrize("batch,M,N,K", [(3, 33, 17, 65), (16, 128, 128, 64), (5, 100, 200, 300)])
-def test_f32_bit_exact(dev, batch, M, N, K):
+def test_f32_bit_exact(dev, fp32_ffma, batch, M, N, K):
     A = O.uniform((batch, M, K), seed=1)
     B = O.uniform((batch, K, N), seed=2)
     C0 = O.uniform((batch, M, N), seed=3)
@@ -83,7 +83,7 @@ def test_c4_bf16_batched_full(dev):
         assert O.max_relative(O.from_lowp(got, dt), O.from_lowp(ref, dt)) <= 1e-2
 
 
-def test_shared_b_stride_zero(dev):
+def test_shared_b_stride_zero(dev, fp32_ffma):
     """strideB == 0 broadcasts one B to every batch (generic path)."""
     from cuop_b200 import _native as N
 

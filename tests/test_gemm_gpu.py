@@ -1,8 +1,10 @@
 """GEMM parity through the C ABI.
 
-fp32 / fp64 (SIMT kernels): every output is the same ascending-k fma chain as
-the CPU oracle, so results must be BIT-IDENTICAL to it; the bound
+fp32 / fp64 on the FFMA kernels: every output is the same ascending-k fma
+chain as the CPU oracle, so results must be BIT-IDENTICAL to it; the bound
 ||C-R||_F/||R||_F <= 1e-5*sqrt(K) is checked against an fp64 product too.
+fp32 on the tensor cores (3xTF32, the default for >= 256^3): the same bound
+against the fp64 product.
 fp16 / bf16 (tcgen05 kernels): max|C-R| / max|R| <= 1e-2 against the oracle
 (fp32 products and sums, one rounding)."""
 import json
@@ -38,7 +40,7 @@ F32_CASES = [
 
 
 @pytest.mark.parametrize("M,N,K,tA,tB", F32_CASES)
-def test_f32_bit_exact_vs_oracle(dev, M, N, K, tA, tB):
+def test_f32_bit_exact_vs_oracle(dev, fp32_ffma, M, N, K, tA, tB):
     A = O.uniform((K, M) if tA else (M, K), seed=M + 1)
     B = O.uniform((N, K) if tB else (K, N), seed=N + 2)
     C0 = O.uniform((M, N), seed=3)
@@ -51,7 +53,7 @@ def test_f32_bit_exact_vs_oracle(dev, M, N, K, tA, tB):
     assert O.rel_frobenius(got, exact) <= 1e-5 * np.sqrt(K)
 
 
-def test_f32_fast_kernel_selected(dev):
+def test_f32_fast_kernel_selected(dev, fp32_ffma):
     A = to_dev_f32(O.uniform((512, 512), seed=1), dev)
     B = to_dev_f32(O.uniform((512, 512), seed=2), dev)
     cx.gemm(A, B)
@@ -65,25 +67,81 @@ def test_f64_bit_exact_vs_oracle(dev):
     np.testing.assert_array_equal(C.cpu().numpy(), O.gemm_f64(A, B))
 
 
+def test_c1_fp32_1024_ffma_bit_exact(dev, fp32_ffma):
+    """C1 on the FFMA kernel: bit-identical to the oracle's ascending-k chain."""
+    n = 1024
+    A32 = O.uniform((n, n), seed=0)
+    B32 = O.uniform((n, n), seed=1)
+    C = cx.gemm(to_dev_f32(A32, dev), to_dev_f32(B32, dev))
+    assert cx.last_kernel().startswith("gemm_f32_")
+    np.testing.assert_array_equal(C.cpu().numpy(), O.gemm_f32(A32, B32))
+
+
 def test_c1_fp32_1024_vs_oracle_and_reference_operator(dev):
-    """C1: fp32 1024^3, A,B ~ U[-1,1) seeds 0/1, C zero, alpha=1 beta=0."""
+    """C1: fp32 1024^3, A,B ~ U[-1,1) seeds 0/1, C zero, alpha=1 beta=0 —
+    default path (3xTF32), the CPU oracle and the reference's own Gemm<float>
+    all within 1e-5*sqrt(K) of the fp64 product."""
     n = 1024
     A32 = O.uniform((n, n), seed=0)
     B32 = O.uniform((n, n), seed=1)
     A, B = to_dev_f32(A32, dev), to_dev_f32(B32, dev)
     C = cx.gemm(A, B)
+    assert cx.last_kernel().startswith("gemm_tf32x3_"), cx.last_kernel()
     cpu = O.gemm_f32(A32, B32)
-    np.testing.assert_array_equal(C.cpu().numpy(), cpu)
     exact = A32.astype(np.float64) @ B32.astype(np.float64)
-    assert O.rel_frobenius(cpu, exact) <= 1e-5 * np.sqrt(n)
+    tol = 1e-5 * np.sqrt(n)
+    assert O.rel_frobenius(cpu, exact) <= tol
+    err = O.rel_frobenius(C.cpu().numpy(), exact)
+    assert err <= tol
+    assert err <= 0.1 * tol  # 3xTF32 sits at least 10x inside the bound
     if O.ref_available():
         Cr = torch.zeros(n, n, device=dev)
         torch.cuda.synchronize()
         assert O.ref_lib().ref_gemm_f32(0, 0, n, n, n, 1.0, A.data_ptr(), B.data_ptr(), 0.0, Cr.data_ptr()) == 0
         ref_gpu = Cr.cpu().numpy()
-        assert O.rel_frobenius(ref_gpu, exact) <= 1e-5 * np.sqrt(n)
-        # The reference's blocked kernel is the same ascending-k fma chain.
-        assert O.rel_frobenius(C.cpu().numpy(), ref_gpu) <= 1e-6
+        assert O.rel_frobenius(ref_gpu, exact) <= tol
+        # The reference's blocked kernel is the oracle's ascending-k fma chain.
+        assert O.rel_frobenius(ref_gpu, cpu) <= 1e-6
+        assert O.rel_frobenius(C.cpu().numpy(), ref_gpu) <= tol
+
+
+X3_CASES = [
+    (256, 256, 256, False, False), (1024, 512, 768, False, False), (300, 200, 500, False, False),
+    (512, 384, 256, True, False), (512, 384, 256, False, True), (512, 384, 256, True, True),
+    (2048, 2048, 2048, False, False), (4096, 96, 4100, False, False),
+]
+
+
+@pytest.mark.parametrize("M,N,K,tA,tB", X3_CASES)
+def test_f32_tf32x3_within_tolerance(dev, M, N, K, tA, tB):
+    A = O.uniform((K, M) if tA else (M, K), seed=M + 5)
+    B = O.uniform((N, K) if tB else (K, N), seed=N + 6)
+    C0 = O.uniform((M, N), seed=7)
+    C = cx.gemm(to_dev_f32(A, dev), to_dev_f32(B, dev), to_dev_f32(C0, dev), transA=tA, transB=tB, alpha=0.75,
+                beta=-0.5)
+    assert cx.last_kernel().startswith("gemm_tf32x3_"), cx.last_kernel()
+    exact = 0.75 * ((A.T if tA else A).astype(np.float64) @ (B.T if tB else B).astype(np.float64)) - 0.5 * C0
+    err = O.rel_frobenius(C.cpu().numpy(), exact)
+    assert err <= 1e-5 * np.sqrt(K), err
+    assert err <= 0.1 * 1e-5 * np.sqrt(K), err  # at least 10x inside the required bound
+
+
+def test_f32_tf32x3_batched_and_deterministic(dev):
+    A = to_dev_f32(O.uniform((6, 256, 192), seed=1), dev)
+    B = to_dev_f32(O.uniform((6, 192, 320), seed=2), dev)
+    C1 = cx.batched_gemm(A, B)
+    assert cx.last_kernel().startswith("gemm_tf32x3_")
+    C2 = cx.batched_gemm(A, B)
+    assert torch.equal(C1, C2)
+    exact = np.einsum("bmk,bkn->bmn", A.double().cpu().numpy(), B.double().cpu().numpy())
+    assert O.rel_frobenius(C1.cpu().numpy(), exact) <= 0.1 * 1e-5 * np.sqrt(192)
+
+
+def test_fp32_mode_switch_validates():
+    from cuop_b200 import _native as N
+
+    assert N.lib().cuopx_set_fp32_gemm_mode(7) == N.INVALID_ARGUMENT
+    assert N.lib().cuopx_get_fp32_gemm_mode() == N.FP32_AUTO
 
 
 LOWP_CASES = [
