@@ -9,12 +9,12 @@
 // reference's FFMA chain (gemm.cu:14-42), so results match within that
 // tolerance, not bit for bit (the FFMA kernels in gemm_simt.cu are exact).
 //
-// One persistent CTA per SM, 10 warps:
+// One persistent CTA per SM, 14 warps:
 //   warp 0      TMA producer: fp32 A (128 x 32) and B (BN x 32) tiles into the
 //               "hi" buffers of a STAGES-deep ring: 128-byte swizzle for
 //               K-major operands, 128-byte swizzle with 32-byte atoms for
 //               MN-major ones (the only MN-major layout tf32 MMAs accept).
-//   warps 6..9  converters: wait for a landed stage, rewrite hi in place and
+//   warps 6..13 converters: wait for a landed stage, rewrite hi in place and
 //               write lo next to it (same swizzled layout: the split is
 //               elementwise), fence the async proxy, signal the MMA warp.
 //   warp 1      TMEM allocator + MMA issuer: 3 x (BK/8) MMAs (M=128, N=BN,
@@ -30,9 +30,9 @@ namespace {
 
 constexpr int X3_BM = 128;
 constexpr int X3_BK = 32;  // 32 fp32 = 128 bytes = one swizzle row
-constexpr int X3_THREADS = 320;
+constexpr int X3_THREADS = 448;
 constexpr int X3_EPI_WARPS = 4;
-constexpr int X3_CONV_WARPS = 4;
+constexpr int X3_CONV_WARPS = 8;
 constexpr int X3_CHUNK = 32;  // epilogue columns per TMA store (32 fp32 = 128 bytes)
 
 struct X3Params {
@@ -84,21 +84,28 @@ __device__ __forceinline__ uint32_t to_tf32_rna(float x) {
   return r;
 }
 
-// hi/lo split of `bytes` bytes at `hi` (in place) and `lo`, by `nthreads` threads.
-__device__ __forceinline__ void split_tf32(unsigned char* hi, unsigned char* lo, int bytes, int tid, int nthreads) {
-  for (int off = tid * 16; off < bytes; off += nthreads * 16) {
-    float4 v = *reinterpret_cast<const float4*>(hi + off);
+// hi/lo split of BYTES bytes at `hi` (in place) and `lo` by NT threads; the
+// trip count is a compile-time constant so every load is issued up front.
+template <int BYTES, int NT>
+__device__ __forceinline__ void split_tf32(unsigned char* hi, unsigned char* lo, int tid) {
+  static_assert(BYTES % (NT * 16) == 0, "split must divide evenly");
+  constexpr int ITERS = BYTES / (NT * 16);
+  float4 v[ITERS];
+#pragma unroll
+  for (int i = 0; i < ITERS; ++i) v[i] = *reinterpret_cast<const float4*>(hi + (i * NT + tid) * 16);
+#pragma unroll
+  for (int i = 0; i < ITERS; ++i) {
     float4 h, l;
-    h.x = __uint_as_float(to_tf32_rna(v.x));
-    h.y = __uint_as_float(to_tf32_rna(v.y));
-    h.z = __uint_as_float(to_tf32_rna(v.z));
-    h.w = __uint_as_float(to_tf32_rna(v.w));
-    l.x = __fsub_rn(v.x, h.x);
-    l.y = __fsub_rn(v.y, h.y);
-    l.z = __fsub_rn(v.z, h.z);
-    l.w = __fsub_rn(v.w, h.w);
-    *reinterpret_cast<float4*>(hi + off) = h;
-    *reinterpret_cast<float4*>(lo + off) = l;
+    h.x = __uint_as_float(to_tf32_rna(v[i].x));
+    h.y = __uint_as_float(to_tf32_rna(v[i].y));
+    h.z = __uint_as_float(to_tf32_rna(v[i].z));
+    h.w = __uint_as_float(to_tf32_rna(v[i].w));
+    l.x = __fsub_rn(v[i].x, h.x);
+    l.y = __fsub_rn(v[i].y, h.y);
+    l.z = __fsub_rn(v[i].z, h.z);
+    l.w = __fsub_rn(v[i].w, h.w);
+    *reinterpret_cast<float4*>(hi + (i * NT + tid) * 16) = h;
+    *reinterpret_cast<float4*>(lo + (i * NT + tid) * 16) = l;
   }
 }
 
@@ -220,8 +227,8 @@ __global__ void __launch_bounds__(X3_THREADS, 1)
           ok = false;
           break;
         }
-        split_tf32(L::a_hi(smem, stage), L::a_lo(smem, stage), L::A_BYTES, ctid, X3_CONV_WARPS * 32);
-        split_tf32(L::b_hi(smem, stage), L::b_lo(smem, stage), L::B_BYTES, ctid, X3_CONV_WARPS * 32);
+        split_tf32<L::A_BYTES, X3_CONV_WARPS * 32>(L::a_hi(smem, stage), L::a_lo(smem, stage), ctid);
+        split_tf32<L::B_BYTES, X3_CONV_WARPS * 32>(L::b_hi(smem, stage), L::b_lo(smem, stage), ctid);
         fence_proxy_async_shared();  // generic-proxy writes -> visible to the tensor cores
         __syncwarp();
         if (lane == 0) mbar_arrive(&conv[stage]);
