@@ -7,5 +7,6 @@
 #include "gemv_noalloc.cu"
 #include "gemm_simt.cu"
 #include "gemm_tc.cu"
+#include "gemm_tc2.cu"
 #include "gemm_tf32x3.cu"
 #include "vector_ops.cu"

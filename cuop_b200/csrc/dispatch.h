@@ -51,6 +51,10 @@ int gemm_simt_f32(const GemmProblem& p, cudaStream_t stream);
 bool gemm_tc_supported(const GemmProblem& p);
 int gemm_tc(const GemmProblem& p, cudaStream_t stream);
 
+// Two-SM (cta_group::2) tcgen05 back-end (gemm_tc2.cu) for large fp16/bf16.
+bool gemm_tc2_wanted(const GemmProblem& p);
+int gemm_tc2(const GemmProblem& p, cudaStream_t stream);
+
 // 3xTF32 tcgen05 back-end (gemm_tf32x3.cu) for fp32.
 bool gemm_tf32x3_supported(const GemmProblem& p);
 int gemm_tf32x3(const GemmProblem& p, cudaStream_t stream);

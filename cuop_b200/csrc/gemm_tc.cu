@@ -449,6 +449,7 @@ bool gemm_tc_supported(const GemmProblem& p) {
 }
 
 int gemm_tc(const GemmProblem& p, cudaStream_t stream) {
+  if (gemm_tc2_wanted(p)) return gemm_tc2(p, stream);
   // BN=256 when N fills it and the tile count still covers the SMs; else BN=128.
   const int sms = device_sm_count();
   const int64_t tiles256 = ((p.M + BM - 1) / BM) * ((p.N + 255) / 256) * p.batch;

@@ -1,0 +1,470 @@
+// Two-SM tcgen05 GEMM (cta_group::2) for large fp16/bf16 problems.
+//
+// A cluster of two CTAs on two SMs owns a 256 x 256 output tile.  CTA r of the
+// pair loads rows [128r, 128r+128) of the A tile and columns [128r, 128r+128)
+// of the B tile into its own shared memory; one tcgen05.mma.cta_group::2
+// (M=256, N=256, K=16) issued by the even CTA reads both CTAs' halves and
+// writes each CTA's 128 accumulator rows into that CTA's TMEM.  Per SM this
+// halves the shared-memory operand traffic of the 1-SM 128 x 256 kernel
+// (32 KB instead of 48 KB per 64-deep K block).
+//
+//   warp 0      TMA producer (both CTAs): loads complete on the LEADER's
+//               `full` mbarrier (.cta_group::2); the leader posts the
+//               expected byte count for both halves.
+//   warp 1      TMEM allocation (cta_group::2, both CTAs); on the leader, the
+//               MMA issuer: waits `full`, issues 4 MMAs per stage, commits
+//               stage release to `empty` and tile completion to `acc_full`
+//               in BOTH CTAs (tcgen05.commit multicast).
+//   warps 2..5  epilogue (both CTAs): own TMEM rows -> alpha/beta -> swizzled
+//               staging -> TMA store; then arrive on the leader's `acc_empty`.
+// No TMA multicast: every CTA loads its own halves.  Cluster barriers bracket
+// the kernel so no CTA exits while its peer may still touch its shared memory.
+#include "common.cuh"
+#include "dispatch.h"
+
+namespace cuopx {
+
+namespace {
+
+constexpr int P_BM = 128;   // rows per CTA (pair: 256)
+constexpr int P_BN = 256;   // pair tile columns; each CTA holds 128 of B
+constexpr int P_BK = 64;
+constexpr int P_STAGES = 6;
+constexpr int P_THREADS = 192;
+constexpr int P_EPI_WARPS = 4;
+constexpr int P_CHUNK = 64;
+constexpr uint32_t P_TMEM_COLS = 512;
+constexpr int P_ACC_BUFS = 2;
+constexpr int P_GROUP_M = 8;  // pair-row tiles per raster group
+
+struct PairSmem {
+  static constexpr int A_STAGE = P_BM * P_BK * 2;            // 16 KB
+  static constexpr int B_STAGE = (P_BN / 2) * P_BK * 2;      // 16 KB (this CTA's half)
+  static constexpr int C_STAGE = 32 * P_CHUNK * 2;           // 4 KB
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_B = P_STAGES * A_STAGE;
+  static constexpr int OFF_C = OFF_B + P_STAGES * B_STAGE;
+  static constexpr int OFF_BAR = OFF_C + P_EPI_WARPS * 2 * C_STAGE;
+  // full[S], empty[S], acc_full[2], acc_empty[2], drain
+  static constexpr int NUM_BARS = 2 * P_STAGES + 2 * P_ACC_BUFS + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr int ALLOC = OFF_MISC + 16 + 1024;
+  static_assert(ALLOC <= 232448, "shared memory budget exceeded");
+};
+
+struct PairParams {
+  int M, N, K, batch;
+  int tiles_m, tiles_n, num_tiles, k_blocks;  // tiles are 256 x 256 pair tiles
+  float alpha, beta;
+  const void* C_in;
+  int64_t ldc, strideC;
+};
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t nclusters_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of the same shared variable in CTA `rank`.
+__device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
+  return out;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// TMA load into this CTA's smem, completing bytes on the mbarrier at a
+// shared::cluster address (the leader's), no multicast.
+__device__ __forceinline__ void tma_load_3d_pair(void* smem_dst, const void* tmap, uint32_t mbar_cluster, int c0,
+                                                 int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(mbar_cluster), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` (same offset) in both CTAs of the pair when all prior
+// tcgen05 ops of this thread complete.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void pair_tile_coords(int t, const PairParams& p, int& b, int& mt, int& nt) {
+  const int per_batch = p.tiles_m * p.tiles_n;
+  b = t / per_batch;
+  const int r = t - b * per_batch;
+  const int span = P_GROUP_M * p.tiles_n;
+  const int g = r / span;
+  const int first_m = g * P_GROUP_M;
+  const int gsize = min(P_GROUP_M, p.tiles_m - first_m);
+  const int rr = r - g * span;
+  mt = first_m + rr % gsize;
+  nt = rr / gsize;
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2_pair(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack2_pair<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2_pair<__half>(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <typename T, bool A_MN, bool B_MN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmC, const PairParams p) {
+  using L = PairSmem;
+  constexpr uint32_t PAIR_TX = 2u * static_cast<uint32_t>(L::A_STAGE + L::B_STAGE);
+  constexpr uint32_t AB_FMT = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+  constexpr uint32_t IDESC = make_idesc(AB_FMT, A_MN, B_MN, 2 * P_BM, P_BN);
+
+  extern __shared__ __align__(1024) unsigned char pair_smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(pair_smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + P_STAGES;
+  uint64_t* acc_full = bars + 2 * P_STAGES;
+  uint64_t* acc_empty = bars + 2 * P_STAGES + P_ACC_BUFS;
+  uint64_t* drain = bars + 2 * P_STAGES + 2 * P_ACC_BUFS;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = static_cast<int>(cluster_id_x());
+  const int npairs = static_cast<int>(nclusters_x());
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&full[s], 1);   // leader: its own arrive.expect_tx; both CTAs' bytes
+      mbar_init(&empty[s], 1);  // one multicast commit per phase
+    }
+    for (int a = 0; a < P_ACC_BUFS; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 2 * P_EPI_WARPS);  // leader's copy: 4 local + 4 remote arrivals
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    prefetch_tmap(&tmC);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(P_TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  cluster_sync_all();  // barrier inits and TMEM allocation visible to the peer
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      bool issued_any[P_STAGES];
+      uint32_t last_phase[P_STAGES];
+      for (int s = 0; s < P_STAGES; ++s) issued_any[s] = false, last_phase[s] = 0;
+      for (int t = pair; t < p.num_tiles && ok; t += npairs) {
+        int b, mt, nt;
+        pair_tile_coords(t, p, b, mt, nt);
+        const int m0 = mt * 2 * P_BM + static_cast<int>(rank) * P_BM;
+        const int n0 = nt * P_BN + static_cast<int>(rank) * (P_BN / 2);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, kDevErrWaitTimeoutEmpty, abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(&full[stage], PAIR_TX);
+          const uint32_t mbar = map_to_rank(&full[stage], 0);
+          unsigned char* sa = smem + L::OFF_A + stage * L::A_STAGE;
+          unsigned char* sb = smem + L::OFF_B + stage * L::B_STAGE;
+          const int k0 = kb * P_BK;
+          if constexpr (A_MN) {
+#pragma unroll
+            for (int j = 0; j < P_BM / 64; ++j) tma_load_3d_pair(sa + j * (64 * P_BK * 2), &tmA, mbar, m0 + 64 * j, k0, b);
+          } else {
+            tma_load_3d_pair(sa, &tmA, mbar, k0, m0, b);
+          }
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int j = 0; j < (P_BN / 2) / 64; ++j)
+              tma_load_3d_pair(sb + j * (64 * P_BK * 2), &tmB, mbar, n0 + 64 * j, k0, b);
+          } else {
+            tma_load_3d_pair(sb, &tmB, mbar, k0, n0, b);
+          }
+          issued_any[stage] = true;
+          last_phase[stage] = phase;
+          if (++stage == P_STAGES) stage = 0, phase ^= 1u;
+        }
+      }
+      if (ok) {
+        // Tail: wait until the leader has released every stage, so no
+        // multicast commit can still be on its way to this CTA's barriers.
+        for (int i = 0; i < P_STAGES; ++i) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, kDevErrWaitTimeoutEmpty, abort_flag)) break;
+          if (++stage == P_STAGES) stage = 0, phase ^= 1u;
+        }
+      } else if (leader) {
+        // Abort: let every phase this pair issued land (the leader's barrier
+        // counts both CTAs' bytes) before the cluster exits.
+        for (int s = 0; s < P_STAGES; ++s) {
+          if (!issued_any[s]) continue;
+          const uint32_t addr = smem_u32(&full[s]);
+          const unsigned long long t0 = global_timer_ns();
+          while (!mbar_try_wait(addr, last_phase[s])) {
+            if (global_timer_ns() - t0 > kWaitLimitNs) {
+              record_device_error(kDevErrAbortDrain);
+              break;
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (leader && lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true, issued = false;
+      for (int t = pair; t < p.num_tiles && ok; t += npairs) {
+        if (!mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1u, kDevErrWaitTimeoutAccEmpty, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after_sync();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * P_BN);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait_bounded(&full[stage], phase, kDevErrWaitTimeoutFull, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after_sync();
+          const uint32_t sa = smem_u32(smem + L::OFF_A + stage * L::A_STAGE);
+          const uint32_t sb = smem_u32(smem + L::OFF_B + stage * L::B_STAGE);
+#pragma unroll
+          for (int kk = 0; kk < P_BK / 16; ++kk) {
+            const uint64_t ad = A_MN ? make_smem_desc_sw128(sa + kk * 2048, 64 * P_BK * 2, 1024)
+                                     : make_smem_desc_sw128(sa + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? make_smem_desc_sw128(sb + kk * 2048, 64 * P_BK * 2, 1024)
+                                     : make_smem_desc_sw128(sb + kk * 32, 16, 1024);
+            umma_f16_pair(d_tmem, ad, bd, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          issued = true;
+          umma_commit_pair(&empty[stage]);
+          if (++stage == P_STAGES) stage = 0, phase ^= 1u;
+        }
+        if (!ok) break;
+        umma_commit_pair(&acc_full[acc]);
+        if (++acc == P_ACC_BUFS) acc = 0, acc_phase ^= 1u;
+      }
+      if (!ok && issued) {
+        umma_commit_pair(drain);
+        const uint32_t addr = smem_u32(drain);
+        const unsigned long long t0 = global_timer_ns();
+        while (!mbar_try_wait(addr, 0)) {
+          if (global_timer_ns() - t0 > kWaitLimitNs) {
+            record_device_error(kDevErrAbortDrain);
+            break;
+          }
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;
+    const int row_in_tile = 32 * q + lane;
+    unsigned char* stage_buf[2] = {smem + L::OFF_C + ((warp - 2) * 2 + 0) * L::C_STAGE,
+                                   smem + L::OFF_C + ((warp - 2) * 2 + 1) * L::C_STAGE};
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int sbuf = 0;
+    const T* Cin = static_cast<const T*>(p.C_in);
+    for (int t = pair; t < p.num_tiles; t += npairs) {
+      int b, mt, nt;
+      pair_tile_coords(t, p, b, mt, nt);
+      const int m0 = mt * 2 * P_BM + static_cast<int>(rank) * P_BM;
+      const int n0 = nt * P_BN;
+      if (!mbar_wait_bounded(&acc_full[acc], acc_phase, kDevErrWaitTimeoutAccFull, abort_flag)) break;
+      tc_fence_after_sync();
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(acc * P_BN);
+      const int64_t grow = static_cast<int64_t>(m0) + row_in_tile;
+#pragma unroll 1
+      for (int ch = 0; ch < P_BN / P_CHUNK; ++ch) {
+        uint32_t r0[32], r1[32];
+        tmem_ld_32x32b_x32(t_row + ch * P_CHUNK, r0);
+        tmem_ld_32x32b_x32(t_row + ch * P_CHUNK + 32, r1);
+        tmem_wait_ld();
+        if (ch == P_BN / P_CHUNK - 1) {
+          tc_fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(map_to_rank(&acc_empty[acc], 0));
+        }
+        float v[64];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          v[i] = p.alpha * __uint_as_float(r0[i]);
+          v[32 + i] = p.alpha * __uint_as_float(r1[i]);
+        }
+        if (p.beta != 0.f && grow < p.M) {
+          const int64_t gcol0 = static_cast<int64_t>(n0) + ch * P_CHUNK;
+          const T* crow = Cin + static_cast<int64_t>(b) * p.strideC + grow * p.ldc;
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (gcol0 + i < p.N) v[i] = __fadd_rn(v[i], __fmul_rn(p.beta, to_acc<T>(crow[gcol0 + i])));
+        }
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+        unsigned char* sbase = stage_buf[sbuf];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          uint4 w;
+          w.x = pack2_pair<T>(v[8 * j + 0], v[8 * j + 1]);
+          w.y = pack2_pair<T>(v[8 * j + 2], v[8 * j + 3]);
+          w.z = pack2_pair<T>(v[8 * j + 4], v[8 * j + 5]);
+          w.w = pack2_pair<T>(v[8 * j + 6], v[8 * j + 7]);
+          *reinterpret_cast<uint4*>(sbase + lane * 128 + ((j ^ (lane & 7)) << 4)) = w;
+        }
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_3d(&tmC, sbase, n0 + ch * P_CHUNK, m0 + 32 * q, b);
+          bulk_commit_group();
+        }
+        sbuf ^= 1;
+      }
+      if (++acc == P_ACC_BUFS) acc = 0, acc_phase ^= 1u;
+    }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  tc_fence_before_sync();
+  __syncthreads();
+  cluster_sync_all();  // the peer is done with this CTA's smem, barriers and TMEM
+  if (warp == 1) {
+    tc_fence_after_sync();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(P_TMEM_COLS)
+                 : "memory");
+  }
+}
+
+template <typename T, bool A_MN, bool B_MN>
+int launch_tc2(const GemmProblem& p, cudaStream_t stream, const char* name) {
+  using L = PairSmem;
+  const CUtensorMapDataType dt =
+      std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap mA, mB, mC;
+  bool ok = true;
+  if (A_MN) ok &= make_map(&mA, dt, p.A, p.M, p.K, p.batch, p.lda, p.strideA, 64, P_BK);
+  else ok &= make_map(&mA, dt, p.A, p.K, p.M, p.batch, p.lda, p.strideA, P_BK, P_BM);
+  if (B_MN) ok &= make_map(&mB, dt, p.B, p.N, p.K, p.batch, p.ldb, p.strideB, 64, P_BK);
+  else ok &= make_map(&mB, dt, p.B, p.K, p.N, p.batch, p.ldb, p.strideB, P_BK, P_BN / 2);
+  ok &= make_map(&mC, dt, p.C, p.N, p.M, p.batch, p.ldc, p.strideC, P_CHUNK, 32);
+  if (!ok) return CUOPX_CUDA_ERROR;
+  PairParams prm;
+  prm.M = static_cast<int>(p.M);
+  prm.N = static_cast<int>(p.N);
+  prm.K = static_cast<int>(p.K);
+  prm.batch = static_cast<int>(p.batch);
+  prm.tiles_m = static_cast<int>((p.M + 2 * P_BM - 1) / (2 * P_BM));
+  prm.tiles_n = static_cast<int>((p.N + P_BN - 1) / P_BN);
+  prm.num_tiles = prm.tiles_m * prm.tiles_n * prm.batch;
+  prm.k_blocks = static_cast<int>((p.K + P_BK - 1) / P_BK);
+  prm.alpha = static_cast<float>(p.alpha);
+  prm.beta = static_cast<float>(p.beta);
+  prm.C_in = p.C;
+  prm.ldc = p.ldc;
+  prm.strideC = p.strideC;
+  auto kern = gemm_tc2_kernel<T, A_MN, B_MN>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return CUOPX_CUDA_ERROR;
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) != cudaSuccess)
+      return CUOPX_CUDA_ERROR;
+    attr_set[dev] = true;
+  }
+  const int sms = device_sm_count() / 2 * 2;
+  const int grid = std::min(prm.num_tiles * 2, sms);  // even: whole clusters
+  kern<<<grid, P_THREADS, L::ALLOC, stream>>>(mA, mB, mC, prm);
+  note_launch(name);
+  return check_launch();
+}
+
+}  // namespace
+
+bool gemm_tc2_wanted(const GemmProblem& p) {
+  // Pair tiles pay off when there are enough 256 x 256 tiles to fill the SMs.
+  if (!gemm_tc_supported(p)) return false;
+  const int64_t tiles = ((p.M + 255) / 256) * ((p.N + 255) / 256) * p.batch;
+  return p.M >= 256 && p.N >= 256 && p.K >= 256 && tiles >= device_sm_count() / 2;
+}
+
+int gemm_tc2(const GemmProblem& p, cudaStream_t stream) {
+  const bool a_mn = p.transA, b_mn = !p.transB;
+  if (p.dtype == CUOPX_BF16) {
+    if (!a_mn && b_mn) return launch_tc2<__nv_bfloat16, false, true>(p, stream, "gemm_tc2_256x256");
+    if (!a_mn && !b_mn) return launch_tc2<__nv_bfloat16, false, false>(p, stream, "gemm_tc2_256x256");
+    if (a_mn && b_mn) return launch_tc2<__nv_bfloat16, true, true>(p, stream, "gemm_tc2_256x256");
+    return launch_tc2<__nv_bfloat16, true, false>(p, stream, "gemm_tc2_256x256");
+  }
+  if (!a_mn && b_mn) return launch_tc2<__half, false, true>(p, stream, "gemm_tc2_256x256");
+  if (!a_mn && !b_mn) return launch_tc2<__half, false, false>(p, stream, "gemm_tc2_256x256");
+  if (a_mn && b_mn) return launch_tc2<__half, true, true>(p, stream, "gemm_tc2_256x256");
+  return launch_tc2<__half, true, false>(p, stream, "gemm_tc2_256x256");
+}
+
+}  // namespace cuopx

@@ -164,6 +164,30 @@ def test_lowp_tcgen05_vs_oracle(dev, dt, M, N, K, tA, tB):
     assert err <= LOWP_TOL, (err, cx.last_kernel())
 
 
+PAIR_CASES = [  # enough 256x256 tiles to take the two-SM (cta_group::2) kernel
+    (4096, 2560, 512, False, False), (4000, 2600, 520, False, False), (2560, 4096, 256, True, False),
+    (2560, 4096, 256, False, True), (2560, 4096, 256, True, True), (3072, 3072, 1000, False, False),
+]
+
+
+@pytest.mark.parametrize("dt", [O.F16, O.BF16])
+@pytest.mark.parametrize("M,N,K,tA,tB", PAIR_CASES)
+def test_lowp_pair_kernel_vs_oracle(dev, dt, M, N, K, tA, tB):
+    A = O.to_lowp(O.normal((K, M) if tA else (M, K), seed=M + 11) / np.sqrt(K), dt)
+    B = O.to_lowp(O.normal((N, K) if tB else (K, N), seed=N + 13), dt)
+    C0 = O.to_lowp(O.normal((M, N), seed=17), dt)
+    Cd = to_dev_lowp(C0, dt, dev)
+    cx.gemm(to_dev_lowp(A, dt, dev), to_dev_lowp(B, dt, dev), Cd, transA=tA, transB=tB, alpha=1.5, beta=0.5)
+    assert cx.last_kernel() == "gemm_tc2_256x256", cx.last_kernel()
+    full = 1.5 * fp32_reference_gpu(to_dev_lowp(A, dt, dev), to_dev_lowp(B, dt, dev), tA, tB) + \
+        0.5 * to_dev_lowp(C0, dt, dev).float()
+    assert O.max_relative(Cd.float().cpu().numpy(), full.cpu().numpy()) <= LOWP_TOL
+    rows = np.array([0, 1, 255, 256, M - 1])
+    ref = O.gemm_lowp(dt, A[:, rows] if tA else A[rows], B, C0[rows], transA=tA, transB=tB, alpha=1.5, beta=0.5)
+    got = O.from_lowp(lowp_bits(Cd[torch.as_tensor(rows, device=dev)]), dt)
+    assert O.max_relative(got, O.from_lowp(ref, dt)) <= LOWP_TOL
+
+
 @pytest.mark.parametrize("dt", [O.F16, O.BF16])
 def test_lowp_alpha_beta(dev, dt):
     M, N, K = 320, 640, 256
@@ -218,7 +242,7 @@ def test_c3_fp16_8192_full(dev):
     B16 = O.to_lowp(O.normal((n, n), seed=1) / np.sqrt(n), dt)
     A, B = to_dev_lowp(A16, dt, dev), to_dev_lowp(B16, dt, dev)
     C = cx.gemm(A, B)
-    assert cx.last_kernel() == "gemm_tc_128x256"
+    assert cx.last_kernel() == "gemm_tc2_256x256"
     full = fp32_reference_gpu(A, B)
     assert O.max_relative(C.float().cpu().numpy(), full.cpu().numpy()) <= LOWP_TOL
     rng = np.random.default_rng(0)
