@@ -9,9 +9,12 @@ L2).  Metric: HBM GB/s of algorithmic traffic (A once, x once, y written once
 per GEMV).  The GEMV path does not shard, so `--gpus N` runs N replicas.
 
 The same line carries, under "configs", the other GEMM shapes of the path:
-fp32 GEMM 1024^3, fp16 GEMM 8192^3 (N-sharded + NCCL all-gather when N>1),
-bf16 batched 4096 x 128x128x64 (batch-sharded, no collective), bf16 linear
-4096 x 8192 x 28672 (column-sharded + all-gather).
+fp32 GEMM 1024^3, fp16 GEMM 8192^3, bf16 batched 4096 x 128x128x64
+(batch-sharded, no collective), bf16 linear 4096 x 8192 x 28672.  At N>1 the
+two large GEMMs are column-sharded and the full output is assembled on every
+rank by the GEMM epilogue's own stores into the peers' outputs over NVLink
+(GEMM + NCCL all-gather + gather kernel is timed beside it).
+`--configs c3` (etc.) runs a subset of them.
 
 `--impl reference` times the reference path's CPU restatement (the
 reference has no CPU implementation of its own) on the host cores.
@@ -166,9 +169,11 @@ def capture_graph(fn, n):
     return g, cx.launch_count() - c0
 
 
-def time_graph(fn, steps, warmup, world):
+def time_graph(fn, steps, warmup, world, align=None):
     """Device time (ms per call) of `steps` calls of fn replayed as one CUDA
-    graph after `warmup` eager calls; max over ranks."""
+    graph after `warmup` eager calls; max over ranks.  `align`, if given, is
+    launched on the stream just before the timed replay (a cross-GPU barrier,
+    so that host-side skew between ranks stays out of the timed region)."""
     import torch
 
     for i in range(warmup):
@@ -176,6 +181,8 @@ def time_graph(fn, steps, warmup, world):
     g, _ = capture_graph(fn, steps)
     g.replay()  # first replay uploads the graph
     barrier(world)
+    if align is not None:
+        align()
     s = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(s)
@@ -369,45 +376,93 @@ def run_configs(args, rank, world, local_rank):
     g = torch.Generator(device=dev)
     g.manual_seed(99 + rank)
 
-    # C1: fp32 GEMM 1024^3 (replicas)
+    want = {c.strip().lower() for c in args.configs.split(",") if c.strip()}
+    if "c1" in want:
+        out.update(_config_c1(cx, dev, g, steps, world))
+    if "c3" in want:
+        out.update(_config_c3(cx, sharding, dev, g, steps, rank, world, bf16_peak, peak_src))
+    if "c4" in want:
+        out.update(_config_c4(cx, sharding, dev, g, steps, rank, world, hbm))
+    if "c5" in want:
+        out.update(_config_c5(cx, sharding, dev, g, steps, rank, world, bf16_peak))
+    return out
+
+
+def _config_c1(cx, dev, g, steps, world):
+    """fp32 GEMM 1024^3 (replicas)."""
+    import torch
+
     n = 1024
     A = torch.rand(n, n, device=dev, generator=g) * 2 - 1
     B = torch.rand(n, n, device=dev, generator=g) * 2 - 1
     C = torch.empty(n, n, device=dev)
     ms = time_graph(lambda i: cx.gemm(A, B, C), steps * 4, 5, world)
     tf = 2 * n ** 3 / (ms * 1e-3) / 1e12
-    out["c1_fp32_gemm_1024"] = {"tflops_total": round(world * tf, 3), "ms": round(ms, 5), "kernel": cx.last_kernel(),
-                                "frac_fp32_simt_nominal": round(tf / FP32_SIMT_NOMINAL_TFLOPS, 4),
-                                "parallelism": f"replicas x{world}"}
-    del A, B, C
+    return {"c1_fp32_gemm_1024": {"tflops_total": round(world * tf, 3), "ms": round(ms, 5),
+                                  "kernel": cx.last_kernel(),
+                                  "frac_fp32_simt_nominal": round(tf / FP32_SIMT_NOMINAL_TFLOPS, 4),
+                                  "parallelism": f"replicas x{world}"}}
 
-    # C3: fp16 GEMM 8192^3, N-sharded with all-gather when world > 1
+
+def _sharded_gemm(cx, sharding, X, Wl, rank, world, steps, n_total):
+    """Column-sharded Y = X @ W with the full Y on every rank: the fused
+    peer-store GEMM (graph-replayed, cross-GPU barriers inside) and, for
+    comparison, GEMM + NCCL all-gather + gather kernel.  Returns
+    (ms fused, ms nccl, kernel name)."""
+    import torch
+    from cuop_b200 import peer
+
+    M = X.size(0)
+    pg = peer.PeerShardedGemm(Wl, rank, world, max_rows=M)
+    try:
+        ms_peer = time_graph(lambda i: pg.forward(X), steps, 3, world, align=lambda: peer.peer_barrier(pg.signals))
+        pg.forward(X)
+        kname = "gemm_tc2_256x256_peer"
+    finally:
+        torch.cuda.synchronize()
+        pg.close()
+    sg = sharding.ColumnShardedGemm(Wl, world)
+    Y = torch.empty(M, n_total, device=X.device, dtype=X.dtype)
+    ms_nccl = time_loop(lambda i: sg.forward(X, out=Y), steps, 3, world)
+    del Y
+    return ms_peer, ms_nccl, kname
+
+
+def _config_c3(cx, sharding, dev, g, steps, rank, world, bf16_peak, peak_src):
+    """fp16 GEMM 8192^3; N-sharded with an all-gather of C when world > 1."""
+    import torch
+
     n = 8192
     A = (torch.randn(n, n, device=dev, generator=g) / math.sqrt(n)).half()
     Wfull_cols = n // world
     Wl = (torch.randn(n, Wfull_cols, device=dev, generator=g) / math.sqrt(n)).half()
+    Cl = torch.empty(n, Wfull_cols, device=dev, dtype=torch.half)
+    ms_local = time_graph(lambda i: cx.gemm(A, Wl, Cl), steps, 3, world)
+    kname = cx.last_kernel()
+    del Cl
+    res = {}
     if world == 1:
-        C = torch.empty(n, n, device=dev, dtype=torch.half)
-        ms = time_graph(lambda i: cx.gemm(A, Wl, C), steps, 3, world)
-        kname = cx.last_kernel()
-        ms_local = ms
+        ms = ms_local
     else:
-        sg = sharding.ColumnShardedGemm(Wl, world)
-        Cfull = torch.empty(n, n, device=dev, dtype=torch.half)
-        ms = time_loop(lambda i: sg.forward(A, out=Cfull), steps, 3, world)
-        Cl = torch.empty(n, Wfull_cols, device=dev, dtype=torch.half)
-        ms_local = time_graph(lambda i: cx.gemm(A, Wl, Cl), steps, 3, world)
-        kname = cx.last_kernel()
+        ms, ms_nccl, kname = _sharded_gemm(cx, sharding, A, Wl, rank, world, steps, n)
+        res["nccl_allgather_path"] = {"ms": round(ms_nccl, 4),
+                                      "tflops_total": round(2 * n ** 3 / (ms_nccl * 1e-3) / 1e12, 1)}
     tf_local = 2 * n * n * Wfull_cols / (ms_local * 1e-3) / 1e12
-    out["c3_fp16_gemm_8192"] = {
+    res = {
         "tflops_total": round(2 * n ** 3 / (ms * 1e-3) / 1e12, 1), "ms": round(ms, 4), "kernel": kname,
         "gemm_only_tflops_per_gpu": round(tf_local, 1), "frac_gemm_only": round(tf_local / bf16_peak, 4),
         "peak_tflops": bf16_peak, "peak_source": f"{peak_src} bf16_tflops (burst)",
-        "parallelism": "single GPU" if world == 1 else f"N-sharded x{world} + NCCL all-gather (chunked overlap)"}
+        "parallelism": "single GPU" if world == 1 else
+        f"N-sharded x{world}; GEMM epilogue stores every tile into all ranks' outputs over NVLink", **res}
     del A, Wl
     torch.cuda.empty_cache()
+    return {"c3_fp16_gemm_8192": res}
 
-    # C4: bf16 batched 4096 x (128x128x64), batch-sharded, no collective
+
+def _config_c4(cx, sharding, dev, g, steps, rank, world, hbm):
+    """bf16 batched 4096 x (128x128x64), batch-sharded, no collective."""
+    import torch
+
     batch, M, N_, K = 4096, 128, 128, 64
     b0, b1 = sharding.shard_range(batch, rank, world)
     lb = b1 - b0
@@ -419,15 +474,20 @@ def run_configs(args, rank, world, local_rank):
     ms = time_graph(lambda i: cx.batched_gemm(As[i % sets], Bs[i % sets], Cs[i % sets]), steps * 4, 5, world)
     bytes_total = batch * (M * K + K * N_ + M * N_) * 2
     gbs_local = lb * (M * K + K * N_ + M * N_) * 2 / (ms * 1e-3) / 1e9
-    out["c4_bf16_batched_4096x128x128x64"] = {
+    res = {
         "gbs_total": round(bytes_total / (ms * 1e-3) / 1e9, 1), "ms": round(ms, 5), "kernel": cx.last_kernel(),
         "tflops_total": round(2 * batch * M * N_ * K / (ms * 1e-3) / 1e12, 2),
         "frac_hbm_per_gpu": round(gbs_local / hbm, 4), "l2": f"{sets} rotated input sets > L2",
         "parallelism": f"batch-sharded x{world}, no collective"}
     del As, Bs, Cs
     torch.cuda.empty_cache()
+    return {"c4_bf16_batched_4096x128x128x64": res}
 
-    # C5: bf16 linear 4096 x 8192 x 28672, W column-sharded, all-gather of Y
+
+def _config_c5(cx, sharding, dev, g, steps, rank, world, bf16_peak):
+    """bf16 linear 4096 x 8192 x 28672, W column-sharded, all-gather of Y."""
+    import torch
+
     M, K, N_ = 4096, 8192, 28672
     X = torch.randn(M, K, device=dev, generator=g).bfloat16()
     nl = N_ // world
@@ -435,18 +495,24 @@ def run_configs(args, rank, world, local_rank):
     Yl = torch.empty(M, nl, device=dev, dtype=torch.bfloat16)
     ms_local = time_graph(lambda i: cx.gemm(X, Wl, Yl), steps, 3, world)
     kname = cx.last_kernel()
+    del Yl
+    res = {}
     if world > 1:
-        sg = sharding.ColumnShardedGemm(Wl, world)
-        Y = torch.empty(M, N_, device=dev, dtype=torch.bfloat16)
-        ms = time_loop(lambda i: sg.forward(X, out=Y), steps, 3, world)
+        ms, ms_nccl, kname = _sharded_gemm(cx, sharding, X, Wl, rank, world, steps, N_)
+        res["nccl_allgather_path"] = {"ms": round(ms_nccl, 4),
+                                      "tflops_total": round(2 * M * K * N_ / (ms_nccl * 1e-3) / 1e12, 1)}
     else:
         ms = ms_local
     tf_local = 2 * M * K * nl / (ms_local * 1e-3) / 1e12
-    out["c5_bf16_linear_4096x8192x28672"] = {
+    res = {
         "tflops_total": round(2 * M * K * N_ / (ms * 1e-3) / 1e12, 1), "ms": round(ms, 4), "kernel": kname,
         "gemm_only_tflops_per_gpu": round(tf_local, 1), "frac_gemm_only": round(tf_local / bf16_peak, 4),
-        "parallelism": "single GPU" if world == 1 else f"W column-sharded x{world} + NCCL all-gather of Y"}
-    return out
+        "parallelism": "single GPU" if world == 1 else
+        f"W column-sharded x{world}; GEMM epilogue stores every tile of Y into all ranks' outputs over NVLink",
+        **res}
+    del X, Wl
+    torch.cuda.empty_cache()
+    return {"c5_bf16_linear_4096x8192x28672": res}
 
 
 # --------------------------------------------------------------------------- reference arm
@@ -506,6 +572,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-configs", action="store_true", help="skip the other GEMM configs")
+    ap.add_argument("--configs", default="c1,c3,c4,c5",
+                    help="comma-separated subset of the other configs to run (c1, c3, c4, c5)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)

@@ -33,6 +33,9 @@ STATUS_NAMES = {
 
 F32, F64, F16, BF16 = 0, 1, 2, 3
 FP32_AUTO, FP32_FFMA, FP32_TF32X3 = 0, 1, 2
+PEER_HANDLE_BYTES = 64
+PEER_SIGNAL_BYTES = 512
+DEVERR_PEER_TIMEOUT = 8
 
 _i64, _dbl, _vp, _sz, _int = C.c_int64, C.c_double, C.c_void_p, C.c_size_t, C.c_int
 _fp = C.c_void_p  # float* as raw address
@@ -53,6 +56,13 @@ SIGNATURES = [
     ("cuopx_gemv", _int, [_int, _int, _i64, _i64, _dbl, _vp, _i64, _vp, _dbl, _vp, _vp, _sz, _vp]),
     ("cuopx_gemv_noalloc", _int, [_int, _int, _i64, _i64, _dbl, _vp, _i64, _vp, _dbl, _vp, _vp]),
     ("cuopx_gather_column_blocks", _int, [_int, _i64, _i64, _i64, _vp, _vp, _i64, _vp]),
+    ("cuopx_peer_alloc", _int, [_sz, C.POINTER(_vp), _vp]),
+    ("cuopx_peer_open", _int, [_vp, C.POINTER(_vp)]),
+    ("cuopx_peer_close", _int, [_vp]),
+    ("cuopx_peer_free", _int, [_vp]),
+    ("cuopx_peer_barrier", _int, [C.POINTER(_vp), _int, _int, _vp]),
+    ("cuopx_gemm_allgather", _int,
+     [_int, _int, _int, _i64, _i64, _i64, _dbl, _vp, _i64, _vp, _i64, C.POINTER(_vp), _int, _int, _i64, _vp]),
     ("cuopx_vector_workspace_size", _sz, [_i64]),
     ("cuopx_dot", _int, [_i64, _fp, _i64, _fp, _i64, _fp, _vp, _sz, _vp]),
     ("cuopx_axpy", _int, [_i64, C.c_float, _fp, _i64, _fp, _i64, _vp]),

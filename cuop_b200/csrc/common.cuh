@@ -33,6 +33,7 @@ enum DeviceError : int {
   kDevErrWaitTimeoutStore = 5,     // bulk store drain took too long
   kDevErrSplitReduce = 6,          // split-K arrival counter out of range
   kDevErrAbortDrain = 7,           // in-flight TMA did not land during abort
+  kDevErrPeerTimeout = 8,          // a peer GPU did not reach the barrier
 };
 
 __device__ __forceinline__ void record_device_error(int code) {

@@ -8,5 +8,6 @@
 #include "gemm_simt.cu"
 #include "gemm_tc.cu"
 #include "gemm_tc2.cu"
+#include "peer.cu"
 #include "gemm_tf32x3.cu"
 #include "vector_ops.cu"

@@ -54,6 +54,9 @@ int gemm_tc(const GemmProblem& p, cudaStream_t stream);
 // Two-SM (cta_group::2) tcgen05 back-end (gemm_tc2.cu) for large fp16/bf16.
 bool gemm_tc2_wanted(const GemmProblem& p);
 int gemm_tc2(const GemmProblem& p, cudaStream_t stream);
+// Same kernel; every output chunk is also stored to peers[0..npeers) (peer
+// mappings of identically laid out outputs, offset to this block's columns).
+int gemm_tc2_peers(const GemmProblem& p, void* const* peers, int npeers, cudaStream_t stream);
 
 // 3xTF32 tcgen05 back-end (gemm_tf32x3.cu) for fp32.
 bool gemm_tf32x3_supported(const GemmProblem& p);

@@ -52,12 +52,18 @@ struct PairSmem {
   static_assert(ALLOC <= 232448, "shared memory budget exceeded");
 };
 
+constexpr int P_MAX_PEERS = 7;  // one node: up to 8 ranks
+
 struct PairParams {
   int M, N, K, batch;
   int tiles_m, tiles_n, num_tiles, k_blocks;  // tiles are 256 x 256 pair tiles
   float alpha, beta;
   const void* C_in;
   int64_t ldc, strideC;
+  // Peer-store all-gather: each staged output chunk is also written to
+  // peer_C[i] (same row stride ldc, same column offset) for i < npeers.
+  int npeers;
+  void* peer_C[P_MAX_PEERS];
 };
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -383,12 +389,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
           tma_store_3d(&tmC, sbase, n0 + ch * P_CHUNK, m0 + 32 * q, b);
           bulk_commit_group();
         }
+        if (p.npeers > 0) {
+          // Same 32 x 64 chunk to every peer's output: lanes 8r..8r+7 write
+          // the 128 contiguous bytes of one row, so each warp store is four
+          // full 128-byte lines over NVLink.  Rows past M and 16-byte
+          // column groups past N are skipped (N is a multiple of 8).
+          const int c16 = lane & 7;
+          const int64_t gcol = static_cast<int64_t>(n0) + ch * P_CHUNK + 8 * c16;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int r = 4 * i + (lane >> 3);
+            const int64_t grow_r = static_cast<int64_t>(m0) + 32 * q + r;
+            const uint4 w = *reinterpret_cast<const uint4*>(sbase + r * 128 + ((c16 ^ (r & 7)) << 4));
+            if (grow_r < p.M && gcol < p.N) {
+              const int64_t off = grow_r * p.ldc + gcol;
+#pragma unroll
+              for (int d = 0; d < P_MAX_PEERS; ++d)  // constant indices keep peer_C in the param bank
+                if (d < p.npeers) *reinterpret_cast<uint4*>(static_cast<T*>(p.peer_C[d]) + off) = w;
+            }
+          }
+        }
         sbuf ^= 1;
       }
       if (++acc == P_ACC_BUFS) acc = 0, acc_phase ^= 1u;
     }
     if (lane == 0) bulk_wait_group<0>();
     __syncwarp();
+    // Peer stores of this thread are ordered before anything the stream
+    // runs after the kernel (the peer barrier's release).
+    if (p.npeers > 0) __threadfence_system();
   }
 
   tc_fence_before_sync();
@@ -402,7 +431,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
 }
 
 template <typename T, bool A_MN, bool B_MN>
-int launch_tc2(const GemmProblem& p, cudaStream_t stream, const char* name) {
+int launch_tc2(const GemmProblem& p, cudaStream_t stream, const char* name, void* const* peers = nullptr,
+               int npeers = 0) {
   using L = PairSmem;
   const CUtensorMapDataType dt =
       std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -428,6 +458,9 @@ int launch_tc2(const GemmProblem& p, cudaStream_t stream, const char* name) {
   prm.C_in = p.C;
   prm.ldc = p.ldc;
   prm.strideC = p.strideC;
+  if (npeers < 0 || npeers > P_MAX_PEERS) return CUOPX_INVALID_ARGUMENT;
+  prm.npeers = npeers;
+  for (int i = 0; i < P_MAX_PEERS; ++i) prm.peer_C[i] = i < npeers ? peers[i] : nullptr;
   auto kern = gemm_tc2_kernel<T, A_MN, B_MN>;
   static bool attr_set[64] = {};
   int dev = 0;
@@ -453,18 +486,21 @@ bool gemm_tc2_wanted(const GemmProblem& p) {
   return p.M >= 256 && p.N >= 256 && p.K >= 256 && tiles >= device_sm_count() / 2;
 }
 
-int gemm_tc2(const GemmProblem& p, cudaStream_t stream) {
+int gemm_tc2(const GemmProblem& p, cudaStream_t stream) { return gemm_tc2_peers(p, nullptr, 0, stream); }
+
+int gemm_tc2_peers(const GemmProblem& p, void* const* peers, int npeers, cudaStream_t stream) {
   const bool a_mn = p.transA, b_mn = !p.transB;
+  const char* name = npeers > 0 ? "gemm_tc2_256x256_peer" : "gemm_tc2_256x256";
   if (p.dtype == CUOPX_BF16) {
-    if (!a_mn && b_mn) return launch_tc2<__nv_bfloat16, false, true>(p, stream, "gemm_tc2_256x256");
-    if (!a_mn && !b_mn) return launch_tc2<__nv_bfloat16, false, false>(p, stream, "gemm_tc2_256x256");
-    if (a_mn && b_mn) return launch_tc2<__nv_bfloat16, true, true>(p, stream, "gemm_tc2_256x256");
-    return launch_tc2<__nv_bfloat16, true, false>(p, stream, "gemm_tc2_256x256");
+    if (!a_mn && b_mn) return launch_tc2<__nv_bfloat16, false, true>(p, stream, name, peers, npeers);
+    if (!a_mn && !b_mn) return launch_tc2<__nv_bfloat16, false, false>(p, stream, name, peers, npeers);
+    if (a_mn && b_mn) return launch_tc2<__nv_bfloat16, true, true>(p, stream, name, peers, npeers);
+    return launch_tc2<__nv_bfloat16, true, false>(p, stream, name, peers, npeers);
   }
-  if (!a_mn && b_mn) return launch_tc2<__half, false, true>(p, stream, "gemm_tc2_256x256");
-  if (!a_mn && !b_mn) return launch_tc2<__half, false, false>(p, stream, "gemm_tc2_256x256");
-  if (a_mn && b_mn) return launch_tc2<__half, true, true>(p, stream, "gemm_tc2_256x256");
-  return launch_tc2<__half, true, false>(p, stream, "gemm_tc2_256x256");
+  if (!a_mn && b_mn) return launch_tc2<__half, false, true>(p, stream, name, peers, npeers);
+  if (!a_mn && !b_mn) return launch_tc2<__half, false, false>(p, stream, name, peers, npeers);
+  if (a_mn && b_mn) return launch_tc2<__half, true, true>(p, stream, name, peers, npeers);
+  return launch_tc2<__half, true, false>(p, stream, name, peers, npeers);
 }
 
 }  // namespace cuopx

@@ -5,8 +5,9 @@
  * pointer, every size is int64_t, every call is asynchronous on the given
  * cudaStream_t (passed as void*, NULL = legacy default stream) and returns
  * a cuOP StatusCode integer (same numeric values as the reference's
- * `enum class StatusCode`, include/util/status_code.hpp:28-161).  No call
- * allocates device memory; scratch is passed in by the caller.
+ * `enum class StatusCode`, include/util/status_code.hpp:28-161).  No compute
+ * call allocates device memory (scratch is passed in by the caller); only
+ * the set-up call cuopx_peer_alloc does.
  *
  * Layout convention: row-major, like the reference operators
  * (src/cuda_op/detail/cuBlas/gemm.cu:14-42, gemv.cu:10-23).
@@ -141,6 +142,62 @@ int cuopx_gemv_noalloc(int dtype, int trans, int64_t M, int64_t N, double alpha,
  */
 int cuopx_gather_column_blocks(int dtype, int64_t G, int64_t M, int64_t Nb, const void* blocks, void* out,
                                int64_t ldo, void* stream);
+
+/*
+ * Peer memory for the fused column-sharded GEMM (one process per GPU, GPUs
+ * of one NVLink/NVSwitch node).  No reference counterpart: the reference is
+ * single-GPU.
+ *
+ * cuopx_peer_alloc   device allocation on the current GPU, zero-filled, plus
+ *                    an opaque CUOPX_PEER_HANDLE_BYTES handle that another
+ *                    process passes to cuopx_peer_open to map it.  A set-up
+ *                    call: it allocates, the compute entry points never do.
+ * cuopx_peer_open    maps a peer's allocation into this process (peer access
+ *                    over NVLink); cuopx_peer_close unmaps it.
+ * cuopx_peer_free    releases an allocation made by cuopx_peer_alloc (after
+ *                    every peer has closed it).
+ */
+#define CUOPX_PEER_HANDLE_BYTES 64
+int cuopx_peer_alloc(size_t bytes, void** ptr, void* handle_out);
+int cuopx_peer_open(const void* handle, void** ptr);
+int cuopx_peer_close(void* ptr);
+int cuopx_peer_free(void* ptr);
+
+/*
+ * Cross-GPU barrier on `stream`: signals[r] is rank r's signal block (a
+ * cuopx_peer_alloc block of at least CUOPX_PEER_SIGNAL_BYTES, mapped in this
+ * process).  Every rank posts an epoch into each rank's block with a
+ * system-scope release, then waits (acquire) until all `world` ranks have
+ * posted, so that device writes a rank made on its stream before the barrier
+ * are visible to every rank's stream after it.  The epoch counter lives in
+ * the local block, so the call can be captured in a CUDA graph.  A wait that
+ * exceeds 5 s records CUOPX_DEVERR_PEER_TIMEOUT in the device error word and
+ * returns.  No reference counterpart.
+ */
+#define CUOPX_PEER_SIGNAL_BYTES 512
+#define CUOPX_DEVERR_PEER_TIMEOUT 8
+int cuopx_peer_barrier(void* const* signals, int world, int rank, void* stream);
+
+/*
+ * Column-sharded GEMM fused with the all-gather of its output: this rank
+ * holds B_local = W[:, rank*N_local : (rank+1)*N_local] and computes
+ * C_block = alpha * op(A) * B_local; every output tile is written, from the
+ * epilogue, into the column block [rank*N_local, (rank+1)*N_local) of every
+ * rank's full output C_ranks[r] (row-major [M][world*N_local], leading
+ * dimension ldc, identical layout on every rank; C_ranks[rank] is local, the
+ * others peer mappings).  Stores to peers are plain global stores over
+ * NVLink, overlapped with the next tile's MMAs; no collective library call.
+ * The caller brackets the call with cuopx_peer_barrier (before: peers are
+ * done reading their outputs; after: all blocks have landed).
+ * fp16/bf16 only, M, N_local, K >= 256, N_local and ldc multiples of 8;
+ * other problems return CUOPX_NOT_IMPLEMENTED (the caller then uses
+ * cuopx_gemm + an all-gather + cuopx_gather_column_blocks).
+ * Replaces, for the multi-GPU case, Gemm<T>::Forward
+ * (src/cuda_op/detail/cuBlas/gemm.cu:417-511) followed by an all-gather.
+ */
+int cuopx_gemm_allgather(int dtype, int transA, int transB, int64_t M, int64_t N_local, int64_t K, double alpha,
+                         const void* A, int64_t lda, const void* B, int64_t ldb, void* const* C_ranks, int world,
+                         int rank, int64_t ldc, void* stream);
 
 /*
  * Level-1 vector operations (fp32), replacing VectorOpsJITPlugin::Execute
