@@ -34,6 +34,7 @@ enum DeviceError : int {
   kDevErrSplitReduce = 6,          // split-K arrival counter out of range
   kDevErrAbortDrain = 7,           // in-flight TMA did not land during abort
   kDevErrPeerTimeout = 8,          // a peer GPU did not reach the barrier
+  kDevErrSchedule = 9,             // launch-control answer outside the grid
 };
 
 __device__ __forceinline__ void record_device_error(int code) {
@@ -82,6 +83,36 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
   asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
                "r"(bytes)
                : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Cluster launch control (sm_100): a running CTA asks the hardware to cancel
+// a CTA of the same grid that has not been launched yet and takes over its
+// work.  The 16-byte response lands in shared memory and completes 16 bytes
+// on `bar` (the issuing thread posts expect_tx(16) first).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void clc_try_cancel(void* resp, uint64_t* bar) {
+  asm volatile("clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 [%0], [%1];" ::"r"(
+                   smem_u32(resp)),
+               "r"(smem_u32(bar))
+               : "memory");
+}
+
+// Decode a completed response: true and the cancelled CTA's blockIdx.x, or
+// false when no unlaunched CTA was left.
+__device__ __forceinline__ bool clc_query(const void* resp, int& ctaid_x) {
+  uint32_t canceled, x;
+  asm volatile(
+      "{\n\t.reg .b128 r;\n\t.reg .pred p;\n\t"
+      "ld.shared.b128 r, [%2];\n\t"
+      "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, r;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t"
+      "clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %1, r;\n\t}"
+      : "=r"(canceled), "=r"(x)
+      : "r"(smem_u32(resp))
+      : "memory");
+  ctaid_x = static_cast<int>(x);
+  return canceled != 0;
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {

@@ -1,7 +1,15 @@
 // tcgen05 / TMEM / TMA GEMM for fp16 and bf16 inputs (fp32 accumulate),
 // plain and strided-batched, any transpose combination.
 //
-// One persistent CTA per SM, 6 warps, warp-specialised:
+// The grid has one CTA per output tile, but a CTA does not stop after its
+// own tile: before finishing a tile it asks the hardware (cluster launch
+// control, clusterlaunchcontrol.try_cancel) to cancel a CTA that has not been
+// launched yet and takes over that CTA's tile.  The first wave of CTAs (one
+// per SM) therefore runs persistently, and an SM that is fast takes more
+// tiles than one that is slow, with no tile counter in global memory.
+// Every role of the CTA reads the same responses from a shared-memory ring,
+// so producer, MMA issuer and epilogue walk the same tile sequence.
+// 6 warps, warp-specialised:
 //   warp 0      TMA producer: K-blocks of A (128 x 64) and B (BN x 64) into a
 //               STAGES-deep shared-memory ring (128-byte swizzle), one
 //               mbarrier pair (full/empty) per stage.
@@ -40,6 +48,11 @@ constexpr int EPI_WARPS = 4;
 constexpr int STAGE_CHUNK_COLS = 64;  // epilogue column chunk (one TMA store box)
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int GROUP_M = 16;  // raster: walk 16 M-tiles per N step for L2 reuse
+// Scheduler ring depth: more than the producer's lead over the epilogue
+// (STAGES + accumulator buffers, in tiles), so the producer never waits on it.
+constexpr int CLC_SLOTS = 16;
+// Arrivals that free a scheduler slot: producer, MMA issuer, epilogue warps.
+constexpr int CLC_READERS = 2 + EPI_WARPS;
 
 struct TcParams {
   int M, N, K, batch;
@@ -61,7 +74,11 @@ struct SmemLayout {
   static constexpr int OFF_BAR = OFF_C + EPI_WARPS * 2 * C_STAGE;
   // full[STAGES], empty[STAGES], acc_full[ACC_BUFS], acc_empty[ACC_BUFS], drain
   static constexpr int NUM_BARS = 2 * STAGES + 2 * ACC_BUFS + 1;
-  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  // Tile-scheduler ring: CLC_SLOTS 16-byte launch-control responses, then
+  // clc_full[CLC_SLOTS] and clc_empty[CLC_SLOTS] mbarriers.
+  static constexpr int OFF_CLC = (OFF_BAR + NUM_BARS * 8 + 15) / 16 * 16;
+  static constexpr int OFF_CLC_BAR = OFF_CLC + CLC_SLOTS * 16;
+  static constexpr int OFF_MISC = OFF_CLC_BAR + 2 * CLC_SLOTS * 8;
   static constexpr int BYTES = OFF_MISC + 16;
   static constexpr int ALLOC = BYTES + 1024;  // slack for 1024-byte alignment
   static_assert(ALLOC <= 232448, "shared memory budget exceeded");
@@ -78,6 +95,17 @@ __device__ __forceinline__ void tile_coords(int t, const TcParams& p, int& b, in
   const int rr = r - g * span;
   mt = first_m + rr % gsize;
   nt = rr / gsize;
+}
+
+// Next tile from a completed launch-control response; false when the grid
+// has no unlaunched CTA left (or, defensively, the answer is out of range).
+__device__ __forceinline__ bool clc_next_tile(const void* resp, int num_tiles, int& next) {
+  if (!clc_query(resp, next)) return false;
+  if (next < 0 || next >= num_tiles) {
+    record_device_error(kDevErrSchedule);
+    return false;
+  }
+  return true;
 }
 
 template <typename T>
@@ -112,6 +140,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* acc_full = bars + 2 * STAGES;
   uint64_t* acc_empty = bars + 2 * STAGES + ACC_BUFS;
   uint64_t* drain = bars + 2 * STAGES + 2 * ACC_BUFS;
+  unsigned char* clc_resp = smem + L::OFF_CLC;
+  uint64_t* clc_full = reinterpret_cast<uint64_t*>(smem + L::OFF_CLC_BAR);
+  uint64_t* clc_empty = clc_full + CLC_SLOTS;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
 
@@ -126,6 +157,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int a = 0; a < ACC_BUFS; ++a) {
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], EPI_WARPS);
+    }
+    for (int c = 0; c < CLC_SLOTS; ++c) {
+      mbar_init(&clc_full[c], 1);
+      mbar_init(&clc_empty[c], CLC_READERS);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -152,7 +187,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t last_phase[STAGES];
       for (int s = 0; s < STAGES; ++s) issued_any[s] = false, last_phase[s] = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      bool clc_pending = false;
+      int cs = 0;
+      uint32_t cpar = 0;
+      int t = blockIdx.x;
+      for (int seq = 0; ok; ++seq) {
+        // Ask for the tile after this one now, so the answer is in by the
+        // time this tile's loads are issued.
+        cs = seq % CLC_SLOTS;
+        cpar = static_cast<uint32_t>(seq / CLC_SLOTS) & 1u;
+        if (!mbar_wait_bounded(&clc_empty[cs], cpar ^ 1u, kDevErrWaitTimeoutEmpty, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&clc_full[cs], 16);
+        clc_try_cancel(clc_resp + cs * 16, &clc_full[cs]);
+        clc_pending = true;
         int b, mt, nt;
         tile_coords(t, p, b, mt, nt);
         const int m0 = mt * BM, n0 = nt * BN;
@@ -181,14 +231,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           last_phase[stage] = phase;
           if (++stage == STAGES) stage = 0, phase ^= 1u;
         }
+        if (!ok) break;
+        if (!mbar_wait_bounded(&clc_full[cs], cpar, kDevErrWaitTimeoutFull, abort_flag)) {
+          ok = false;
+          break;
+        }
+        clc_pending = false;
+        int next = 0;
+        const bool more = clc_next_tile(clc_resp + cs * 16, p.num_tiles, next);
+        mbar_arrive(&clc_empty[cs]);
+        if (!more) break;
+        t = next;
       }
       if (!ok) {
-        // Abort: let every load already issued land before the CTA exits.
+        // Abort: let every load already issued, and the outstanding
+        // launch-control response, land before the CTA exits.
         for (int s = 0; s < STAGES; ++s) {
           if (!issued_any[s]) continue;
           const uint32_t addr = smem_u32(&full[s]);
           const unsigned long long t0 = global_timer_ns();
           while (!mbar_try_wait(addr, last_phase[s])) {
+            if (global_timer_ns() - t0 > kWaitLimitNs) {
+              record_device_error(kDevErrAbortDrain);
+              break;
+            }
+          }
+        }
+        if (clc_pending) {
+          const uint32_t addr = smem_u32(&clc_full[cs]);
+          const unsigned long long t0 = global_timer_ns();
+          while (!mbar_try_wait(addr, cpar)) {
             if (global_timer_ns() - t0 > kWaitLimitNs) {
               record_device_error(kDevErrAbortDrain);
               break;
@@ -206,7 +278,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       bool issued = false;
-      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      for (int seq = 0; ok; ++seq) {
         if (!mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1u, kDevErrWaitTimeoutAccEmpty, abort_flag)) {
           ok = false;
           break;
@@ -238,6 +310,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (!ok) break;
         umma_commit(&acc_full[acc]);  // accumulator complete
         if (++acc == ACC_BUFS) acc = 0, acc_phase ^= 1u;
+        const int cs = seq % CLC_SLOTS;
+        if (!mbar_wait_bounded(&clc_full[cs], static_cast<uint32_t>(seq / CLC_SLOTS) & 1u, kDevErrWaitTimeoutFull,
+                               abort_flag))
+          break;
+        int next = 0;
+        const bool more = clc_next_tile(clc_resp + cs * 16, p.num_tiles, next);
+        mbar_arrive(&clc_empty[cs]);
+        if (!more) break;
       }
       if (!ok && issued) {
         // Abort: make sure no MMA is still writing TMEM before dealloc.
@@ -262,7 +342,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint32_t acc_phase = 0;
     int sbuf = 0;
     const T* Cin = static_cast<const T*>(p.C_in);
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+    int t = blockIdx.x;
+    for (int seq = 0;; ++seq) {
       int b, mt, nt;
       tile_coords(t, p, b, mt, nt);
       const int m0 = mt * BM, n0 = nt * BN;
@@ -319,6 +400,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         sbuf ^= 1;
       }
       if (++acc == ACC_BUFS) acc = 0, acc_phase ^= 1u;
+      const int cs = seq % CLC_SLOTS;
+      if (!mbar_wait_bounded(&clc_full[cs], static_cast<uint32_t>(seq / CLC_SLOTS) & 1u, kDevErrWaitTimeoutAccFull,
+                             abort_flag))
+        break;
+      int next = 0;
+      const bool more = clc_next_tile(clc_resp + cs * 16, p.num_tiles, next);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&clc_empty[cs]);
+      if (!more) break;
+      t = next;
     }
     if (lane == 0) bulk_wait_group<0>();
     __syncwarp();
@@ -417,8 +508,8 @@ int launch_tc(const GemmProblem& p, cudaStream_t stream, const char* name) {
       return CUOPX_CUDA_ERROR;
     attr_set[dev] = true;
   }
-  const int grid = std::min(prm.num_tiles, device_sm_count());
-  kern<<<grid, NUM_THREADS, L::ALLOC, stream>>>(mA, mB, mC, prm);
+  // One CTA per tile; running CTAs take over unlaunched ones' tiles.
+  kern<<<prm.num_tiles, NUM_THREADS, L::ALLOC, stream>>>(mA, mB, mC, prm);
   note_launch(name);
   return check_launch();
 }
