@@ -17,6 +17,13 @@
 //               in BOTH CTAs (tcgen05.commit multicast).
 //   warps 2..5  epilogue (both CTAs): own TMEM rows -> alpha/beta -> swizzled
 //               staging -> TMA store; then arrive on the leader's `acc_empty`.
+// Tile scheduling: one cluster per pair tile is launched; the leader asks the
+// hardware (clusterlaunchcontrol.try_cancel, answer in its own shared
+// memory) to cancel a cluster that has not been launched yet and takes over
+// its tile, then forwards the answer into the partner CTA's ring slot with a
+// shared::cluster store and a remote release-arrive.  Every role of both
+// CTAs walks the same tile sequence; the partner's roles release a slot by
+// arriving on the leader's clc_empty barrier.
 // No TMA multicast: every CTA loads its own halves.  Cluster barriers bracket
 // the kernel so no CTA exits while its peer may still touch its shared memory.
 #include "common.cuh"
@@ -36,6 +43,11 @@ constexpr int P_CHUNK = 64;
 constexpr uint32_t P_TMEM_COLS = 512;
 constexpr int P_ACC_BUFS = 2;
 constexpr int P_GROUP_M = 8;  // pair-row tiles per raster group
+// Scheduler ring depth (> the producers' lead over the epilogue, in tiles).
+constexpr int P_CLC_SLOTS = 16;
+// Arrivals on the leader's clc_empty per slot: leader producer, MMA issuer and
+// epilogue warps, plus the partner's producer and epilogue warps (remote).
+constexpr int P_CLC_READERS = (2 + P_EPI_WARPS) + (1 + P_EPI_WARPS);
 
 struct PairSmem {
   static constexpr int A_STAGE = P_BM * P_BK * 2;            // 16 KB
@@ -47,7 +59,11 @@ struct PairSmem {
   static constexpr int OFF_BAR = OFF_C + P_EPI_WARPS * 2 * C_STAGE;
   // full[S], empty[S], acc_full[2], acc_empty[2], drain
   static constexpr int NUM_BARS = 2 * P_STAGES + 2 * P_ACC_BUFS + 1;
-  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  // Tile-scheduler ring: P_CLC_SLOTS 16-byte launch-control responses, then
+  // clc_full[P_CLC_SLOTS] and clc_empty[P_CLC_SLOTS] mbarriers.
+  static constexpr int OFF_CLC = (OFF_BAR + NUM_BARS * 8 + 15) / 16 * 16;
+  static constexpr int OFF_CLC_BAR = OFF_CLC + P_CLC_SLOTS * 16;
+  static constexpr int OFF_MISC = OFF_CLC_BAR + 2 * P_CLC_SLOTS * 8;
   static constexpr int ALLOC = OFF_MISC + 16 + 1024;
   static_assert(ALLOC <= 232448, "shared memory budget exceeded");
 };
@@ -78,12 +94,6 @@ __device__ __forceinline__ uint32_t cluster_id_x() {
   return r;
 }
 
-__device__ __forceinline__ uint32_t nclusters_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
-  return r;
-}
-
 // shared::cluster address of the same shared variable in CTA `rank`.
 __device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
   uint32_t out;
@@ -93,6 +103,52 @@ __device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
 
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Bounded wait with cluster-scope acquire (data written by the partner CTA
+// before its release-arrive is visible afterwards).
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t* bar, uint32_t parity, int err,
+                                                          volatile int* abort) {
+  const uint32_t addr = smem_u32(bar);
+  const unsigned long long t0 = global_timer_ns();
+  for (uint32_t it = 0;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred P1;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P1, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, P1;\n\t}"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((it & 255u) == 255u) {
+      if (*abort) return false;
+      if (global_timer_ns() - t0 > kWaitLimitNs) {
+        record_device_error(err);
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, uint4 v) {
+  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+
+// Next pair tile from a completed launch-control response (the cancelled
+// cluster's first CTA index / 2); false when none was left.
+__device__ __forceinline__ bool clc_next_pair_tile(const void* resp, int num_tiles, int& next) {
+  int ctaid = 0;
+  if (!clc_query(resp, ctaid)) return false;
+  next = ctaid >> 1;
+  if (ctaid < 0 || next >= num_tiles) {
+    record_device_error(kDevErrSchedule);
+    return false;
+  }
+  return true;
 }
 
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
@@ -174,6 +230,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
   uint64_t* acc_full = bars + 2 * P_STAGES;
   uint64_t* acc_empty = bars + 2 * P_STAGES + P_ACC_BUFS;
   uint64_t* drain = bars + 2 * P_STAGES + 2 * P_ACC_BUFS;
+  unsigned char* clc_resp = smem + L::OFF_CLC;
+  uint64_t* clc_full = reinterpret_cast<uint64_t*>(smem + L::OFF_CLC_BAR);
+  uint64_t* clc_empty = clc_full + P_CLC_SLOTS;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
 
@@ -182,7 +241,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int pair = static_cast<int>(cluster_id_x());
-  const int npairs = static_cast<int>(nclusters_x());
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < P_STAGES; ++s) {
@@ -192,6 +250,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     for (int a = 0; a < P_ACC_BUFS; ++a) {
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], 2 * P_EPI_WARPS);  // leader's copy: 4 local + 4 remote arrivals
+    }
+    for (int c = 0; c < P_CLC_SLOTS; ++c) {
+      mbar_init(&clc_full[c], 1);  // leader: its expect_tx; partner: the leader's forward
+      mbar_init(&clc_empty[c], P_CLC_READERS);  // used on the leader only
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -221,7 +283,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
       bool issued_any[P_STAGES];
       uint32_t last_phase[P_STAGES];
       for (int s = 0; s < P_STAGES; ++s) issued_any[s] = false, last_phase[s] = 0;
-      for (int t = pair; t < p.num_tiles && ok; t += npairs) {
+      bool clc_pending = false;
+      int cs = 0;
+      uint32_t cpar = 0;
+      int t = pair;
+      for (int seq = 0; ok; ++seq) {
+        cs = seq % P_CLC_SLOTS;
+        cpar = static_cast<uint32_t>(seq / P_CLC_SLOTS) & 1u;
+        if (leader) {
+          // Ask for the pair tile after this one (answer by the end of it).
+          if (!mbar_wait_bounded(&clc_empty[cs], cpar ^ 1u, kDevErrWaitTimeoutEmpty, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&clc_full[cs], 16);
+          clc_try_cancel(clc_resp + cs * 16, &clc_full[cs]);
+          clc_pending = true;
+        }
         int b, mt, nt;
         pair_tile_coords(t, p, b, mt, nt);
         const int m0 = mt * 2 * P_BM + static_cast<int>(rank) * P_BM;
@@ -253,6 +331,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
           last_phase[stage] = phase;
           if (++stage == P_STAGES) stage = 0, phase ^= 1u;
         }
+        if (!ok) break;
+        int next = 0;
+        bool more;
+        if (leader) {
+          if (!mbar_wait_bounded(&clc_full[cs], cpar, kDevErrWaitTimeoutFull, abort_flag)) {
+            ok = false;
+            break;
+          }
+          clc_pending = false;
+          // Forward the answer to the partner's slot, then release it there.
+          const uint4 r = *reinterpret_cast<const uint4*>(clc_resp + cs * 16);
+          st_cluster_v4(map_to_rank(clc_resp + cs * 16, 1), r);
+          mbar_arrive_cluster(map_to_rank(&clc_full[cs], 1));
+          more = clc_next_pair_tile(clc_resp + cs * 16, p.num_tiles, next);
+          mbar_arrive(&clc_empty[cs]);
+        } else {
+          if (!mbar_wait_cluster_bounded(&clc_full[cs], cpar, kDevErrWaitTimeoutFull, abort_flag)) {
+            ok = false;
+            break;
+          }
+          more = clc_next_pair_tile(clc_resp + cs * 16, p.num_tiles, next);
+          mbar_arrive_cluster(map_to_rank(&clc_empty[cs], 0));
+        }
+        if (!more) break;
+        t = next;
       }
       if (ok) {
         // Tail: wait until the leader has released every stage, so no
@@ -263,12 +366,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
         }
       } else if (leader) {
         // Abort: let every phase this pair issued land (the leader's barrier
-        // counts both CTAs' bytes) before the cluster exits.
+        // counts both CTAs' bytes), and the outstanding launch-control
+        // answer, before the cluster exits.
         for (int s = 0; s < P_STAGES; ++s) {
           if (!issued_any[s]) continue;
           const uint32_t addr = smem_u32(&full[s]);
           const unsigned long long t0 = global_timer_ns();
           while (!mbar_try_wait(addr, last_phase[s])) {
+            if (global_timer_ns() - t0 > kWaitLimitNs) {
+              record_device_error(kDevErrAbortDrain);
+              break;
+            }
+          }
+        }
+        if (clc_pending) {
+          const uint32_t addr = smem_u32(&clc_full[cs]);
+          const unsigned long long t0 = global_timer_ns();
+          while (!mbar_try_wait(addr, cpar)) {
             if (global_timer_ns() - t0 > kWaitLimitNs) {
               record_device_error(kDevErrAbortDrain);
               break;
@@ -285,7 +399,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true, issued = false;
-      for (int t = pair; t < p.num_tiles && ok; t += npairs) {
+      for (int seq = 0; ok; ++seq) {
         if (!mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1u, kDevErrWaitTimeoutAccEmpty, abort_flag)) {
           ok = false;
           break;
@@ -315,6 +429,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
         if (!ok) break;
         umma_commit_pair(&acc_full[acc]);
         if (++acc == P_ACC_BUFS) acc = 0, acc_phase ^= 1u;
+        const int cs = seq % P_CLC_SLOTS;
+        if (!mbar_wait_bounded(&clc_full[cs], static_cast<uint32_t>(seq / P_CLC_SLOTS) & 1u, kDevErrWaitTimeoutFull,
+                               abort_flag))
+          break;
+        int next = 0;
+        const bool more = clc_next_pair_tile(clc_resp + cs * 16, p.num_tiles, next);
+        mbar_arrive(&clc_empty[cs]);
+        if (!more) break;
       }
       if (!ok && issued) {
         umma_commit_pair(drain);
@@ -338,7 +460,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     uint32_t acc_phase = 0;
     int sbuf = 0;
     const T* Cin = static_cast<const T*>(p.C_in);
-    for (int t = pair; t < p.num_tiles; t += npairs) {
+    int t = pair;
+    for (int seq = 0;; ++seq) {
       int b, mt, nt;
       pair_tile_coords(t, p, b, mt, nt);
       const int m0 = mt * 2 * P_BM + static_cast<int>(rank) * P_BM;
@@ -412,6 +535,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
         sbuf ^= 1;
       }
       if (++acc == P_ACC_BUFS) acc = 0, acc_phase ^= 1u;
+      const int cs = seq % P_CLC_SLOTS;
+      const uint32_t cpar = static_cast<uint32_t>(seq / P_CLC_SLOTS) & 1u;
+      const bool got = leader ? mbar_wait_bounded(&clc_full[cs], cpar, kDevErrWaitTimeoutAccFull, abort_flag)
+                              : mbar_wait_cluster_bounded(&clc_full[cs], cpar, kDevErrWaitTimeoutAccFull, abort_flag);
+      if (!got) break;
+      int next = 0;
+      const bool more = clc_next_pair_tile(clc_resp + cs * 16, p.num_tiles, next);
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(map_to_rank(&clc_empty[cs], 0));
+      if (!more) break;
+      t = next;
     }
     if (lane == 0) bulk_wait_group<0>();
     __syncwarp();
@@ -470,9 +604,8 @@ int launch_tc2(const GemmProblem& p, cudaStream_t stream, const char* name, void
       return CUOPX_CUDA_ERROR;
     attr_set[dev] = true;
   }
-  const int sms = device_sm_count() / 2 * 2;
-  const int grid = std::min(prm.num_tiles * 2, sms);  // even: whole clusters
-  kern<<<grid, P_THREADS, L::ALLOC, stream>>>(mA, mB, mC, prm);
+  // One cluster per pair tile; running clusters take over unlaunched ones.
+  kern<<<prm.num_tiles * 2, P_THREADS, L::ALLOC, stream>>>(mA, mB, mC, prm);
   note_launch(name);
   return check_launch();
 }
