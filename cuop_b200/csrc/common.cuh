@@ -54,6 +54,14 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// First 1024-byte boundary (swizzle-atom alignment) at or after `raw`, a
+// shared-memory array.  The offset is computed from the shared-window
+// address and added to the array pointer, so the compiler still knows the
+// result is shared memory and emits shared (not generic) loads and stores.
+__device__ __forceinline__ unsigned char* align_smem_1024(unsigned char* raw) {
+  return raw + ((1024u - (smem_u32(raw) & 1023u)) & 1023u);
+}
+
 __device__ __forceinline__ bool elect_one_sync() {
   uint32_t pred = 0;
   asm volatile(

@@ -132,8 +132,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   constexpr uint32_t IDESC = make_idesc(AB_FMT, A_MN, B_MN, BM, BN);
 
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  unsigned char* smem =
-      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* smem = align_smem_1024(smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
@@ -183,9 +182,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      bool issued_any[STAGES];
-      uint32_t last_phase[STAGES];
-      for (int s = 0; s < STAGES; ++s) issued_any[s] = false, last_phase[s] = 0;
+      // Abort bookkeeping, one bit per stage: loaded at least once, and the
+      // parity of the last phase loaded.
+      uint32_t issued_mask = 0, phase_mask = 0;
       bool ok = true;
       bool clc_pending = false;
       int cs = 0;
@@ -227,8 +226,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           } else {
             tma_load_3d(sb, &tmB, &full[stage], k0, n0, b);
           }
-          issued_any[stage] = true;
-          last_phase[stage] = phase;
+          issued_mask |= 1u << stage;
+          phase_mask = (phase_mask & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) stage = 0, phase ^= 1u;
         }
         if (!ok) break;
@@ -247,10 +246,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // Abort: let every load already issued, and the outstanding
         // launch-control response, land before the CTA exits.
         for (int s = 0; s < STAGES; ++s) {
-          if (!issued_any[s]) continue;
+          if (!((issued_mask >> s) & 1u)) continue;
           const uint32_t addr = smem_u32(&full[s]);
           const unsigned long long t0 = global_timer_ns();
-          while (!mbar_try_wait(addr, last_phase[s])) {
+          while (!mbar_try_wait(addr, (phase_mask >> s) & 1u)) {
             if (global_timer_ns() - t0 > kWaitLimitNs) {
               record_device_error(kDevErrAbortDrain);
               break;
@@ -336,8 +335,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row_in_tile = 32 * q + lane;
-    unsigned char* stage_buf[2] = {smem + L::OFF_C + ((warp - 2) * 2 + 0) * L::C_STAGE,
-                                   smem + L::OFF_C + ((warp - 2) * 2 + 1) * L::C_STAGE};
+    unsigned char* const stage_base = smem + L::OFF_C + (warp - 2) * 2 * L::C_STAGE;  // two buffers
     int acc = 0;
     uint32_t acc_phase = 0;
     int sbuf = 0;
@@ -381,7 +379,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // Stage 32 rows x 128 bytes, 128-byte swizzle (16-byte chunk j of row r at j ^ (r & 7)).
         if (lane == 0) bulk_wait_group_read<1>();
         __syncwarp();
-        unsigned char* sbase = stage_buf[sbuf];
+        unsigned char* sbase = stage_base + sbuf * L::C_STAGE;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           uint4 w;

@@ -119,8 +119,7 @@ __global__ void __launch_bounds__(X3_THREADS, 1)
   constexpr uint32_t CHUNK_BYTES = 32 * X3_BK * 4;  // one 32 x 32 fp32 box = 4 KB
 
   extern __shared__ __align__(1024) unsigned char x3_smem_raw[];
-  unsigned char* smem =
-      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(x3_smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* smem = align_smem_1024(x3_smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* full = bars;
   uint64_t* conv = bars + STAGES;
@@ -165,9 +164,9 @@ __global__ void __launch_bounds__(X3_THREADS, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      bool issued_any[STAGES];
-      uint32_t last_phase[STAGES];
-      for (int s = 0; s < STAGES; ++s) issued_any[s] = false, last_phase[s] = 0;
+      // Abort bookkeeping, one bit per stage: loaded at least once, and the
+      // parity of the last phase loaded.
+      uint32_t issued_mask = 0, phase_mask = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
         int b, mt, nt;
@@ -196,17 +195,17 @@ __global__ void __launch_bounds__(X3_THREADS, 1)
           } else {
             tma_load_3d(sb, &tmB, &full[stage], k0, n0, b);
           }
-          issued_any[stage] = true;
-          last_phase[stage] = phase;
+          issued_mask |= 1u << stage;
+          phase_mask = (phase_mask & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) stage = 0, phase ^= 1u;
         }
       }
       if (!ok) {
         for (int s = 0; s < STAGES; ++s) {
-          if (!issued_any[s]) continue;
+          if (!((issued_mask >> s) & 1u)) continue;
           const uint32_t addr = smem_u32(&full[s]);
           const unsigned long long t0 = global_timer_ns();
-          while (!mbar_try_wait(addr, last_phase[s])) {
+          while (!mbar_try_wait(addr, (phase_mask >> s) & 1u)) {
             if (global_timer_ns() - t0 > kWaitLimitNs) {
               record_device_error(kDevErrAbortDrain);
               break;
@@ -301,8 +300,7 @@ __global__ void __launch_bounds__(X3_THREADS, 1)
     // ------------------------------------------------------------ epilogue (warps 2..5)
     const int q = warp & 3;
     const int row_in_tile = 32 * q + lane;
-    unsigned char* stage_buf[2] = {smem + L::OFF_C + ((warp - 2) * 2 + 0) * L::C_STAGE,
-                                   smem + L::OFF_C + ((warp - 2) * 2 + 1) * L::C_STAGE};
+    unsigned char* const stage_base = smem + L::OFF_C + (warp - 2) * 2 * L::C_STAGE;  // two buffers
     int acc = 0;
     uint32_t acc_phase = 0;
     int sbuf = 0;
@@ -336,7 +334,7 @@ __global__ void __launch_bounds__(X3_THREADS, 1)
         }
         if (lane == 0) bulk_wait_group_read<1>();
         __syncwarp();
-        unsigned char* sbase = stage_buf[sbuf];
+        unsigned char* sbase = stage_base + sbuf * L::C_STAGE;
 #pragma unroll
         for (int j = 0; j < 8; ++j)
           *reinterpret_cast<float4*>(sbase + lane * 128 + ((j ^ (lane & 7)) << 4)) =
