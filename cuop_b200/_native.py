@@ -33,6 +33,7 @@ STATUS_NAMES = {
 
 F32, F64, F16, BF16 = 0, 1, 2, 3
 FP32_AUTO, FP32_FFMA, FP32_TF32X3 = 0, 1, 2
+EPI_NONE, EPI_BIAS, EPI_RELU = 0, 1, 2
 PEER_HANDLE_BYTES = 64
 PEER_SIGNAL_BYTES = 512
 DEVERR_PEER_TIMEOUT = 8
@@ -50,6 +51,8 @@ SIGNATURES = [
     ("cuopx_get_device_error", _int, [C.POINTER(_int)]),
     ("cuopx_clear_device_error", _int, []),
     ("cuopx_gemm", _int, [_int, _int, _int, _i64, _i64, _i64, _dbl, _vp, _i64, _vp, _i64, _dbl, _vp, _i64, _vp]),
+    ("cuopx_gemm_ex", _int,
+     [_int, _int, _int, _i64, _i64, _i64, _dbl, _vp, _i64, _vp, _i64, _dbl, _vp, _i64, _vp, _int, _vp]),
     ("cuopx_gemm_strided_batched", _int,
      [_int, _int, _int, _i64, _i64, _i64, _dbl, _vp, _i64, _i64, _vp, _i64, _i64, _dbl, _vp, _i64, _i64, _i64, _vp]),
     ("cuopx_gemv_workspace_size", _sz, [_int, _int, _i64, _i64]),

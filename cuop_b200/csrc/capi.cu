@@ -139,6 +139,23 @@ int cuopx_gemm(int dtype, int transA, int transB, int64_t M, int64_t N, int64_t 
   return gemm_route(p, static_cast<cudaStream_t>(stream));
 }
 
+int cuopx_gemm_ex(int dtype, int transA, int transB, int64_t M, int64_t N, int64_t K, double alpha, const void* A,
+                  int64_t lda, const void* B, int64_t ldb, double beta, void* C, int64_t ldc, const void* bias,
+                  int epilogue, void* stream) {
+  if (epilogue < 0 || epilogue > (CUOPX_EPI_BIAS | CUOPX_EPI_RELU)) return CUOPX_INVALID_ARGUMENT;
+  if ((epilogue & CUOPX_EPI_BIAS) && bias == nullptr && M > 0 && N > 0) return CUOPX_INVALID_ARGUMENT;
+  GemmProblem p{dtype, transA != 0, transB != 0, M, N, K, alpha, beta, A, lda, 0, B, ldb, 0, C, ldc, 0, 1};
+  p.bias = (epilogue & CUOPX_EPI_BIAS) ? bias : nullptr;
+  p.epi = epilogue;
+  const int v = validate_gemm(p);
+  if (v >= 0) return v;
+  if (epilogue & CUOPX_EPI_BIAS) {
+    const size_t es = dtype_size(dtype);
+    if (overlaps(C, span_bytes(M, N, ldc, es), bias, static_cast<size_t>(N) * es)) return CUOPX_INVALID_ARGUMENT;
+  }
+  return gemm_route(p, static_cast<cudaStream_t>(stream));
+}
+
 int cuopx_gemm_strided_batched(int dtype, int transA, int transB, int64_t M, int64_t N, int64_t K, double alpha,
                                const void* A, int64_t lda, int64_t strideA, const void* B, int64_t ldb,
                                int64_t strideB, double beta, void* C, int64_t ldc, int64_t strideC, int64_t batch,

@@ -350,4 +350,19 @@ __device__ __forceinline__ __nv_bfloat16 from_acc<__nv_bfloat16>(float v) {
   return __float2bfloat16_rn(v);
 }
 
+// Fused GEMM epilogue, applied to alpha*acc (+ beta*C) before the one
+// rounding to the output type: + bias[col] (rounded add, never contracted
+// with the product), then ReLU(x) = x if x > 0 else +0 (NaN -> +0).
+__device__ __forceinline__ float epi_add(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ double epi_add(double a, double b) { return __dadd_rn(a, b); }
+
+template <typename T>
+__device__ __forceinline__ typename AccOf<T>::type apply_epilogue(typename AccOf<T>::type v, const void* bias,
+                                                                  int64_t col, int epi) {
+  using Acc = typename AccOf<T>::type;
+  if (epi & CUOPX_EPI_BIAS) v = epi_add(v, to_acc<T>(static_cast<const T*>(bias)[col]));
+  if (epi & CUOPX_EPI_RELU) v = v > Acc(0) ? v : Acc(0);
+  return v;
+}
+
 }  // namespace cuopx

@@ -39,6 +39,10 @@ struct GemmProblem {
   void* C;
   int64_t ldc, strideC;
   int64_t batch;
+  // Fused epilogue (cuopx_gemm_ex): CUOPX_EPI_* flags; bias[N] of the
+  // problem's dtype when CUOPX_EPI_BIAS is set.
+  const void* bias = nullptr;
+  int epi = 0;
 };
 
 // SIMT back-ends (gemm_simt.cu): generic any-dtype/any-layout kernel and

@@ -10,7 +10,8 @@
 //   outputs per thread.
 //
 // Both accumulate every output as one fused-multiply-add chain over k in
-// ascending order, then apply C = alpha*acc (+ beta*C, unfused) — the
+// ascending order, then apply C = alpha*acc (+ beta*C, unfused; then the
+// optional bias add and ReLU of cuopx_gemm_ex) — the
 // reference kernels' summation order (src/cuda_op/detail/cuBlas/gemm.cu:23-41,
 // gemm.cu:264-291) — so fp32 results are reproducible bit for bit by a CPU
 // loop doing the same fmaf chain.
@@ -118,7 +119,7 @@ __global__ void __launch_bounds__(256) gemm_generic_kernel(GemmProblem p) {
         const int64_t gn = n0 + tx + 16 * j;
         if (gn >= p.N) continue;
         T* c = C + gm * p.ldc + gn;
-        *c = from_acc<T>(epilogue_value<T>(acc[i][j], alpha, beta, c));
+        *c = from_acc<T>(apply_epilogue<T>(epilogue_value<T>(acc[i][j], alpha, beta, c), p.bias, gn, p.epi));
       }
     }
   }
@@ -242,7 +243,9 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(GemmProblem p) {
         float4 out;
         float* o = &out.x;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) o[j] = epilogue_value<float>(acc[i][g * 4 + j], alpha, beta, c + j);
+        for (int j = 0; j < 4; ++j)
+          o[j] = apply_epilogue<float>(epilogue_value<float>(acc[i][g * 4 + j], alpha, beta, c + j), p.bias, gn + j,
+                                       p.epi);
         *reinterpret_cast<float4*>(c) = out;
       }
     }

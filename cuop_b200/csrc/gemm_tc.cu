@@ -60,6 +60,8 @@ struct TcParams {
   float alpha, beta;
   const void* C_in;  // read only when beta != 0
   int64_t ldc, strideC;
+  const void* bias;  // CUOPX_EPI_BIAS: N elements of the output type
+  int epi;           // CUOPX_EPI_* flags
 };
 
 template <int BN, int STAGES>
@@ -376,6 +378,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               if (gcol0 + i < p.N) v[i] = __fadd_rn(v[i], __fmul_rn(p.beta, to_acc<T>(crow[gcol0 + i])));
           }
         }
+        if (p.epi) {
+          const int64_t gcol0 = static_cast<int64_t>(n0) + ch * STAGE_CHUNK_COLS;
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (gcol0 + i < p.N) v[i] = apply_epilogue<T>(v[i], p.bias, gcol0 + i, p.epi);
+        }
         // Stage 32 rows x 128 bytes, 128-byte swizzle (16-byte chunk j of row r at j ^ (r & 7)).
         if (lane == 0) bulk_wait_group_read<1>();
         __syncwarp();
@@ -496,6 +504,8 @@ int launch_tc(const GemmProblem& p, cudaStream_t stream, const char* name) {
   prm.C_in = p.C;
   prm.ldc = p.ldc;
   prm.strideC = p.strideC;
+  prm.bias = p.bias;
+  prm.epi = p.epi;
 
   auto kern = gemm_tc_kernel<T, BN, STAGES, A_MN, B_MN>;
   static bool attr_set[64] = {};  // per instantiation and device

@@ -80,6 +80,8 @@ struct PairParams {
   // peer_C[i] (same row stride ldc, same column offset) for i < npeers.
   int npeers;
   void* peer_C[P_MAX_PEERS];
+  const void* bias;  // CUOPX_EPI_BIAS: N elements of the output type
+  int epi;           // CUOPX_EPI_* flags
 };
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -492,6 +494,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
           for (int i = 0; i < 64; ++i)
             if (gcol0 + i < p.N) v[i] = __fadd_rn(v[i], __fmul_rn(p.beta, to_acc<T>(crow[gcol0 + i])));
         }
+        if (p.epi) {
+          const int64_t gcol0 = static_cast<int64_t>(n0) + ch * P_CHUNK;
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (gcol0 + i < p.N) v[i] = apply_epilogue<T>(v[i], p.bias, gcol0 + i, p.epi);
+        }
         if (lane == 0) bulk_wait_group_read<1>();
         __syncwarp();
         unsigned char* sbase = stage_base + sbuf * L::C_STAGE;
@@ -590,6 +598,8 @@ int launch_tc2(const GemmProblem& p, cudaStream_t stream, const char* name, void
   prm.C_in = p.C;
   prm.ldc = p.ldc;
   prm.strideC = p.strideC;
+  prm.bias = p.bias;
+  prm.epi = p.epi;
   if (npeers < 0 || npeers > P_MAX_PEERS) return CUOPX_INVALID_ARGUMENT;
   prm.npeers = npeers;
   for (int i = 0; i < P_MAX_PEERS; ++i) prm.peer_C[i] = i < npeers ? peers[i] : nullptr;

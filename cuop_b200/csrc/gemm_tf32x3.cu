@@ -41,6 +41,8 @@ struct X3Params {
   float alpha, beta;
   const float* C_in;
   int64_t ldc, strideC;
+  const void* bias;  // CUOPX_EPI_BIAS: N elements of the output type
+  int epi;           // CUOPX_EPI_* flags
 };
 
 template <int BN, int STAGES>
@@ -332,6 +334,12 @@ __global__ void __launch_bounds__(X3_THREADS, 1)
           for (int i = 0; i < 32; ++i)
             if (gcol0 + i < p.N) v[i] = __fadd_rn(v[i], __fmul_rn(p.beta, crow[gcol0 + i]));
         }
+        if (p.epi) {
+          const int64_t gcol0 = static_cast<int64_t>(n0) + ch * X3_CHUNK;
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (gcol0 + i < p.N) v[i] = apply_epilogue<float>(v[i], p.bias, gcol0 + i, p.epi);
+        }
         if (lane == 0) bulk_wait_group_read<1>();
         __syncwarp();
         unsigned char* sbase = stage_base + sbuf * L::C_STAGE;
@@ -388,6 +396,8 @@ int launch_x3(const GemmProblem& p, cudaStream_t stream, const char* name) {
   prm.C_in = static_cast<const float*>(p.C);
   prm.ldc = p.ldc;
   prm.strideC = p.strideC;
+  prm.bias = p.bias;
+  prm.epi = p.epi;
   auto kern = gemm_tf32x3_kernel<BN, STAGES, A_MN, B_MN>;
   static bool attr_set[64] = {};
   int dev = 0;

@@ -5,13 +5,22 @@
 //   BatchMatMul<T>::Forward reference src/cuda_op/detail/cuDNN/batchmatmul.cu:52-94
 //   MatMul<T>::Forward     reference src/cuda_op/detail/cuDNN/matmul.cu:75-158
 //   GemmBatched<T>::Forward (plugin semantics, gemm_batched_jit_plugin.cu:113-188)
+//   MatMulReluFused<T>::Forward reference src/cuda_op/detail/cuDNN/kernel_fusion.cu:330-370
+//   Dot/Axpy/Scal/Copy      reference src/cuda_op/detail/cuBlas/{dot,axpy,scal,copy}.cu
+#include <type_traits>
+
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include "cuda_op/detail/cuBlas/axpy.hpp"
+#include "cuda_op/detail/cuBlas/copy.hpp"
+#include "cuda_op/detail/cuBlas/dot.hpp"
 #include "cuda_op/detail/cuBlas/gemm.hpp"
 #include "cuda_op/detail/cuBlas/gemm_batched.hpp"
 #include "cuda_op/detail/cuBlas/gemv.hpp"
+#include "cuda_op/detail/cuBlas/scal.hpp"
 #include "cuda_op/detail/cuDNN/batchmatmul.hpp"
+#include "cuda_op/detail/cuDNN/kernel_fusion.hpp"
 #include "cuda_op/detail/cuDNN/matmul.hpp"
 #include "cuopx.h"
 
@@ -163,12 +172,109 @@ StatusCode MatMul<T>::Forward(const Tensor<T>& A, const Tensor<T>& B, Tensor<T>&
   return cudaDeviceSynchronize() == cudaSuccess ? StatusCode::SUCCESS : StatusCode::CUDA_ERROR;
 }
 
+// ----------------------------------------------------------------- MatMulReluFused
+template <typename T>
+void MatMulReluFused<T>::SetWeight(const Tensor<T>& weight) {
+  copy_weight(weight_, weight);
+}
+
+template <typename T>
+void MatMulReluFused<T>::SetBias(const Tensor<T>& bias) {
+  copy_weight(bias_, bias);
+}
+
+template <typename T>
+StatusCode MatMulReluFused<T>::Forward(const std::vector<Tensor<T>*>& inputs, std::vector<Tensor<T>*>& outputs) {
+  if (inputs.size() != 1 || outputs.size() != 1 || !inputs[0] || !outputs[0]) return StatusCode::SHAPE_MISMATCH;
+  const Tensor<T>& input = *inputs[0];
+  Tensor<T>& output = *outputs[0];
+  const auto& a = input.shape();
+  const auto& w = weight_.shape();
+  if (a.size() != 2 || w.size() != 2) return StatusCode::TENSOR_DIMONSION_MISMATCH;
+  const int64_t M = static_cast<int64_t>(transA_ ? a[1] : a[0]);
+  const int64_t K = static_cast<int64_t>(transA_ ? a[0] : a[1]);
+  const int64_t Kw = static_cast<int64_t>(transB_ ? w[1] : w[0]);
+  const int64_t N = static_cast<int64_t>(transB_ ? w[0] : w[1]);
+  if (Kw != K) return StatusCode::SHAPE_MISMATCH;
+  output.resize({static_cast<std::size_t>(M), static_cast<std::size_t>(N)});
+  // As in the reference, a bias is used only when it has N elements.
+  const bool has_bias = bias_.numel() == static_cast<std::size_t>(N) && N > 0;
+  const int epi = CUOPX_EPI_RELU | (has_bias ? CUOPX_EPI_BIAS : 0);
+  const int rc = cuopx_gemm_ex(dtype_of<T>(), transA_, transB_, M, N, K, 1.0, input.data(),
+                               static_cast<int64_t>(a[1]), weight_.data(), static_cast<int64_t>(w[1]), 0.0,
+                               output.data(), N, has_bias ? bias_.data() : nullptr, epi, stream_);
+  if (rc != CUOPX_SUCCESS) return to_status(rc);
+  return cudaStreamSynchronize(stream_) == cudaSuccess ? StatusCode::SUCCESS : StatusCode::CUDA_ERROR;
+}
+
+// ----------------------------------------------------------------- vector operators (fp32)
+template <typename T>
+StatusCode Dot<T>::Forward(const Tensor<T>& x, const Tensor<T>& y, T& result) {
+  if (x.numel() != y.numel()) return StatusCode::SHAPE_MISMATCH;
+  if constexpr (!std::is_same<T, float>::value) {
+    (void)result;
+    return StatusCode::UNSUPPORTED_TYPE;
+  } else {
+    const int64_t n = static_cast<int64_t>(x.numel());
+    const std::size_t ws = cuopx_vector_workspace_size(n);
+    Tensor<unsigned char> scratch({ws + 256});
+    float* d_result = reinterpret_cast<float*>(scratch.data() + ws);
+    // Arrival counters must start at zero (the pool may hand back a used block).
+    if (ws && cudaMemsetAsync(scratch.data(), 0, ws, stream_) != cudaSuccess) return StatusCode::CUDA_ERROR;
+    const int rc = cuopx_dot(n, x.data(), 1, y.data(), 1, d_result, scratch.data(), ws, stream_);
+    if (rc != CUOPX_SUCCESS) return to_status(rc);
+    if (cudaMemcpyAsync(&result, d_result, sizeof(float), cudaMemcpyDeviceToHost, stream_) != cudaSuccess ||
+        cudaStreamSynchronize(stream_) != cudaSuccess)
+      return StatusCode::CUDA_ERROR;
+    return StatusCode::SUCCESS;
+  }
+}
+
+template <typename T>
+StatusCode Axpy<T>::Forward(const Tensor<T>& x, Tensor<T>& y) {
+  if (x.numel() != y.numel()) return StatusCode::SHAPE_MISMATCH;
+  if constexpr (!std::is_same<T, float>::value) {
+    return StatusCode::UNSUPPORTED_TYPE;
+  } else {
+    return to_status(cuopx_axpy(static_cast<int64_t>(x.numel()), alpha_, x.data(), 1, y.data(), 1, stream_));
+  }
+}
+
+template <typename T>
+StatusCode Scal<T>::Forward(Tensor<T>& x) {
+  if constexpr (!std::is_same<T, float>::value) {
+    return StatusCode::UNSUPPORTED_TYPE;
+  } else {
+    return to_status(cuopx_scal(static_cast<int64_t>(x.numel()), alpha_, x.data(), 1, stream_));
+  }
+}
+
+template <typename T>
+StatusCode Copy<T>::Forward(const Tensor<T>& input, Tensor<T>& output) {
+  if (input.numel() != output.numel()) return StatusCode::SHAPE_MISMATCH;
+  if constexpr (!std::is_same<T, float>::value) {
+    return StatusCode::UNSUPPORTED_TYPE;
+  } else {
+    return to_status(cuopx_copy(static_cast<int64_t>(input.numel()), input.data(), 1, output.data(), 1, stream_));
+  }
+}
+
+template class Dot<float>;
+template class Dot<double>;
+template class Axpy<float>;
+template class Axpy<double>;
+template class Scal<float>;
+template class Scal<double>;
+template class Copy<float>;
+template class Copy<double>;
+
 #define CUOP_INSTANTIATE(T)         \
   template class Gemm<T>;           \
   template class Gemv<T>;           \
   template class GemmBatched<T>;    \
   template class BatchMatMul<T>;    \
-  template class MatMul<T>;
+  template class MatMul<T>;         \
+  template class MatMulReluFused<T>;
 CUOP_INSTANTIATE(float)
 CUOP_INSTANTIATE(double)
 CUOP_INSTANTIATE(__half)

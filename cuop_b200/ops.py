@@ -66,8 +66,10 @@ def workspace(nbytes: int, device: torch.device, tag: str = "ws") -> tuple[int, 
 
 
 def gemm(A: torch.Tensor, B: torch.Tensor, C: Optional[torch.Tensor] = None, *, transA: bool = False,
-         transB: bool = False, alpha: float = 1.0, beta: float = 0.0, stream=None) -> torch.Tensor:
-    """C = alpha * op(A) op(B) + beta * C for row-major 2-D tensors."""
+         transB: bool = False, alpha: float = 1.0, beta: float = 0.0, bias: Optional[torch.Tensor] = None,
+         relu: bool = False, stream=None) -> torch.Tensor:
+    """C = act(alpha * op(A) op(B) + beta * C + bias) for row-major 2-D tensors;
+    bias ([N], same dtype) and relu select the fused epilogue (cuopx_gemm_ex)."""
     _require_cuda(A, B)
     M = A.size(1) if transA else A.size(0)
     K = A.size(0) if transA else A.size(1)
@@ -83,10 +85,24 @@ def gemm(A: torch.Tensor, B: torch.Tensor, C: Optional[torch.Tensor] = None, *, 
     _require_cuda(C)
     if tuple(C.shape) != (M, Nn) or C.dtype != A.dtype:
         raise N.CuopError(N.SHAPE_MISMATCH, f"gemm: C must be {M}x{Nn} {A.dtype}")
-    rc = N.lib().cuopx_gemm(_dtype_code(A), int(transA), int(transB), M, Nn, K, float(alpha), A.data_ptr(),
-                            _row_ld(A), B.data_ptr(), _row_ld(B), float(beta), C.data_ptr(), _row_ld(C),
-                            _stream(stream))
-    N.check(rc, "cuopx_gemm")
+    if bias is None and not relu:
+        rc = N.lib().cuopx_gemm(_dtype_code(A), int(transA), int(transB), M, Nn, K, float(alpha), A.data_ptr(),
+                                _row_ld(A), B.data_ptr(), _row_ld(B), float(beta), C.data_ptr(), _row_ld(C),
+                                _stream(stream))
+        N.check(rc, "cuopx_gemm")
+        return C
+    epi = N.EPI_RELU if relu else N.EPI_NONE
+    bptr = 0
+    if bias is not None:
+        _require_cuda(bias)
+        if bias.dtype != A.dtype or bias.numel() != Nn or not bias.is_contiguous():
+            raise N.CuopError(N.SHAPE_MISMATCH, f"gemm: bias must be a contiguous [{Nn}] {A.dtype} vector")
+        epi |= N.EPI_BIAS
+        bptr = bias.data_ptr()
+    rc = N.lib().cuopx_gemm_ex(_dtype_code(A), int(transA), int(transB), M, Nn, K, float(alpha), A.data_ptr(),
+                               _row_ld(A), B.data_ptr(), _row_ld(B), float(beta), C.data_ptr(), _row_ld(C), bptr,
+                               epi, _stream(stream))
+    N.check(rc, "cuopx_gemm_ex")
     return C
 
 

@@ -87,6 +87,24 @@ int cuopx_gemm(int dtype, int transA, int transB, int64_t M, int64_t N, int64_t 
                int64_t lda, const void* B, int64_t ldb, double beta, void* C, int64_t ldc, void* stream);
 
 /*
+ * GEMM with a fused epilogue: C = act(alpha * op(A) * op(B) + beta * C + bias)
+ *   epilogue = CUOPX_EPI_NONE, CUOPX_EPI_BIAS, CUOPX_EPI_RELU or
+ *   CUOPX_EPI_BIAS | CUOPX_EPI_RELU.  bias is a device vector of N elements
+ *   of `dtype` (added to every row; may be NULL without CUOPX_EPI_BIAS).
+ *   ReLU(x) = x if x > 0 else +0.  The bias add and ReLU happen in the
+ *   accumulation type before the one rounding to the output type.
+ * Replaces MatMulReluFused<T>::Forward
+ * (src/cuda_op/detail/cuDNN/kernel_fusion.cu:330-370: relu(A*W + bias)),
+ * and Gemm<T>::Forward when epilogue == CUOPX_EPI_NONE.
+ */
+#define CUOPX_EPI_NONE 0
+#define CUOPX_EPI_BIAS 1
+#define CUOPX_EPI_RELU 2
+int cuopx_gemm_ex(int dtype, int transA, int transB, int64_t M, int64_t N, int64_t K, double alpha, const void* A,
+                  int64_t lda, const void* B, int64_t ldb, double beta, void* C, int64_t ldc, const void* bias,
+                  int epilogue, void* stream);
+
+/*
  * Strided batched GEMM: for b in [0, batch):
  *   C_b = alpha * op(A_b) * op(B_b) + beta * C_b,
  *   X_b = X + b * strideX (element strides; strideB may be 0 to share B).

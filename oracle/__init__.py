@@ -45,6 +45,10 @@ def lib() -> C.CDLL:
             "oracle_gemm_f64": [_int, _int, _i64, _i64, _i64, _f64, _vp, _i64, _vp, _i64, _f64, _vp, _i64, _int],
             "oracle_gemm_lowp": [_int, _int, _int, _i64, _i64, _i64, _f32, _vp, _i64, _vp, _i64, _f32, _vp, _i64,
                                  _int],
+            "oracle_gemm_lowp_ex": [_int, _int, _int, _i64, _i64, _i64, _f32, _vp, _i64, _vp, _i64, _f32, _vp,
+                                    _i64, _vp, _int, _int],
+            "oracle_epilogue_f32": [_i64, _i64, _vp, _i64, _vp, _int],
+            "oracle_epilogue_f64": [_i64, _i64, _vp, _i64, _vp, _int],
             "oracle_gemm_batched_lowp": [_int, _int, _int, _i64, _i64, _i64, _f32, _vp, _i64, _i64, _vp, _i64, _i64,
                                          _f32, _vp, _i64, _i64, _i64, _int],
             "oracle_gemm_batched_f32": [_int, _int, _i64, _i64, _i64, _f32, _vp, _i64, _i64, _vp, _i64, _i64, _f32,
@@ -100,7 +104,12 @@ def from_lowp(h: np.ndarray, dtype: int) -> np.ndarray:
 
 
 # ------------------------------------------------------------ GEMM / GEMV
-def gemm_f32(A, B, C=None, transA=False, transB=False, alpha=1.0, beta=0.0, nthreads=None):
+def _epi(bias, relu):
+    return (1 if bias is not None else 0) | (2 if relu else 0)
+
+
+def gemm_f32(A, B, C=None, transA=False, transB=False, alpha=1.0, beta=0.0, nthreads=None, bias=None, relu=False):
+    """bias / relu: the fused epilogue of cuopx_gemm_ex (bias add, then ReLU)."""
     A = np.ascontiguousarray(A, np.float32)
     B = np.ascontiguousarray(B, np.float32)
     M, K = (A.shape[1], A.shape[0]) if transA else A.shape
@@ -108,10 +117,13 @@ def gemm_f32(A, B, C=None, transA=False, transB=False, alpha=1.0, beta=0.0, nthr
     C = np.zeros((M, N), np.float32) if C is None else np.array(C, np.float32, copy=True)
     lib().oracle_gemm_f32(int(transA), int(transB), M, N, K, alpha, _p(A), A.shape[1], _p(B), B.shape[1], beta,
                           _p(C), N, nthreads or threads())
+    if bias is not None or relu:
+        bias = None if bias is None else np.ascontiguousarray(bias, np.float32)
+        lib().oracle_epilogue_f32(M, N, _p(C), N, None if bias is None else _p(bias), _epi(bias, relu))
     return C
 
 
-def gemm_f64(A, B, C=None, transA=False, transB=False, alpha=1.0, beta=0.0, nthreads=None):
+def gemm_f64(A, B, C=None, transA=False, transB=False, alpha=1.0, beta=0.0, nthreads=None, bias=None, relu=False):
     A = np.ascontiguousarray(A, np.float64)
     B = np.ascontiguousarray(B, np.float64)
     M, K = (A.shape[1], A.shape[0]) if transA else A.shape
@@ -119,18 +131,24 @@ def gemm_f64(A, B, C=None, transA=False, transB=False, alpha=1.0, beta=0.0, nthr
     C = np.zeros((M, N), np.float64) if C is None else np.array(C, np.float64, copy=True)
     lib().oracle_gemm_f64(int(transA), int(transB), M, N, K, alpha, _p(A), A.shape[1], _p(B), B.shape[1], beta,
                           _p(C), N, nthreads or threads())
+    if bias is not None or relu:
+        bias = None if bias is None else np.ascontiguousarray(bias, np.float64)
+        lib().oracle_epilogue_f64(M, N, _p(C), N, None if bias is None else _p(bias), _epi(bias, relu))
     return C
 
 
-def gemm_lowp(dtype, A, B, C=None, transA=False, transB=False, alpha=1.0, beta=0.0, nthreads=None):
-    """A, B, C as uint16 bit patterns of fp16 (dtype=2) / bf16 (dtype=3)."""
+def gemm_lowp(dtype, A, B, C=None, transA=False, transB=False, alpha=1.0, beta=0.0, nthreads=None, bias=None,
+              relu=False):
+    """A, B, C (and bias) as uint16 bit patterns of fp16 (dtype=2) / bf16 (dtype=3)."""
     A = np.ascontiguousarray(A, np.uint16)
     B = np.ascontiguousarray(B, np.uint16)
     M, K = (A.shape[1], A.shape[0]) if transA else A.shape
     N = B.shape[0] if transB else B.shape[1]
     C = np.zeros((M, N), np.uint16) if C is None else np.array(C, np.uint16, copy=True)
-    lib().oracle_gemm_lowp(dtype, int(transA), int(transB), M, N, K, alpha, _p(A), A.shape[1], _p(B), B.shape[1],
-                           beta, _p(C), N, nthreads or threads())
+    bias = None if bias is None else np.ascontiguousarray(bias, np.uint16)
+    lib().oracle_gemm_lowp_ex(dtype, int(transA), int(transB), M, N, K, alpha, _p(A), A.shape[1], _p(B),
+                              B.shape[1], beta, _p(C), N, None if bias is None else _p(bias), _epi(bias, relu),
+                              nthreads or threads())
     return C
 
 
@@ -217,7 +235,8 @@ def ref_lib() -> C.CDLL:
         L.ref_gemm_f32.argtypes = [_int, _int, _int, _int, _int, _f32, _vp, _vp, _f32, _vp]
         L.ref_gemv_f32.argtypes = [_int, _int, _int, _f32, _vp, _vp, _f32, _vp]
         L.ref_batchmatmul_f32.argtypes = [_int, _int, _int, _int, _vp, _vp, _vp]
-        for f in (L.ref_gemm_f32, L.ref_gemv_f32, L.ref_batchmatmul_f32):
+        L.ref_matmul_relu_f32.argtypes = [_int, _int, _int, _int, _int, _vp, _vp, _vp, _vp]
+        for f in (L.ref_gemm_f32, L.ref_gemv_f32, L.ref_batchmatmul_f32, L.ref_matmul_relu_f32):
             f.restype = _int
         _ref = L
     return _ref

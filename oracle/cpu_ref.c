@@ -190,12 +190,37 @@ ORACLE_API void oracle_gemm_f64(int transA, int transB, int64_t M, int64_t N, in
   }
 }
 
-/* fp16/bf16 inputs, fp32 fma chain, one RNE rounding.  Rows are processed in
- * blocks of RB so each widened B row is reused RB times.                     */
+/* Fused epilogue of cuopx_gemm_ex, restating MatMulReluFused
+ * (src/cuda_op/detail/cuDNN/kernel_fusion.cu:117-136): + bias[col], then
+ * ReLU(x) = x if x > 0 else +0.  Flags: 1 = bias, 2 = ReLU.                  */
+static inline float epi_f32(float v, const float* bias, int64_t j, int epi) {
+  if (epi & 1) v = v + bias[j];
+  if (epi & 2) v = v > 0.0f ? v : 0.0f;
+  return v;
+}
+
+ORACLE_API void oracle_epilogue_f32(int64_t M, int64_t N, float* C, int64_t ldc, const float* bias, int epi) {
+  for (int64_t i = 0; i < M; ++i)
+    for (int64_t j = 0; j < N; ++j) C[i * ldc + j] = epi_f32(C[i * ldc + j], bias, j, epi);
+}
+
+ORACLE_API void oracle_epilogue_f64(int64_t M, int64_t N, double* C, int64_t ldc, const double* bias, int epi) {
+  for (int64_t i = 0; i < M; ++i)
+    for (int64_t j = 0; j < N; ++j) {
+      double v = C[i * ldc + j];
+      if (epi & 1) v = v + bias[j];
+      if (epi & 2) v = v > 0.0 ? v : 0.0;
+      C[i * ldc + j] = v;
+    }
+}
+
+/* fp16/bf16 inputs, fp32 fma chain, one RNE rounding (after the optional
+ * epilogue; bias is fp16/bf16 bits, widened).  Rows are processed in blocks
+ * of RB so each widened B row is reused RB times.                            */
 #define RB 8
-ORACLE_API void oracle_gemm_lowp(int dtype, int transA, int transB, int64_t M, int64_t N, int64_t K, float alpha,
-                                 const uint16_t* A, int64_t lda, const uint16_t* B, int64_t ldb, float beta,
-                                 uint16_t* C, int64_t ldc, int nthreads) {
+ORACLE_API void oracle_gemm_lowp_ex(int dtype, int transA, int transB, int64_t M, int64_t N, int64_t K, float alpha,
+                                    const uint16_t* A, int64_t lda, const uint16_t* B, int64_t ldb, float beta,
+                                    uint16_t* C, int64_t ldc, const uint16_t* bias, int epi, int nthreads) {
   if (nthreads <= 0) nthreads = 1;
   const int64_t nblk = (M + RB - 1) / RB;
 #pragma omp parallel num_threads(nthreads)
@@ -222,6 +247,8 @@ ORACLE_API void oracle_gemm_lowp(int dtype, int transA, int transB, int64_t M, i
         for (int64_t j = 0; j < N; ++j) {
           float v = alpha * ar[j];
           if (beta != 0.0f) v = v + beta * lowp_to_f32(dtype, crow[j]);
+          if (epi & 1) v = v + lowp_to_f32(dtype, bias[j]);
+          if (epi & 2) v = v > 0.0f ? v : 0.0f;
           crow[j] = f32_to_lowp(dtype, v);
         }
       }
@@ -229,6 +256,12 @@ ORACLE_API void oracle_gemm_lowp(int dtype, int transA, int transB, int64_t M, i
     free(acc);
     free(brow);
   }
+}
+
+ORACLE_API void oracle_gemm_lowp(int dtype, int transA, int transB, int64_t M, int64_t N, int64_t K, float alpha,
+                                 const uint16_t* A, int64_t lda, const uint16_t* B, int64_t ldb, float beta,
+                                 uint16_t* C, int64_t ldc, int nthreads) {
+  oracle_gemm_lowp_ex(dtype, transA, transB, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, NULL, 0, nthreads);
 }
 
 /* Strided batched form of oracle_gemm_lowp / oracle_gemm_f32. */

@@ -5,11 +5,13 @@
 //   Gemm<float>::SetWeight + Forward   (src/cuda_op/detail/cuBlas/gemm.cu:410-511)
 //   Gemv<float>::SetWeight + Forward   (src/cuda_op/detail/cuBlas/gemv.cu:203-256)
 //   BatchMatMul<float>::Forward        (src/cuda_op/detail/cuDNN/batchmatmul.cu:52-94)
+//   MatMulReluFused<float>::Forward    (src/cuda_op/detail/cuDNN/kernel_fusion.cu:330-370)
 // Pointers are device pointers owned by the caller (wrapped in non-owning
 // Tensors); the call synchronises before returning.
 #include "cuda_op/detail/cuBlas/gemm.hpp"
 #include "cuda_op/detail/cuBlas/gemv.hpp"
 #include "cuda_op/detail/cuDNN/batchmatmul.hpp"
+#include "cuda_op/detail/cuDNN/kernel_fusion.hpp"
 
 using namespace cu_op_mem;
 
@@ -61,6 +63,30 @@ extern "C" int ref_batchmatmul_f32(int batch, int M, int N, int K, const float* 
     cudaDeviceSynchronize();
   }
   new (&a) Tensor<float>();
+  new (&b) Tensor<float>();
+  new (&c) Tensor<float>();
+  return rc;
+}
+
+// MatMulReluFused<float>::SetWeight/SetBias + Forward
+// (src/cuda_op/detail/cuDNN/kernel_fusion.cu:316-370): C = relu(A*W + bias).
+extern "C" int ref_matmul_relu_f32(int transA, int transB, int M, int N, int K, const float* A, const float* W,
+                                   const float* bias, float* C) {
+  Tensor<float> a(const_cast<float*>(A), {static_cast<size_t>(M), static_cast<size_t>(K)});
+  Tensor<float> w(const_cast<float*>(W), {static_cast<size_t>(K), static_cast<size_t>(N)});
+  Tensor<float> b(const_cast<float*>(bias), {static_cast<size_t>(N)});
+  Tensor<float> c(C, {static_cast<size_t>(M), static_cast<size_t>(N)});
+  int rc;
+  {
+    MatMulReluFused<float> op(transA != 0, transB != 0);
+    op.SetWeight(w);
+    if (bias) op.SetBias(b);
+    std::vector<Tensor<float>*> ins{&a}, outs{&c};
+    rc = static_cast<int>(op.Forward(ins, outs));
+    cudaDeviceSynchronize();
+  }
+  new (&a) Tensor<float>();
+  new (&w) Tensor<float>();
   new (&b) Tensor<float>();
   new (&c) Tensor<float>();
   return rc;

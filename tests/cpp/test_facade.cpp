@@ -13,10 +13,15 @@
 #include <string>
 #include <vector>
 
+#include "cuda_op/detail/cuBlas/axpy.hpp"
+#include "cuda_op/detail/cuBlas/copy.hpp"
+#include "cuda_op/detail/cuBlas/dot.hpp"
 #include "cuda_op/detail/cuBlas/gemm.hpp"
 #include "cuda_op/detail/cuBlas/gemm_batched.hpp"
 #include "cuda_op/detail/cuBlas/gemv.hpp"
+#include "cuda_op/detail/cuBlas/scal.hpp"
 #include "cuda_op/detail/cuDNN/batchmatmul.hpp"
+#include "cuda_op/detail/cuDNN/kernel_fusion.hpp"
 #include "cuda_op/detail/cuDNN/matmul.hpp"
 #include "cuopx.h"
 #include "jit/Blas/blas_jit_plugins.hpp"
@@ -29,6 +34,7 @@ void oracle_gemm_f32(int transA, int transB, int64_t M, int64_t N, int64_t K, fl
                      int64_t lda, const float* B, int64_t ldb, float beta, float* C, int64_t ldc, int nthreads);
 void oracle_gemv_f32(int trans, int64_t M, int64_t N, float alpha, const float* A, int64_t lda, const float* x,
                      float beta, float* y, int nthreads);
+void oracle_epilogue_f32(int64_t M, int64_t N, float* C, int64_t ldc, const float* bias, int epi);
 }
 
 using namespace cu_op_mem;
@@ -249,6 +255,68 @@ TEST_GPU(GemmSeededMatchesOracleBitExact) {
     auto h = to_host(C);
     EXPECT_TRUE(std::memcmp(h.data(), ref.data(), h.size() * sizeof(float)) == 0);
   }
+}
+
+// MatMulReluFused (kernel_fusion.cu:330-370): relu(A*W + bias); below 256^3
+// the fp32 path is the FFMA chain, so the result is the oracle's bit for bit.
+TEST_GPU(MatMulReluFusedMatchesOracleBitExact) {
+  const int M = 257, N = 129, K = 300;
+  std::vector<float> a(size_t(M) * K), w(size_t(K) * N), b(N);
+  oracle_fill_uniform_f32(a.data(), a.size(), 31, -1.f, 1.f);
+  oracle_fill_uniform_f32(w.data(), w.size(), 32, -1.f, 1.f);
+  oracle_fill_uniform_f32(b.data(), b.size(), 33, -1.f, 1.f);
+  Tensor<float> A({size_t(M), size_t(K)}), W({size_t(K), size_t(N)}), B({size_t(N)}), Bbad({size_t(N + 1)});
+  A.copy_from_host(a.data());
+  W.copy_from_host(w.data());
+  B.copy_from_host(b.data());
+  for (int with_bias = 0; with_bias < 2; ++with_bias) {
+    std::vector<float> ref(size_t(M) * N, 0.f);
+    oracle_gemm_f32(0, 0, M, N, K, 1.f, a.data(), K, w.data(), N, 0.f, ref.data(), N, 4);
+    oracle_epilogue_f32(M, N, ref.data(), N, b.data(), with_bias ? 3 : 2);
+    MatMulReluFused<float> op;
+    op.SetWeight(W);
+    op.SetBias(with_bias ? B : Bbad);  // a bias of the wrong length is ignored, as in the reference
+    Tensor<float> C;
+    std::vector<Tensor<float>*> ins{&A}, outs{&C};
+    EXPECT_TRUE(op.Forward(ins, outs) == StatusCode::SUCCESS);
+    EXPECT_TRUE(C.shape() == (std::vector<size_t>{size_t(M), size_t(N)}));
+    auto h = to_host(C);
+    EXPECT_TRUE(std::memcmp(h.data(), ref.data(), h.size() * sizeof(float)) == 0);
+    EXPECT_TRUE(op.Backward(ins, outs, outs) == StatusCode::UNSUPPORTED_OPERATION);
+  }
+}
+
+TEST_GPU(VectorOperatorClasses) {
+  const int n = 100003;
+  std::vector<float> x(n), y(n);
+  oracle_fill_uniform_f32(x.data(), n, 41, -1.f, 1.f);
+  oracle_fill_uniform_f32(y.data(), n, 42, -1.f, 1.f);
+  Tensor<float> X({size_t(n)}), Y({size_t(n)}), Z({size_t(n)});
+  X.copy_from_host(x.data());
+  Y.copy_from_host(y.data());
+  double dot = 0;
+  for (int i = 0; i < n; ++i) dot += double(x[i]) * y[i];
+  float r = 0.f;
+  Dot<float> d;
+  EXPECT_TRUE(d.Forward(X, Y, r) == StatusCode::SUCCESS);
+  EXPECT_NEAR(r, dot, 1e-3);
+  Axpy<float> ax(2.f);
+  EXPECT_TRUE(ax.Forward(X, Y) == StatusCode::SUCCESS);  // y = 2x + y
+  Scal<float> sc(0.5f);
+  EXPECT_TRUE(sc.Forward(Y) == StatusCode::SUCCESS);  // y = x + y/2
+  Copy<float> cp;
+  EXPECT_TRUE(cp.Forward(Y, Z) == StatusCode::SUCCESS);
+  cudaDeviceSynchronize();
+  auto z = to_host(Z);
+  bool ok = true;
+  for (int i = 0; i < n; ++i) ok &= z[i] == 0.5f * (2.f * x[i] + y[i]);
+  EXPECT_TRUE(ok);
+  Tensor<double> Xd({8}), Yd({8});
+  double rd = 0;
+  Dot<double> dd;
+  EXPECT_TRUE(dd.Forward(Xd, Yd, rd) == StatusCode::UNSUPPORTED_TYPE);
+  Tensor<float> short_y({size_t(n - 1)});
+  EXPECT_TRUE(ax.Forward(X, short_y) == StatusCode::SHAPE_MISMATCH);
 }
 
 TEST_GPU(GemvSeededMatchesOracle) {

@@ -72,6 +72,17 @@ def test_argument_validation_without_gpu():
     assert L.cuopx_axpy(-1, 1.0, 16, 1, 32, 1, None) == N.INVALID_ARGUMENT
     assert L.cuopx_axpy(4, 1.0, 16, 0, 32, 1, None) == N.INVALID_ARGUMENT
     assert L.cuopx_gather_column_blocks(N.F16, 2, 4, 4, 16, 64, 7, None) == N.INVALID_ARGUMENT
+    # fused epilogue: unknown flags, bias flag without a bias vector
+    assert L.cuopx_gemm_ex(N.F32, 0, 0, 4, 4, 4, 1.0, 16, 4, 16, 4, 0.0, 64, 4, None, 4, None) == N.INVALID_ARGUMENT
+    assert L.cuopx_gemm_ex(N.F32, 0, 0, 4, 4, 4, 1.0, 16, 4, 16, 4, 0.0, 64, 4, None, N.EPI_BIAS,
+                           None) == N.INVALID_ARGUMENT
+    # fused all-gather: rank outside the world, too many ranks
+    ptrs = (C.c_void_p * 2)(4096, 8192)
+    assert L.cuopx_gemm_allgather(N.F16, 0, 0, 512, 256, 512, 1.0, 16, 512, 32, 256, ptrs, 2, 2, 512,
+                                  None) == N.INVALID_ARGUMENT
+    assert L.cuopx_gemm_allgather(N.F16, 0, 0, 512, 256, 512, 1.0, 16, 512, 32, 256, ptrs, 9, 0, 4608,
+                                  None) == N.INVALID_ARGUMENT
+    assert L.cuopx_peer_barrier(ptrs, 2, 5, None) == N.INVALID_ARGUMENT
 
 
 def test_workspace_sizing_is_host_only():
