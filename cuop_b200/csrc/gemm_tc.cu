@@ -178,6 +178,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
+  // Everything above touched only shared memory, TMEM and the parameter
+  // tensor maps; global memory waits for the previous kernel on the stream.
+  grid_dependency_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -241,7 +244,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         int next = 0;
         const bool more = clc_next_tile(clc_resp + cs * 16, p.num_tiles, next);
         mbar_arrive(&clc_empty[cs]);
-        if (!more) break;
+        if (!more) {
+          grid_launch_dependents();  // all loads issued: the next kernel may start its prologue
+          break;
+        }
         t = next;
       }
       if (!ok) {
@@ -516,8 +522,14 @@ int launch_tc(const GemmProblem& p, cudaStream_t stream, const char* name) {
       return CUOPX_CUDA_ERROR;
     attr_set[dev] = true;
   }
-  // One CTA per tile; running CTAs take over unlaunched ones' tiles.
-  kern<<<prm.num_tiles, NUM_THREADS, L::ALLOC, stream>>>(mA, mB, mC, prm);
+  // One CTA per tile; running CTAs take over unlaunched ones' tiles.  The
+  // launch may overlap the previous kernel's tail (programmatic dependent
+  // launch; the kernel waits before touching global memory).
+  if (launch_pdl(kern, dim3(static_cast<unsigned>(prm.num_tiles)), dim3(NUM_THREADS), L::ALLOC, stream, mA, mB, mC,
+                 prm) != cudaSuccess) {
+    cudaGetLastError();
+    return CUOPX_CUDA_ERROR;
+  }
   note_launch(name);
   return check_launch();
 }

@@ -70,6 +70,10 @@ __global__ void __launch_bounds__(GS_THREADS, 2)
   const int64_t nvec = N / V;
   const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_cta;
   const int64_t r1 = min(M, r0 + rows_per_cta);
+  // Single-wave grid: the next kernel may start launching now (its CTAs
+  // wait for free slots and for this grid's completion).
+  grid_dependency_wait();
+  grid_launch_dependents();
   if (r0 >= r1) return;
 
   Acc xr[KV][V];
@@ -160,6 +164,8 @@ __global__ void __launch_bounds__(GS_THREADS, 2)
   const int64_t j0 = static_cast<int64_t>(blockIdx.y) * rows_per_split;
   const int64_t j1 = min(N, j0 + rows_per_split);
   const unsigned int splits = gridDim.y;
+  grid_dependency_wait();
+  grid_launch_dependents();
 
   Acc acc[V];
 #pragma unroll
@@ -318,19 +324,28 @@ int launch_gemv_stream(int trans, int64_t M, int64_t N, double alpha_d, const vo
   const Acc alpha = static_cast<Acc>(alpha_d), beta = static_cast<Acc>(beta_d);
   if (!p.trans) {
     const dim3 grid(static_cast<unsigned>(p.grid));
+    cudaError_t e;
+    const int rpc = p.rows_per_cta;
     switch (p.kv) {
-      case 1: gemv_n_xreg<T, 1><<<grid, GS_THREADS, 0, stream>>>(M, N, alpha, A, lda, x, beta, y, p.rows_per_cta); break;
-      case 2: gemv_n_xreg<T, 2><<<grid, GS_THREADS, 0, stream>>>(M, N, alpha, A, lda, x, beta, y, p.rows_per_cta); break;
-      case 4: gemv_n_xreg<T, 4><<<grid, GS_THREADS, 0, stream>>>(M, N, alpha, A, lda, x, beta, y, p.rows_per_cta); break;
-      default: gemv_n_xreg<T, 8><<<grid, GS_THREADS, 0, stream>>>(M, N, alpha, A, lda, x, beta, y, p.rows_per_cta); break;
+      case 1: e = launch_pdl(gemv_n_xreg<T, 1>, grid, dim3(GS_THREADS), 0, stream, M, N, alpha, A, lda, x, beta, y, rpc); break;
+      case 2: e = launch_pdl(gemv_n_xreg<T, 2>, grid, dim3(GS_THREADS), 0, stream, M, N, alpha, A, lda, x, beta, y, rpc); break;
+      case 4: e = launch_pdl(gemv_n_xreg<T, 4>, grid, dim3(GS_THREADS), 0, stream, M, N, alpha, A, lda, x, beta, y, rpc); break;
+      default: e = launch_pdl(gemv_n_xreg<T, 8>, grid, dim3(GS_THREADS), 0, stream, M, N, alpha, A, lda, x, beta, y, rpc); break;
+    }
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return CUOPX_CUDA_ERROR;
     }
     note_launch("gemv_n_xreg");
   } else {
     unsigned int* counters = reinterpret_cast<unsigned int*>(ws);
     Acc* partials = reinterpret_cast<Acc*>(static_cast<char*>(ws) + counter_bytes);
     const dim3 grid(static_cast<unsigned>(p.strips), static_cast<unsigned>(p.splits));
-    gemv_t_lsu<T><<<grid, GS_THREADS, 0, stream>>>(M, N, alpha, A, lda, x, beta, y, p.rows_per_split, partials,
-                                                  counters);
+    if (launch_pdl(gemv_t_lsu<T>, grid, dim3(GS_THREADS), 0, stream, M, N, alpha, A, lda, x, beta, y,
+                   p.rows_per_split, partials, counters) != cudaSuccess) {
+      cudaGetLastError();
+      return CUOPX_CUDA_ERROR;
+    }
     note_launch("gemv_t_lsu");
   }
   return check_launch();
