@@ -274,6 +274,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
   cluster_sync_all();  // barrier inits and TMEM allocation visible to the peer
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
+  // Global memory (and peers' memory) only after the previous kernel on the
+  // stream has completed (programmatic dependent launch).
+  grid_dependency_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer (both CTAs)
@@ -355,7 +358,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
           more = clc_next_pair_tile(clc_resp + cs * 16, p.num_tiles, next);
           mbar_arrive_cluster(map_to_rank(&clc_empty[cs], 0));
         }
-        if (!more) break;
+        if (!more) {
+          grid_launch_dependents();  // all loads issued: the next kernel may start its prologue
+          break;
+        }
         t = next;
       }
       if (ok) {
@@ -613,7 +619,11 @@ int launch_tc2(const GemmProblem& p, cudaStream_t stream, const char* name, void
     attr_set[dev] = true;
   }
   // One cluster per pair tile; running clusters take over unlaunched ones.
-  kern<<<prm.num_tiles * 2, P_THREADS, L::ALLOC, stream>>>(mA, mB, mC, prm);
+  if (launch_pdl(kern, dim3(static_cast<unsigned>(prm.num_tiles * 2)), dim3(P_THREADS), L::ALLOC, stream, mA, mB, mC,
+                 prm) != cudaSuccess) {
+    cudaGetLastError();
+    return CUOPX_CUDA_ERROR;
+  }
   note_launch(name);
   return check_launch();
 }

@@ -160,6 +160,9 @@ __global__ void __launch_bounds__(X3_THREADS, 1)
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
+  // Global memory only after the previous kernel on the stream has completed
+  // (programmatic dependent launch).
+  grid_dependency_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -202,6 +205,7 @@ __global__ void __launch_bounds__(X3_THREADS, 1)
           if (++stage == STAGES) stage = 0, phase ^= 1u;
         }
       }
+      if (ok) grid_launch_dependents();  // all loads issued: the next kernel may start its prologue
       if (!ok) {
         for (int s = 0; s < STAGES; ++s) {
           if (!((issued_mask >> s) & 1u)) continue;
@@ -408,7 +412,11 @@ int launch_x3(const GemmProblem& p, cudaStream_t stream, const char* name) {
     attr_set[dev] = true;
   }
   const int grid = std::min(prm.num_tiles, device_sm_count());
-  kern<<<grid, X3_THREADS, L::ALLOC, stream>>>(mA, mB, mC, prm);
+  if (launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(X3_THREADS), L::ALLOC, stream, mA, mB, mC, prm) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return CUOPX_CUDA_ERROR;
+  }
   note_launch(name);
   return check_launch();
 }
