@@ -363,6 +363,56 @@ def cpu_gemv_baseline(budget_s: float = 4.0):
                       f"oracle/cpu_ref.c, OpenMP {nt} threads"}
 
 
+def cpu_config_baselines(budget_s: float = 1.5) -> dict:
+    """The oracle (CPU restatement of the reference kernels' arithmetic) on
+    the GEMM configs, all host threads: C1 and C4 in full, C3 and C5 on a
+    64-row slab of A with the full-problem time extrapolated by rows."""
+    import numpy as np
+    import oracle as O
+
+    nt = O.threads()
+
+    def timed(fn):
+        fn()  # page-in
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            fn()
+            reps += 1
+            el = time.perf_counter() - t0
+            if el >= budget_s or reps >= 20:
+                return el / reps
+
+    out = {}
+    n = 1024
+    A, B = O.uniform((n, n), seed=0), O.uniform((n, n), seed=1)
+    t = timed(lambda: O.gemm_f32(A, B, nthreads=nt))
+    out["c1_fp32_gemm_1024"] = {"value": round(2 * n ** 3 / t / 1e12, 4), "unit": "TFLOP/s", "cores": nt,
+                                "kind": "port", "sample": f"full 1024^3 fp32 GEMM, {t * 1e3:.1f} ms"}
+    n, rows = 8192, 64
+    A = O.to_lowp(O.normal((rows, n), seed=2) / math.sqrt(n), O.F16)
+    B = O.to_lowp(O.normal((n, n), seed=3) / math.sqrt(n), O.F16)
+    t = timed(lambda: O.gemm_lowp(O.F16, A, B, nthreads=nt))
+    out["c3_fp16_gemm_8192"] = {"value": round(2 * rows * n * n / t / 1e12, 4), "unit": "TFLOP/s", "cores": nt,
+                                "kind": "port", "sample": f"64-row slab of the 8192^3 fp16 GEMM, {t * 1e3:.0f} ms; "
+                                                          f"extrapolated full problem {t * n / rows:.1f} s"}
+    bt, M, N_, K = 4096, 128, 128, 64
+    A = O.to_lowp(O.normal((bt, M, K), seed=4), O.BF16)
+    B = O.to_lowp(O.normal((bt, K, N_), seed=5), O.BF16)
+    t = timed(lambda: O.gemm_batched_lowp(O.BF16, A, B, nthreads=nt))
+    out["c4_bf16_batched_4096x128x128x64"] = {
+        "value": round(bt * (M * K + K * N_ + M * N_) * 2 / t / 1e9, 3), "unit": "GB/s", "cores": nt, "kind": "port",
+        "sample": f"full 4096 x 128x128x64 bf16 batched GEMM, {t * 1e3:.0f} ms"}
+    M, K, N_ = 4096, 8192, 28672
+    X = O.to_lowp(O.normal((rows, K), seed=6), O.BF16)
+    W = O.to_lowp(O.normal((K, N_), seed=7) * 0.02, O.BF16)
+    t = timed(lambda: O.gemm_lowp(O.BF16, X, W, nthreads=nt))
+    out["c5_bf16_linear_4096x8192x28672"] = {
+        "value": round(2 * rows * K * N_ / t / 1e12, 4), "unit": "TFLOP/s", "cores": nt, "kind": "port",
+        "sample": f"64-row slab of the 4096 x 8192 x 28672 bf16 GEMM, {t * 1e3:.0f} ms; "
+                  f"extrapolated full problem {t * M / rows:.1f} s"}
+    return out
+
+
 # --------------------------------------------------------------------------- other configs
 def run_configs(args, rank, world, local_rank):
     import torch
@@ -594,6 +644,10 @@ def main():
         line["configs"] = run_configs(args, rank, world, local_rank)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_gemv_baseline()
+        if "configs" in line:
+            for key, cb in cpu_config_baselines().items():
+                if key in line["configs"]:
+                    line["configs"][key]["cpu_baseline"] = cb
     elif rank == 0:
         line["cpu_baseline"] = None
     barrier(world)

@@ -264,23 +264,28 @@ ORACLE_API void oracle_gemm_lowp(int dtype, int transA, int transB, int64_t M, i
   oracle_gemm_lowp_ex(dtype, transA, transB, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, NULL, 0, nthreads);
 }
 
-/* Strided batched form of oracle_gemm_lowp / oracle_gemm_f32. */
+/* Strided batched form of oracle_gemm_lowp / oracle_gemm_f32: batches are
+ * spread over the threads (each batch single-threaded), the arithmetic of
+ * every batch is the single-GEMM oracle's.                                   */
 ORACLE_API void oracle_gemm_batched_lowp(int dtype, int transA, int transB, int64_t M, int64_t N, int64_t K,
                                          float alpha, const uint16_t* A, int64_t lda, int64_t sA,
                                          const uint16_t* B, int64_t ldb, int64_t sB, float beta, uint16_t* C,
                                          int64_t ldc, int64_t sC, int64_t batch, int nthreads) {
+  if (nthreads <= 0) nthreads = 1;
+#pragma omp parallel for num_threads(nthreads) schedule(static)
   for (int64_t b = 0; b < batch; ++b)
     oracle_gemm_lowp(dtype, transA, transB, M, N, K, alpha, A + b * sA, lda, B + b * sB, ldb, beta, C + b * sC, ldc,
-                     nthreads);
+                     1);
 }
 
 ORACLE_API void oracle_gemm_batched_f32(int transA, int transB, int64_t M, int64_t N, int64_t K, float alpha,
                                         const float* A, int64_t lda, int64_t sA, const float* B, int64_t ldb,
                                         int64_t sB, float beta, float* C, int64_t ldc, int64_t sC, int64_t batch,
                                         int nthreads) {
+  if (nthreads <= 0) nthreads = 1;
+#pragma omp parallel for num_threads(nthreads) schedule(static)
   for (int64_t b = 0; b < batch; ++b)
-    oracle_gemm_f32(transA, transB, M, N, K, alpha, A + b * sA, lda, B + b * sB, ldb, beta, C + b * sC, ldc,
-                    nthreads);
+    oracle_gemm_f32(transA, transB, M, N, K, alpha, A + b * sA, lda, B + b * sB, ldb, beta, C + b * sC, ldc, 1);
 }
 
 /* fp64-accumulated value of selected outputs (rows[r], cols[c]) of
