@@ -50,6 +50,12 @@ SIGNATURES = [
     ("cuopx_launch_count", _i64, []),
     ("cuopx_get_device_error", _int, [C.POINTER(_int)]),
     ("cuopx_clear_device_error", _int, []),
+    ("cuopx_tuning_load", _int, [C.c_char_p]),
+    ("cuopx_tuning_load_file", _int, [C.c_char_p]),
+    ("cuopx_tuning_clear", _int, []),
+    ("cuopx_tuning_rows", _int, []),
+    ("cuopx_set_gemm_variant", _int, [C.c_char_p]),
+    ("cuopx_gemm_variant_name", C.c_char_p, [_int]),
     ("cuopx_gemm", _int, [_int, _int, _int, _i64, _i64, _i64, _dbl, _vp, _i64, _vp, _i64, _dbl, _vp, _i64, _vp]),
     ("cuopx_gemm_ex", _int,
      [_int, _int, _int, _i64, _i64, _i64, _dbl, _vp, _i64, _vp, _i64, _dbl, _vp, _i64, _vp, _int, _vp]),
@@ -100,6 +106,10 @@ def lib() -> C.CDLL:
             fn = getattr(handle, name)
             fn.restype = res
             fn.argtypes = args
+        # GEMM variant table from the offline sweep (cuop_b200/tuning.py).
+        table = _LIB_PATH.parent / "tuning_b200.txt"
+        if table.exists():
+            check(handle.cuopx_tuning_load_file(str(table).encode()), f"cuopx_tuning_load_file({table})")
         _lib = handle
     return _lib
 

@@ -58,7 +58,34 @@ constexpr double kTcMinWork = 64.0 * 64.0 * 64.0;
 constexpr double kTf32x3MinWork = 256.0 * 256.0 * 256.0;
 std::atomic<int> g_fp32_mode{CUOPX_FP32_AUTO};
 
+// Runs variant `v` when it can take `p`; -1 when it cannot (the caller then
+// makes the built-in choice).  In a non-default fp32 mode, variants of the
+// other fp32 arithmetic are declined: the mode is an accuracy contract.
+int run_variant(int v, const GemmProblem& p, cudaStream_t stream) {
+  const int mode = g_fp32_mode.load(std::memory_order_relaxed);
+  const bool tc_ok = p.K > 0 && gemm_tc_supported(p);
+  const bool x3_ok = p.K > 0 && gemm_tf32x3_supported(p) && mode != CUOPX_FP32_FFMA;
+  const bool ffma_ok = p.K > 0 && gemm_simt_f32_supported(p) && mode != CUOPX_FP32_TF32X3;
+  switch (v) {
+    case kVariantTc2: return tc_ok ? gemm_tc2(p, stream) : -1;
+    case kVariantTc128x256: return tc_ok ? gemm_tc(p, stream, 256) : -1;
+    case kVariantTc128x128: return tc_ok ? gemm_tc(p, stream, 128) : -1;
+    case kVariantTf32x3_64: return x3_ok ? gemm_tf32x3(p, stream, 64) : -1;
+    case kVariantTf32x3_128: return x3_ok ? gemm_tf32x3(p, stream, 128) : -1;
+    case kVariantFfma: return ffma_ok ? gemm_simt_f32(p, stream) : -1;
+    case kVariantGeneric:
+      return (p.dtype == CUOPX_F32 && mode == CUOPX_FP32_TF32X3 && gemm_tf32x3_supported(p)) ? -1
+                                                                                             : gemm_simt_generic(p, stream);
+    default: return -1;
+  }
+}
+
 int gemm_route(const GemmProblem& p, cudaStream_t stream) {
+  const int v = select_gemm_variant(p);  // override or tuning-table row
+  if (v != kVariantAuto) {
+    const int rc = run_variant(v, p, stream);
+    if (rc != -1) return rc;
+  }
   const double work = static_cast<double>(p.M) * p.N * p.K * p.batch;
   if (p.K > 0 && work >= kTcMinWork && gemm_tc_supported(p)) return gemm_tc(p, stream);
   const int mode = g_fp32_mode.load(std::memory_order_relaxed);

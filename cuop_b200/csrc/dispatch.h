@@ -52,8 +52,10 @@ bool gemm_simt_f32_supported(const GemmProblem& p);
 int gemm_simt_f32(const GemmProblem& p, cudaStream_t stream);
 
 // tcgen05/TMA back-end (gemm_tc.cu) for fp16/bf16.
+// bn = 0: choose (2-SM kernel for large problems, else BN 256 or 128);
+// bn = 128 / 256: the 1-SM kernel with that tile width.
 bool gemm_tc_supported(const GemmProblem& p);
-int gemm_tc(const GemmProblem& p, cudaStream_t stream);
+int gemm_tc(const GemmProblem& p, cudaStream_t stream, int bn = 0);
 
 // Two-SM (cta_group::2) tcgen05 back-end (gemm_tc2.cu) for large fp16/bf16.
 bool gemm_tc2_wanted(const GemmProblem& p);
@@ -64,7 +66,25 @@ int gemm_tc2_peers(const GemmProblem& p, void* const* peers, int npeers, cudaStr
 
 // 3xTF32 tcgen05 back-end (gemm_tf32x3.cu) for fp32.
 bool gemm_tf32x3_supported(const GemmProblem& p);
-int gemm_tf32x3(const GemmProblem& p, cudaStream_t stream);
+int gemm_tf32x3(const GemmProblem& p, cudaStream_t stream, int bn = 0);  // bn: 0 = choose, 64, 128
+
+// ---- variant selection (host/tuning.cpp) ----
+// GEMM variants a tuning table or an override may name.
+enum GemmVariant : int {
+  kVariantAuto = 0,
+  kVariantTc2 = 1,         // 2-SM tcgen05, 256 x 256 pair tiles
+  kVariantTc128x256 = 2,   // 1-SM tcgen05
+  kVariantTc128x128 = 3,
+  kVariantTf32x3_64 = 4,   // 3xTF32, 128 x 64 tiles
+  kVariantTf32x3_128 = 5,
+  kVariantFfma = 6,        // register-blocked fp32 FFMA
+  kVariantGeneric = 7,     // any dtype / layout
+  kVariantCount = 8,
+};
+const char* gemm_variant_name(int v);
+// The override (set by cuopx_set_gemm_variant) if any, else the first
+// tuning-table row matching the problem, else kVariantAuto.
+int select_gemm_variant(const GemmProblem& p);
 
 // Column-block gather (vector_ops.cu).
 int gather_column_blocks(int dtype, int64_t G, int64_t M, int64_t Nb, const void* blocks, void* out, int64_t ldo,

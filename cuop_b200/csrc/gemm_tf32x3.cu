@@ -445,10 +445,13 @@ bool gemm_tf32x3_supported(const GemmProblem& p) {
   return true;
 }
 
-int gemm_tf32x3(const GemmProblem& p, cudaStream_t stream) {
-  const int sms = device_sm_count();
-  const int64_t tiles128 = ((p.M + X3_BM - 1) / X3_BM) * ((p.N + 127) / 128) * p.batch;
-  if (p.N > 64 && tiles128 >= sms) return launch_x3_layout<128, 3>(p, stream, "gemm_tf32x3_128x128");
+int gemm_tf32x3(const GemmProblem& p, cudaStream_t stream, int bn) {
+  if (bn == 0) {
+    const int sms = device_sm_count();
+    const int64_t tiles128 = ((p.M + X3_BM - 1) / X3_BM) * ((p.N + 127) / 128) * p.batch;
+    bn = (p.N > 64 && tiles128 >= sms) ? 128 : 64;
+  }
+  if (bn == 128) return launch_x3_layout<128, 3>(p, stream, "gemm_tf32x3_128x128");
   return launch_x3_layout<64, 4>(p, stream, "gemm_tf32x3_128x64");
 }
 

@@ -73,6 +73,27 @@ int cuopx_set_fp32_gemm_mode(int mode);
 int cuopx_get_fp32_gemm_mode(void);
 
 /*
+ * GEMM variant selection.  The built-in choice (size thresholds per dtype,
+ * like the reference's selector, src/cuda_op/detail/cuBlas/gemm.cu:305-356)
+ * can be refined by a tuning table — text rules
+ *   dtype transA transB M N K batch variant
+ * (dtype f32|f64|f16|bf16|*, trans 0|1|*, sizes lo:hi inclusive with either
+ * side optional, or *) produced by an offline sweep; the first matching row
+ * wins, and a variant that cannot run a problem falls back to the built-in
+ * choice.  cuopx_set_gemm_variant forces one variant process-wide (NULL or
+ * "auto" restores table + built-in choice); used by the sweep.  Variant
+ * names: cuopx_gemm_variant_name(0..) until it returns NULL.  Replaces the
+ * selection tables and AutoTuner-driven kernel choice of the reference
+ * (src/jit/Blas/gemm_jit_plugin.cu:667-738, src/performance/auto_tuner.cu:100-295).
+ */
+int cuopx_tuning_load(const char* text);
+int cuopx_tuning_load_file(const char* path);
+int cuopx_tuning_clear(void);
+int cuopx_tuning_rows(void);
+int cuopx_set_gemm_variant(const char* name);
+const char* cuopx_gemm_variant_name(int index);
+
+/*
  * GEMM: C = alpha * op(A) * op(B) + beta * C, all row-major.
  *   op(A) is M x K: A is M x K (lda >= K) or, if transA, K x M (lda >= M).
  *   op(B) is K x N: B is K x N (ldb >= N) or, if transB, N x K (ldb >= K).

@@ -23,6 +23,17 @@ def pytest_collection_modifyitems(config, items):
             item.add_marker(skip)
 
 
+@pytest.fixture(scope="session", autouse=True)
+def _builtin_gemm_selection():
+    """Kernel-parity tests name the kernel each shape must reach under the
+    built-in selection; the shipped tuning table is cleared for the session
+    (tests of the table load their own)."""
+    from cuop_b200 import _native as N
+
+    N.lib().cuopx_tuning_clear()
+    yield
+
+
 @pytest.fixture(scope="session")
 def dev():
     import torch

@@ -27,6 +27,7 @@
 #include "jit/Blas/blas_jit_plugins.hpp"
 #include "jit/global_jit_manager.hpp"
 #include "jit/jit_wrapper.hpp"
+#include "performance/auto_tuner.hpp"
 
 extern "C" {
 void oracle_fill_uniform_f32(float* out, int64_t n, uint64_t seed, float lo, float hi);
@@ -232,6 +233,53 @@ TEST_GPU(ShapeMismatchIsReported) {
   EXPECT_TRUE(v.Forward(A, y) == StatusCode::SHAPE_MISMATCH);
 }
 
+TEST_HOST(AutoTunerGridRandomEarlyStopAndHistory) {
+  AutoTuner t;
+  TuningConfig cfg;
+  cfg.operator_name = "toy";
+  cfg.optimization_target = "throughput";
+  t.SetTuningConfig(cfg);
+  ParameterDefinition a{"a", ParameterType::INTEGER, "", {"1", "2", "3"}, "1"};
+  ParameterDefinition b{"b", ParameterType::ENUM, "", {"x", "y"}, "x"};
+  ParameterDefinition fixed{"c", ParameterType::STRING, "", {}, "keep"};
+  fixed.is_tunable = false;
+  t.AddParameter(a);
+  t.AddParameter(b);
+  t.AddParameter(fixed);
+  int calls = 0;
+  auto score = [&](const ParameterSet& p) {
+    ++calls;
+    EXPECT_TRUE(p.at("c") == "keep");
+    return std::stod(p.at("a")) * (p.at("b") == "y" ? 10.0 : 1.0);
+  };
+  TuningResult r = t.Tune("toy", score);
+  EXPECT_EQ(calls, 6);
+  EXPECT_TRUE(r.best_parameters.at("a") == "3" && r.best_parameters.at("b") == "y");
+  EXPECT_NEAR(r.best_performance, 30.0, 0.0);
+  cfg = t.GetTuningConfig();
+  cfg.optimization_target = "latency";  // minimise
+  cfg.tuning_strategy = "random";
+  t.SetTuningConfig(cfg);
+  r = t.Tune("toy", score);
+  EXPECT_TRUE(r.best_parameters.at("a") == "1" && r.best_parameters.at("b") == "x");
+  EXPECT_EQ(r.iterations_used, size_t(6));
+  cfg.tuning_strategy = "grid";
+  cfg.enable_early_stopping = true;
+  cfg.patience = 2;
+  t.SetTuningConfig(cfg);
+  r = t.Tune("toy", score);  // latency: 1,x is first and best -> stops after 2 more
+  EXPECT_EQ(r.iterations_used, size_t(3));
+  EXPECT_TRUE(r.converged);
+  const std::string path = "/tmp/cuop_autotuner_history.txt";
+  t.SaveTuningHistory(path);
+  AutoTuner u;
+  u.LoadTuningHistory(path);
+  auto h = u.GetTuningHistory();
+  EXPECT_EQ(h.size(), size_t(3));
+  EXPECT_TRUE(h[0].best_parameters.at("a") == "3");
+  EXPECT_NEAR(h[0].best_performance, 30.0, 1e-9);
+}
+
 // ------------------------------------------------------------------ GPU: seeded parity vs oracle
 TEST_GPU(GemmSeededMatchesOracleBitExact) {
   for (int t = 0; t < 4; ++t) {
@@ -317,6 +365,50 @@ TEST_GPU(VectorOperatorClasses) {
   EXPECT_TRUE(dd.Forward(Xd, Yd, rd) == StatusCode::UNSUPPORTED_TYPE);
   Tensor<float> short_y({size_t(n - 1)});
   EXPECT_TRUE(ax.Forward(X, short_y) == StatusCode::SHAPE_MISMATCH);
+}
+
+// The AutoTuner drives the GEMM variant override with a timing callback;
+// the winner becomes a selection-table row that Gemm<bf16> then follows.
+TEST_GPU(AutoTunerSelectsGemmVariantIntoTable) {
+  const int M = 1024, N = 1024, K = 1024;
+  Tensor<__nv_bfloat16> A({size_t(M), size_t(K)}), W({size_t(K), size_t(N)}), C({size_t(M), size_t(N)});
+  A.zero();
+  W.zero();
+  AutoTuner t;
+  TuningConfig cfg;
+  cfg.operator_name = "gemm_bf16_1024";
+  cfg.optimization_target = "latency";
+  t.SetTuningConfig(cfg);
+  t.AddParameter({"variant", ParameterType::ENUM, "", {"tc2", "tc_128x256", "tc_128x128"}, "tc2"});
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  TuningResult r = t.Tune("gemm", [&](const ParameterSet& p) {
+    cuopx_set_gemm_variant(p.at("variant").c_str());
+    float ms = 0.f;
+    for (int rep = 0; rep < 2; ++rep) {  // first pass warms up
+      cudaEventRecord(e0);
+      for (int i = 0; i < 5; ++i)
+        cuopx_gemm(CUOPX_BF16, 0, 0, M, N, K, 1.0, A.data(), K, W.data(), N, 0.0, C.data(), N, nullptr);
+      cudaEventRecord(e1);
+      cudaEventSynchronize(e1);
+      cudaEventElapsedTime(&ms, e0, e1);
+    }
+    cuopx_set_gemm_variant(nullptr);
+    return static_cast<double>(ms);
+  });
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  EXPECT_EQ(r.iterations_used, size_t(3));
+  const std::string best = r.best_parameters.at("variant");
+  const std::string row = "bf16 0 0 1024:1024 1024:1024 1024:1024 1:1 " + best + "\n";
+  EXPECT_EQ(cuopx_tuning_load(row.c_str()), CUOPX_SUCCESS);
+  Gemm<__nv_bfloat16> g;
+  g.SetWeight(W);
+  EXPECT_TRUE(g.Forward(A, C) == StatusCode::SUCCESS);
+  const std::string k = cuopx_last_kernel();
+  EXPECT_TRUE(best == "tc2" ? k == "gemm_tc2_256x256" : k == "gemm_" + best);
+  cuopx_tuning_clear();
 }
 
 TEST_GPU(GemvSeededMatchesOracle) {
@@ -491,6 +583,10 @@ TEST_GPU(MemoryPoolReusesAndLimits) {
   EXPECT_TRUE(q == p);
   EXPECT_TRUE(pool.GetStats().cache_hits >= 1);
   pool.Free(q, 4000);
+  // The limit counts reserved bytes (live + cached); idle cached blocks are
+  // released to make room, so start from an empty cache to make 64 MiB
+  // certainly exceed it.
+  pool.ReleaseCached();
   const auto reserved = pool.GetStats().bytes_reserved;
   pool.SetMemoryLimit(reserved + (1 << 20));
   EXPECT_TRUE(pool.Alloc(size_t(64) << 20) == nullptr);  // over the limit: refused on the host

@@ -106,3 +106,29 @@ def test_ops_refuse_cpu_tensors():
         cx.gemm(torch.zeros(4, 4), torch.zeros(4, 4))
     with pytest.raises(cx.CuopError):
         cx.gemv(torch.zeros(4, 4), torch.zeros(4))
+
+
+def test_tuning_table_parsing_without_gpu():
+    L = cx.lib()
+    names = []
+    i = 0
+    while L.cuopx_gemm_variant_name(i) is not None:
+        names.append(L.cuopx_gemm_variant_name(i).decode())
+        i += 1
+    assert names[0] == "auto" and {"tc2", "tc_128x256", "tc_128x128", "tf32x3_128x64", "ffma", "generic"} <= set(names)
+    try:
+        assert L.cuopx_tuning_load(b"# comment only\n\n") == N.SUCCESS and L.cuopx_tuning_rows() == 0
+        ok = b"bf16 0 0 256: 256: 256: 1:1 tc2   # trailing comment\nf32 * * * :255 * * ffma\n"
+        assert L.cuopx_tuning_load(ok) == N.SUCCESS and L.cuopx_tuning_rows() == 2
+        for bad in (b"bf16 0 0 256: 256: tc2\n", b"bf16 0 0 256: 256: 1: * bogus\n", b"x16 0 0 * * * * tc2\n",
+                    b"f32 2 0 * * * * tc2\n", b"f32 0 0 9:1 * * * tc2\n", b"f32 0 0 1-9 * * * tc2\n"):
+            assert L.cuopx_tuning_load(bad) == N.INVALID_ARGUMENT, bad
+        assert L.cuopx_tuning_rows() == 2  # a rejected table leaves the loaded one in place
+        assert L.cuopx_tuning_load_file(b"/nonexistent/table.txt") == N.INVALID_ARGUMENT
+        assert L.cuopx_set_gemm_variant(b"not-a-variant") == N.INVALID_ARGUMENT
+        assert L.cuopx_set_gemm_variant(b"ffma") == N.SUCCESS
+    finally:
+        L.cuopx_set_gemm_variant(None)
+        L.cuopx_tuning_clear()
+    assert L.cuopx_tuning_rows() == 0
+
