@@ -70,8 +70,9 @@ __global__ void __launch_bounds__(GS_THREADS, 2)
   const int64_t nvec = N / V;
   const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_cta;
   const int64_t r1 = min(M, r0 + rows_per_cta);
-  // Single-wave grid: the next kernel may start launching now (its CTAs
-  // wait for free slots and for this grid's completion).
+  // The next kernel may start launching once every CTA of this grid has
+  // started (its CTAs then take slots freed by exiting CTAs and wait for
+  // this grid's completion before touching memory).
   grid_dependency_wait();
   grid_launch_dependents();
   if (r0 >= r1) return;
@@ -189,12 +190,26 @@ __global__ void __launch_bounds__(GS_THREADS, 2)
         for (int i = 0; i < V; ++i) acc[i] = fma(f[i], xv[u], acc[i]);
       }
     }
-    for (; j < j1; ++j) {
-      const Acc xj = to_acc<T>(__ldg(x + j));
-      Acc f[V];
-      unpack_v<T>(ld_nc16(ap + j * lda), f);
+    if (j < j1) {
+      // Remainder (< U rows): one predicated batch, all loads in flight at
+      // once, added in the same ascending row order.
+      uint4 v[U];
+      Acc xv[U];
 #pragma unroll
-      for (int i = 0; i < V; ++i) acc[i] = fma(f[i], xj, acc[i]);
+      for (int u = 0; u < U; ++u) {
+        const bool in = j + u < j1;
+        v[u] = in ? ld_nc16(ap + (j + u) * lda) : make_uint4(0, 0, 0, 0);
+        xv[u] = in ? to_acc<T>(__ldg(x + j + u)) : Acc(0);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (j + u < j1) {
+          Acc f[V];
+          unpack_v<T>(v[u], f);
+#pragma unroll
+          for (int i = 0; i < V; ++i) acc[i] = fma(f[i], xv[u], acc[i]);
+        }
+      }
     }
   }
 
@@ -229,14 +244,24 @@ __global__ void __launch_bounds__(GS_THREADS, 2)
 #pragma unroll
     for (int i = 0; i < V; ++i) sum[i] = 0;
     // Split order 0..splits-1; loads issued GS_T_RED_BATCH at a time.
+    // V partials of one split are V * sizeof(Acc) contiguous, 16-byte
+    // aligned bytes (M % V == 0, 256-byte aligned workspace): vector loads.
+    constexpr int QN = V * static_cast<int>(sizeof(Acc)) / 16;
+    static_assert(QN * 16 == V * static_cast<int>(sizeof(Acc)), "partial vector size");
     for (unsigned int k0 = 0; k0 < splits; k0 += GS_T_RED_BATCH) {
       Acc pv[GS_T_RED_BATCH][V];
 #pragma unroll
       for (int b = 0; b < GS_T_RED_BATCH; ++b) {
         const unsigned int k = k0 + b;
+        union {
+          uint4 q[QN];
+          Acc a[V];
+        } u;
+        const uint4* src = reinterpret_cast<const uint4*>(partials + static_cast<int64_t>(k) * M + col);
 #pragma unroll
-        for (int i = 0; i < V; ++i)
-          pv[b][i] = (k < splits) ? __ldcg(partials + static_cast<int64_t>(k) * M + col + i) : Acc(0);
+        for (int q = 0; q < QN; ++q) u.q[q] = (k < splits) ? __ldcg(src + q) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int i = 0; i < V; ++i) pv[b][i] = u.a[i];
       }
 #pragma unroll
       for (int b = 0; b < GS_T_RED_BATCH; ++b)
@@ -283,7 +308,9 @@ GemvStreamPlan plan_gemv_stream(int trans, int64_t M, int64_t N, int64_t lda, co
     int kv = 1;
     while (kv * 32 * GS_WARPS < nvec) kv *= 2;
     p.kv = kv;
-    int64_t rows = (M + ctas_full - 1) / ctas_full;
+    // Two waves of CTAs: a CTA that finishes early picks up a second row
+    // block, which evens out per-SM bandwidth differences at the tail.
+    int64_t rows = (M + 2 * ctas_full - 1) / (2 * ctas_full);
     rows = std::min<int64_t>(std::max<int64_t>(rows, 1), GS_ROWS_MAX);
     p.rows_per_cta = static_cast<int>(rows);
     p.grid = (M + rows - 1) / rows;
@@ -296,7 +323,9 @@ GemvStreamPlan plan_gemv_stream(int trans, int64_t M, int64_t N, int64_t lda, co
     int64_t splits = std::max<int64_t>(1, ctas_full / p.strips);
     splits = std::min<int64_t>(splits, std::max<int64_t>(1, N / GS_T_UNROLL));
     splits = std::min<int64_t>(splits, 65535);
-    p.rows_per_split = (N + splits - 1) / splits;
+    // Whole batches of GS_T_UNROLL rows per split (only the last split may
+    // end in a partial batch).
+    p.rows_per_split = ((N + splits - 1) / splits + GS_T_UNROLL - 1) / GS_T_UNROLL * GS_T_UNROLL;
     p.splits = (N + p.rows_per_split - 1) / p.rows_per_split;
     if (p.splits > 1) p.partial_bytes = (static_cast<size_t>(p.splits) * M * sizeof(Acc) + 255) / 256 * 256;
     p.trans = true;
