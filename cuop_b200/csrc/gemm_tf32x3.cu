@@ -14,9 +14,11 @@
 //               "hi" buffers of a STAGES-deep ring: 128-byte swizzle for
 //               K-major operands, 128-byte swizzle with 32-byte atoms for
 //               MN-major ones (the only MN-major layout tf32 MMAs accept).
-//   warps 6..13 converters: wait for a landed stage, rewrite hi in place and
-//               write lo next to it (same swizzled layout: the split is
-//               elementwise), fence the async proxy, signal the MMA warp.
+//   warps 6..13 converters: wait for a landed stage; split K-major A straight
+//               into TMEM (tcgen05.st, one tile row per thread, the MMAs read
+//               A from TMEM), split B (and an MN-major A) in place in shared
+//               memory with lo next to it (same swizzled layout: the split is
+//               elementwise); fence, signal the MMA warp.
 //   warp 1      TMEM allocator + MMA issuer: 3 x (BK/8) MMAs (M=128, N=BN,
 //               K=8) per stage, commit frees the stage / hands off the tile.
 //   warps 2..5  epilogue: tcgen05.ld, alpha/beta, swizzled staging, TMA store.
@@ -119,6 +121,13 @@ __global__ void __launch_bounds__(X3_THREADS, 1)
   constexpr uint32_t STAGE_TX = static_cast<uint32_t>(L::A_BYTES + L::B_BYTES);
   constexpr uint32_t IDESC = make_idesc(2u /*tf32*/, A_MN, B_MN, X3_BM, BN);
   constexpr uint32_t CHUNK_BYTES = 32 * X3_BK * 4;  // one 32 x 32 fp32 box = 4 KB
+  // K-major A is split straight into TMEM (the MMAs read A from there), so
+  // only B's split goes back through shared memory.  TMEM: two accumulators
+  // (2 x BN columns), then per stage 32 hi + 32 lo columns of A.
+  constexpr bool A_TMEM = !A_MN;
+  constexpr uint32_t A_COL0 = 2 * BN;
+  constexpr uint32_t TMEM_COLS = A_TMEM ? 512u : L::TMEM_COLS;
+  static_assert(!A_TMEM || A_COL0 + STAGES * 2 * X3_BK <= 512, "TMEM budget");
 
   extern __shared__ __align__(1024) unsigned char x3_smem_raw[];
   unsigned char* smem = align_smem_1024(x3_smem_raw);
@@ -153,7 +162,7 @@ __global__ void __launch_bounds__(X3_THREADS, 1)
     prefetch_tmap(&tmC);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, L::TMEM_COLS);
+    tmem_alloc(tmem_slot, TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before_sync();
@@ -232,8 +241,35 @@ __global__ void __launch_bounds__(X3_THREADS, 1)
           ok = false;
           break;
         }
-        split_tf32<L::A_BYTES, X3_CONV_WARPS * 32>(L::a_hi(smem, stage), L::a_lo(smem, stage), ctid);
-        split_tf32<L::B_BYTES, X3_CONV_WARPS * 32>(L::b_hi(smem, stage), L::b_lo(smem, stage), ctid);
+        if constexpr (A_TMEM) {
+          // This warp owns TMEM lane quarter q (tile rows 32q..32q+31) and
+          // K columns 16h..16h+15 of the stage; each thread splits its row.
+          const int q = warp & 3;
+          const int h = (warp - 6) >> 2;
+          const int r = 32 * q + lane;
+          const unsigned char* arow = L::a_hi(smem, stage) + r * 128;  // 128-byte swizzled row
+          uint32_t hi[16], lo[16];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const float4 v = *reinterpret_cast<const float4*>(arow + (((4 * h + c) ^ (r & 7)) << 4));
+            const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              hi[4 * c + i] = to_tf32_rna(e[i]);
+              lo[4 * c + i] = __float_as_uint(__fsub_rn(e[i], __uint_as_float(hi[4 * c + i])));
+            }
+          }
+          const uint32_t tcol = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + A_COL0 +
+                                static_cast<uint32_t>(stage * 2 * X3_BK + 16 * h);
+          tmem_st_32x32b_x16(tcol, hi);
+          tmem_st_32x32b_x16(tcol + X3_BK, lo);
+          split_tf32<L::B_BYTES, X3_CONV_WARPS * 32>(L::b_hi(smem, stage), L::b_lo(smem, stage), ctid);
+          tmem_wait_st();
+          tc_fence_before_sync();
+        } else {
+          split_tf32<L::A_BYTES, X3_CONV_WARPS * 32>(L::a_hi(smem, stage), L::a_lo(smem, stage), ctid);
+          split_tf32<L::B_BYTES, X3_CONV_WARPS * 32>(L::b_hi(smem, stage), L::b_lo(smem, stage), ctid);
+        }
         fence_proxy_async_shared();  // generic-proxy writes -> visible to the tensor cores
         __syncwarp();
         if (lane == 0) mbar_arrive(&conv[stage]);
@@ -278,9 +314,16 @@ __global__ void __launch_bounds__(X3_THREADS, 1)
                                       : make_smem_desc_sw128(bh + bo, 16, 1024);
             const uint64_t dbl = B_MN ? make_smem_desc_sw128_32b(bl + bo, CHUNK_BYTES, 512)
                                       : make_smem_desc_sw128(bl + bo, 16, 1024);
-            umma_tf32(d_tmem, dal, dbh, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);  // small terms first
-            umma_tf32(d_tmem, dah, dbl, IDESC, 1u);
-            umma_tf32(d_tmem, dah, dbh, IDESC, 1u);
+            if constexpr (A_TMEM) {
+              const uint32_t ta = tmem_base + A_COL0 + static_cast<uint32_t>(stage * 2 * X3_BK + kk * 8);
+              umma_tf32_a_tmem(d_tmem, ta + X3_BK, dbh, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);  // lo*hi first
+              umma_tf32_a_tmem(d_tmem, ta, dbl, IDESC, 1u);
+              umma_tf32_a_tmem(d_tmem, ta, dbh, IDESC, 1u);
+            } else {
+              umma_tf32(d_tmem, dal, dbh, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);  // small terms first
+              umma_tf32(d_tmem, dah, dbl, IDESC, 1u);
+              umma_tf32(d_tmem, dah, dbh, IDESC, 1u);
+            }
           }
           issued = true;
           umma_commit(&empty[stage]);
@@ -369,7 +412,7 @@ __global__ void __launch_bounds__(X3_THREADS, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after_sync();
-    tmem_dealloc(tmem_base, L::TMEM_COLS);
+    tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
