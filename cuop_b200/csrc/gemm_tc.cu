@@ -561,10 +561,12 @@ bool gemm_tc_supported(const GemmProblem& p) {
 
 int gemm_tc(const GemmProblem& p, cudaStream_t stream, int bn) {
   if (bn == 0 && gemm_tc2_wanted(p)) return gemm_tc2(p, stream);
-  // BN=256 when N fills it and the tile count still covers the SMs; else BN=128.
+  // BN=256 when N fills it and there are at least half as many 128 x 256
+  // tiles as SMs (measured on B200: fewer, wider tiles beat a second wave of
+  // 128 x 128 tiles); else BN=128.
   const int sms = device_sm_count();
   const int64_t tiles256 = ((p.M + BM - 1) / BM) * ((p.N + 255) / 256) * p.batch;
-  const bool wide = bn ? bn == 256 : (p.N > 128 && tiles256 >= sms);
+  const bool wide = bn ? bn == 256 : (p.N > 128 && tiles256 >= sms / 2);
   if (p.dtype == CUOPX_BF16) {
     return wide ? launch_tc_layout<__nv_bfloat16, 256, 4>(p, stream, "gemm_tc_128x256")
                 : launch_tc_layout<__nv_bfloat16, 128, 6>(p, stream, "gemm_tc_128x128");

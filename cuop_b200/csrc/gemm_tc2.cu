@@ -631,10 +631,14 @@ int launch_tc2(const GemmProblem& p, cudaStream_t stream, const char* name, void
 }  // namespace
 
 bool gemm_tc2_wanted(const GemmProblem& p) {
-  // Pair tiles pay off when there are enough 256 x 256 tiles to fill the SMs.
+  // Pair tiles halve shared-memory operand traffic per FLOP, which pays off
+  // over long K loops (measured on B200: from K ~ 8192 with at least 64 pair
+  // tiles, or from K = 4096 on very large outputs); shorter K loops are
+  // faster on the 1-SM 128 x 256 tile, whose epilogue overlaps better.
   if (!gemm_tc_supported(p)) return false;
+  if (p.M < 256 || p.N < 256 || p.K < 256) return false;
   const int64_t tiles = ((p.M + 255) / 256) * ((p.N + 255) / 256) * p.batch;
-  return p.M >= 256 && p.N >= 256 && p.K >= 256 && tiles >= device_sm_count() / 2;
+  return (p.K >= 6144 && tiles >= 64) || (p.K >= 4096 && tiles >= 512);
 }
 
 int gemm_tc2(const GemmProblem& p, cudaStream_t stream) { return gemm_tc2_peers(p, nullptr, 0, stream); }

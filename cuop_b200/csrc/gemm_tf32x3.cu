@@ -492,7 +492,9 @@ int gemm_tf32x3(const GemmProblem& p, cudaStream_t stream, int bn) {
   if (bn == 0) {
     const int sms = device_sm_count();
     const int64_t tiles128 = ((p.M + X3_BM - 1) / X3_BM) * ((p.N + 127) / 128) * p.batch;
-    bn = (p.N > 64 && tiles128 >= sms) ? 128 : 64;
+    // 128 x 128 tiles halve B traffic per FLOP; measured on B200 they win
+    // from about two thirds of an SM wave of them.
+    bn = (p.N > 64 && tiles128 * 3 >= sms * 2) ? 128 : 64;
   }
   if (bn == 128) return launch_x3_layout<128, 3>(p, stream, "gemm_tf32x3_128x128");
   return launch_x3_layout<64, 4>(p, stream, "gemm_tf32x3_128x64");

@@ -4,10 +4,11 @@ cuopx_set_gemm_variant).
 
     python -m cuop_b200.tuning --out cuop_b200/tuning_b200.txt
 
-times every applicable variant on one representative problem per size
-bucket (CUDA events over a CUDA graph of back-to-back launches, inputs
-resident) and writes one table row per bucket naming the fastest variant,
-with the measured times in a comment.  `cuop_b200` loads
+times the built-in choice and every applicable variant on a grid of
+problem sizes (CUDA events over a CUDA graph of back-to-back launches,
+inputs resident) and writes a rule, covering sizes within a factor sqrt(2)
+of the measured point, wherever a variant beats the built-in choice by more
+than 5 %, with the measured times in a comment.  `cuop_b200` loads
 `tuning_b200.txt` when the library is first opened; the C++ facade loads a
 table with cuopx_tuning_load_file.
 """
@@ -31,11 +32,14 @@ CANDIDATES = {
     N.F32: ["tf32x3_128x64", "tf32x3_128x128", "ffma"],
 }
 
-# Size buckets: (lo, hi) inclusive, hi None = unbounded; the representative
-# size is hi/2 (4x lo, capped, for the open bucket).
-MN_BUCKETS = [(1, 512), (513, 2048), (2049, None)]
-K_BUCKETS = [(1, 1024), (1025, None)]
-BATCH_BUCKETS = [(1, 1), (2, None)]
+# Sweep grid: problems at powers of two; a rule covers the sizes within a
+# factor sqrt(2) of its measured point, and is written only where a variant
+# beats the built-in choice by more than MARGIN (the built-in thresholds stay
+# in charge everywhere else).
+MN_POINTS = [256, 512, 1024, 2048, 4096, 8192]
+K_POINTS = [256, 1024, 4096, 8192]
+BATCHED_POINTS = [(64, 64, 64), (128, 128, 64), (128, 128, 128), (256, 256, 64), (256, 256, 256), (512, 512, 128)]
+MARGIN = 0.05
 
 
 def variant_names() -> list[str]:
@@ -70,18 +74,14 @@ def force(variant: Optional[str]) -> None:
             f"cuopx_set_gemm_variant({variant})")
 
 
-def _rep(lo: int, hi: Optional[int], cap: int) -> int:
-    if hi is None:
-        return min(cap, 4 * lo) // 64 * 64 or 64
-    return max(64, hi // 2 // 64 * 64)
-
-
-def _fmt_range(lo: int, hi: Optional[int]) -> str:
-    return f"{lo}:{'' if hi is None else hi}"
+def _around(p: int) -> str:
+    """Inclusive range of sizes within a factor sqrt(2) of p."""
+    return f"{int(p * 0.7072) + 1}:{int(p * 1.4142)}"
 
 
 def time_variant(variant: str, A, B, C, batch: int, launches: int = 10) -> Optional[float]:
-    """Median ms per launch of `variant` (None when it cannot run the problem)."""
+    """Median ms per launch of `variant` ("auto": the built-in choice; None
+    when the variant cannot run the problem)."""
     import torch
     from . import ops
 
@@ -91,12 +91,12 @@ def time_variant(variant: str, A, B, C, batch: int, launches: int = 10) -> Optio
         else:
             ops.gemm(A, B, C)
 
-    force(variant)
+    force(None if variant == "auto" else variant)
     try:
         run()
         torch.cuda.synchronize()
         got = ops.last_kernel()
-        if not _kernel_matches(variant, got):
+        if variant != "auto" and not _kernel_matches(variant, got):
             return None  # declined: the built-in choice ran instead
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
@@ -125,38 +125,36 @@ def _kernel_matches(variant: str, kernel: str) -> bool:
 
 
 def sweep(dtypes: Iterable[int] = (N.F16, N.BF16, N.F32), cap: int = 8192, log=print) -> list[str]:
-    """Time the candidates on one problem per bucket; returns table lines."""
+    """Time the built-in choice and every candidate on the sweep grid; returns
+    table lines (rules only where a candidate wins by more than MARGIN)."""
     import torch
 
     dev = torch.device("cuda", torch.cuda.current_device())
     tdt = {N.F16: torch.float16, N.BF16: torch.bfloat16, N.F32: torch.float32}
-    lines = ["# dtype transA transB M N K batch variant   (fastest measured; times in ms per launch)"]
+    lines = ["# dtype transA transB M N K batch variant   (measured point: built-in time vs winner, ms per launch)"]
     clear()
+    shapes = [(m, n, k, 1) for m, n, k in itertools.product(MN_POINTS, MN_POINTS, K_POINTS)
+              if max(m, n, k) <= cap]
+    shapes += [(m, n, k, max(2, (64 << 20) // (m * n * 2))) for m, n, k in BATCHED_POINTS]
     for dt in dtypes:
-        for (mlo, mhi), (nlo, nhi), (klo, khi), (blo, bhi) in itertools.product(MN_BUCKETS, MN_BUCKETS, K_BUCKETS,
-                                                                                BATCH_BUCKETS):
-            M, Nn, K = _rep(mlo, mhi, cap), _rep(nlo, nhi, cap), _rep(klo, khi, cap)
-            batch = 1 if bhi == 1 else max(2, min(256, (64 << 20) // max(1, M * Nn * 2)))
-            if batch > 1 and M * Nn * K > (1 << 30):
-                continue  # large batched problems behave like the non-batched bucket
-            shape = (batch, M, K) if batch > 1 else (M, K)
-            A = torch.randn(*shape, device=dev).to(tdt[dt])
+        for M, Nn, K, batch in shapes:
+            shape_a = (batch, M, K) if batch > 1 else (M, K)
+            A = torch.randn(*shape_a, device=dev).to(tdt[dt])
             B = torch.randn(*((batch, K, Nn) if batch > 1 else (K, Nn)), device=dev).to(tdt[dt])
             C = torch.empty(*((batch, M, Nn) if batch > 1 else (M, Nn)), device=dev, dtype=tdt[dt])
-            times = {}
-            for v in CANDIDATES[dt]:
-                t = time_variant(v, A, B, C, batch)
-                if t is not None:
-                    times[v] = t
+            t_auto = time_variant("auto", A, B, C, batch)
+            times = {v: t for v in CANDIDATES[dt] if (t := time_variant(v, A, B, C, batch)) is not None}
             del A, B, C
             if not times:
                 continue
             best = min(times, key=times.get)
-            row = (f"{_DT_NAME[dt]} 0 0 {_fmt_range(mlo, mhi)} {_fmt_range(nlo, nhi)} {_fmt_range(klo, khi)} "
-                   f"{_fmt_range(blo, bhi)} {best}")
-            note = ", ".join(f"{k} {v:.4f}" for k, v in sorted(times.items(), key=lambda kv: kv[1]))
-            lines.append(f"{row}   # {M}x{Nn}x{K} batch {batch}: {note}")
-            log(lines[-1])
+            desc = f"{M}x{Nn}x{K} batch {batch}: built-in {t_auto:.4f}, {best} {times[best]:.4f}"
+            if times[best] < (1.0 - MARGIN) * t_auto:
+                bat = "1:1" if batch == 1 else "2:"
+                lines.append(f"{_DT_NAME[dt]} 0 0 {_around(M)} {_around(Nn)} {_around(K)} {bat} {best}   # {desc}")
+                log(lines[-1])
+            else:
+                log(f"# keep built-in  {_DT_NAME[dt]} {desc}")
     return lines
 
 

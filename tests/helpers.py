@@ -1,4 +1,6 @@
 """Shared helpers for the GPU parity tests."""
+from contextlib import contextmanager
+
 import numpy as np
 import torch
 
@@ -31,3 +33,17 @@ def fp32_reference_gpu(A: torch.Tensor, B: torch.Tensor, transA=False, transB=Fa
         return a @ b
     finally:
         torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+@contextmanager
+def forced_variant(name):
+    """Run a block with one GEMM variant forced (cuopx_set_gemm_variant), so a
+    parity test exercises that kernel whatever the size thresholds choose."""
+    from cuop_b200 import tuning
+
+    tuning.force(name)
+    try:
+        yield
+    finally:
+        tuning.force(None)
+

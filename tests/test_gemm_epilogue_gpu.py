@@ -14,7 +14,7 @@ import torch
 import cuop_b200 as cx
 import oracle as O
 from cuop_b200 import _native as N
-from helpers import lowp_bits, to_dev_f32, to_dev_lowp
+from helpers import forced_variant, lowp_bits, to_dev_f32, to_dev_lowp
 
 pytestmark = pytest.mark.gpu
 LOWP_TOL = 1e-2
@@ -88,8 +88,9 @@ def test_lowp_epilogue_vs_oracle(dev, dt, M, N, K, kernel, bias, relu):
     b = O.to_lowp(O.normal(N, seed=K), dt) if bias else None
     C0 = O.to_lowp(O.normal((M, N), seed=11), dt)
     Cd = to_dev_lowp(C0, dt, dev)
-    cx.gemm(to_dev_lowp(A, dt, dev), to_dev_lowp(B, dt, dev), Cd, alpha=1.25, beta=0.5,
-            bias=None if b is None else to_dev_lowp(b, dt, dev), relu=relu)
+    with forced_variant("tc2" if kernel == "gemm_tc2_" else None):
+        cx.gemm(to_dev_lowp(A, dt, dev), to_dev_lowp(B, dt, dev), Cd, alpha=1.25, beta=0.5,
+                bias=None if b is None else to_dev_lowp(b, dt, dev), relu=relu)
     assert cx.last_kernel().startswith(kernel), cx.last_kernel()
     rows = np.arange(M) if M <= 512 else np.array([0, 1, 255, 256, 2047, M - 1])
     ref = O.gemm_lowp(dt, A[rows], B, C0[rows], alpha=1.25, beta=0.5, bias=b, relu=relu)

@@ -16,7 +16,7 @@ import torch
 
 import cuop_b200 as cx
 import oracle as O
-from helpers import TDT, fp32_reference_gpu, lowp_bits, to_dev_f32, to_dev_lowp
+from helpers import TDT, forced_variant, fp32_reference_gpu, lowp_bits, to_dev_f32, to_dev_lowp
 
 pytestmark = pytest.mark.gpu
 GOLD = json.loads((Path(__file__).parent / "golden" / "known_answers.json").read_text())
@@ -164,7 +164,7 @@ def test_lowp_tcgen05_vs_oracle(dev, dt, M, N, K, tA, tB):
     assert err <= LOWP_TOL, (err, cx.last_kernel())
 
 
-PAIR_CASES = [  # enough 256x256 tiles to take the two-SM (cta_group::2) kernel
+PAIR_CASES = [  # the two-SM (cta_group::2) kernel, forced (ragged and transposed shapes)
     (4096, 2560, 512, False, False), (4000, 2600, 520, False, False), (2560, 4096, 256, True, False),
     (2560, 4096, 256, False, True), (2560, 4096, 256, True, True), (3072, 3072, 1000, False, False),
 ]
@@ -177,7 +177,8 @@ def test_lowp_pair_kernel_vs_oracle(dev, dt, M, N, K, tA, tB):
     B = O.to_lowp(O.normal((N, K) if tB else (K, N), seed=N + 13), dt)
     C0 = O.to_lowp(O.normal((M, N), seed=17), dt)
     Cd = to_dev_lowp(C0, dt, dev)
-    cx.gemm(to_dev_lowp(A, dt, dev), to_dev_lowp(B, dt, dev), Cd, transA=tA, transB=tB, alpha=1.5, beta=0.5)
+    with forced_variant("tc2"):
+        cx.gemm(to_dev_lowp(A, dt, dev), to_dev_lowp(B, dt, dev), Cd, transA=tA, transB=tB, alpha=1.5, beta=0.5)
     assert cx.last_kernel() == "gemm_tc2_256x256", cx.last_kernel()
     full = 1.5 * fp32_reference_gpu(to_dev_lowp(A, dt, dev), to_dev_lowp(B, dt, dev), tA, tB) + \
         0.5 * to_dev_lowp(C0, dt, dev).float()
