@@ -11,6 +11,7 @@ from __future__ import annotations
 import os
 import shutil
 import subprocess
+from typing import Optional
 import sys
 from pathlib import Path
 
@@ -45,7 +46,7 @@ def _sources() -> list[Path]:
 
 def _deps() -> list[Path]:
     deps = list(CSRC.rglob("*.cu")) + list(CSRC.rglob("*.cuh")) + list(CSRC.rglob("*.h"))
-    deps += list(CSRC.rglob("*.cpp")) + list((ROOT / "include").rglob("*.h*"))
+    deps += list((CSRC / "host").glob("*.cpp")) + list((ROOT / "include").rglob("*.h*"))
     return deps
 
 
@@ -56,8 +57,43 @@ def needs_rebuild() -> bool:
     return any(p.stat().st_mtime > t for p in _deps())
 
 
+CORE_SRC = CSRC / "python" / "core.cpp"
+
+
+def core_module_path() -> Path:
+    import sysconfig
+
+    return PKG / ("core" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
+
+
+def build_core_module(force: bool = False, verbose: bool = False) -> Optional[Path]:
+    """pybind11 module `cuop_b200.core` (the reference's Python operator
+    classes over the C++ facade), linked against libcuopx.so; None when
+    pybind11 is not importable."""
+    import sysconfig
+
+    try:
+        import pybind11
+    except ImportError:
+        return None
+    out = core_module_path()
+    deps = [CORE_SRC, LIB] + list((ROOT / "include").rglob("*.h*"))
+    if not force and out.exists() and all(out.stat().st_mtime >= d.stat().st_mtime for d in deps):
+        return out
+    cmd = [_nvcc(), "-O2", "-std=c++17", "-Xcompiler", "-fPIC", "-shared", f"-I{pybind11.get_include()}",
+           f"-I{sysconfig.get_paths()['include']}", f"-I{ROOT / 'include'}", f"-I{ROOT / 'include' / 'cuop'}",
+           str(CORE_SRC), "-o", str(out), f"-L{PKG}", "-lcuopx", "-Xlinker", "-rpath=$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd), file=sys.stderr)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"building {out.name} failed:\n{r.stderr[-4000:]}")
+    return out
+
+
 def build(force: bool = False, verbose: bool = False) -> Path:
     if not force and not needs_rebuild():
+        build_core_module(verbose=verbose)
         return LIB
     BUILD_DIR.mkdir(exist_ok=True)
     nvcc = _nvcc()
@@ -85,6 +121,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stderr[-4000:]}")
     os.replace(tmp, LIB)
+    build_core_module(force=True, verbose=verbose)
     return LIB
 
 
