@@ -16,6 +16,7 @@ Two oracles:
 from __future__ import annotations
 
 import ctypes as C
+import os
 from pathlib import Path
 
 import numpy as np
@@ -72,7 +73,14 @@ def _p(a: np.ndarray) -> int:
 
 
 def threads() -> int:
-    return int(lib().oracle_max_threads())
+    """Host threads available to this process (its CPU affinity), not
+    OMP_NUM_THREADS: launchers such as torch.distributed.run set that to 1
+    per worker, and the CPU baselines are meant to use the whole host.  Every
+    oracle call passes its thread count explicitly."""
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except (AttributeError, OSError):
+        return max(1, int(lib().oracle_max_threads()))
 
 
 # ------------------------------------------------------------ generators
