@@ -47,12 +47,14 @@ struct X3Params {
   int epi;           // CUOPX_EPI_* flags
 };
 
-template <int BN, int STAGES>
+// A_LO: the stage also holds A's lo part in shared memory (MN-major A);
+// K-major A is split into TMEM instead, and its stages are 16 KB smaller.
+template <int BN, int STAGES, bool A_LO = true>
 struct X3Smem {
   static constexpr int A_BYTES = X3_BM * X3_BK * 4;  // 16 KB
   static constexpr int B_BYTES = BN * X3_BK * 4;
-  static constexpr int STAGE = 2 * (A_BYTES + B_BYTES);  // A_hi, A_lo, B_hi, B_lo
-  static constexpr int C_STAGE = 32 * X3_CHUNK * 4;       // 4 KB
+  static constexpr int STAGE = (A_LO ? 2 : 1) * A_BYTES + 2 * B_BYTES;  // A_hi[, A_lo], B_hi, B_lo
+  static constexpr int C_STAGE = 32 * X3_CHUNK * 4;                      // 4 KB
   static constexpr int OFF_C = STAGES * STAGE;
   static constexpr int OFF_BAR = OFF_C + X3_EPI_WARPS * 2 * C_STAGE;
   // full[S], conv[S], empty[S], acc_full[2], acc_empty[2], drain
@@ -62,10 +64,11 @@ struct X3Smem {
   static_assert(ALLOC <= 232448, "shared memory budget exceeded");
   static constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulator buffers
   static_assert(TMEM_COLS == 128 || TMEM_COLS == 256, "TMEM allocation must be a power of two >= 32");
+  static constexpr int A_OFF = (A_LO ? 2 : 1) * A_BYTES;  // start of B_hi within a stage
   __device__ static unsigned char* a_hi(unsigned char* s, int st) { return s + st * STAGE; }
   __device__ static unsigned char* a_lo(unsigned char* s, int st) { return s + st * STAGE + A_BYTES; }
-  __device__ static unsigned char* b_hi(unsigned char* s, int st) { return s + st * STAGE + 2 * A_BYTES; }
-  __device__ static unsigned char* b_lo(unsigned char* s, int st) { return s + st * STAGE + 2 * A_BYTES + B_BYTES; }
+  __device__ static unsigned char* b_hi(unsigned char* s, int st) { return s + st * STAGE + A_OFF; }
+  __device__ static unsigned char* b_lo(unsigned char* s, int st) { return s + st * STAGE + A_OFF + B_BYTES; }
 };
 
 __device__ __forceinline__ void x3_tile_coords(int t, const X3Params& p, int& b, int& mt, int& nt) {
@@ -117,7 +120,7 @@ template <int BN, int STAGES, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(X3_THREADS, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ CUtensorMap tmC, const X3Params p) {
-  using L = X3Smem<BN, STAGES>;
+  using L = X3Smem<BN, STAGES, A_MN>;
   constexpr uint32_t STAGE_TX = static_cast<uint32_t>(L::A_BYTES + L::B_BYTES);
   constexpr uint32_t IDESC = make_idesc(2u /*tf32*/, A_MN, B_MN, X3_BM, BN);
   constexpr uint32_t CHUNK_BYTES = 32 * X3_BK * 4;  // one 32 x 32 fp32 box = 4 KB
@@ -418,7 +421,7 @@ __global__ void __launch_bounds__(X3_THREADS, 1)
 
 template <int BN, int STAGES, bool A_MN, bool B_MN>
 int launch_x3(const GemmProblem& p, cudaStream_t stream, const char* name) {
-  using L = X3Smem<BN, STAGES>;
+  using L = X3Smem<BN, STAGES, A_MN>;
   const auto dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   CUtensorMap mA, mB, mC;
   bool ok = true;
@@ -464,13 +467,15 @@ int launch_x3(const GemmProblem& p, cudaStream_t stream, const char* name) {
   return check_launch();
 }
 
-template <int BN, int STAGES>
+// Stage counts: K-major A (A split in TMEM, smaller stages) runs deeper
+// rings — 6 x 64 or 4 x 64 TMEM columns of A next to the accumulators.
+template <int BN, int STAGES_TMEM_A, int STAGES_SMEM_A>
 int launch_x3_layout(const GemmProblem& p, cudaStream_t stream, const char* name) {
   const bool a_mn = p.transA, b_mn = !p.transB;
-  if (!a_mn && b_mn) return launch_x3<BN, STAGES, false, true>(p, stream, name);
-  if (!a_mn && !b_mn) return launch_x3<BN, STAGES, false, false>(p, stream, name);
-  if (a_mn && b_mn) return launch_x3<BN, STAGES, true, true>(p, stream, name);
-  return launch_x3<BN, STAGES, true, false>(p, stream, name);
+  if (!a_mn && b_mn) return launch_x3<BN, STAGES_TMEM_A, false, true>(p, stream, name);
+  if (!a_mn && !b_mn) return launch_x3<BN, STAGES_TMEM_A, false, false>(p, stream, name);
+  if (a_mn && b_mn) return launch_x3<BN, STAGES_SMEM_A, true, true>(p, stream, name);
+  return launch_x3<BN, STAGES_SMEM_A, true, false>(p, stream, name);
 }
 
 }  // namespace
@@ -496,8 +501,8 @@ int gemm_tf32x3(const GemmProblem& p, cudaStream_t stream, int bn) {
     // from about two thirds of an SM wave of them.
     bn = (p.N > 64 && tiles128 * 3 >= sms * 2) ? 128 : 64;
   }
-  if (bn == 128) return launch_x3_layout<128, 3>(p, stream, "gemm_tf32x3_128x128");
-  return launch_x3_layout<64, 4>(p, stream, "gemm_tf32x3_128x64");
+  if (bn == 128) return launch_x3_layout<128, 4, 3>(p, stream, "gemm_tf32x3_128x128");
+  return launch_x3_layout<64, 6, 4>(p, stream, "gemm_tf32x3_128x64");
 }
 
 }  // namespace cuopx
