@@ -1,7 +1,7 @@
 // GlobalJITManager (reference include/jit/global_jit_manager.hpp): process-wide
 // plugin configuration.  Save/LoadCacheFromFile persist the per-operator
-// configurations (kernel_type etc.) as plain text; there is no compiled-code
-// cache in this build.
+// configurations (kernel_type etc.) as plain text; the library compiles no
+// code at run time, so there is no compiled-code cache.
 #pragma once
 
 #include <mutex>

@@ -1,8 +1,8 @@
 // Configuration and profile structs of the plugin interface, with the field
 // names and defaults of the reference's include/jit/jit_config.hpp:11-149 so
-// existing configuration code keeps compiling.  In this build there is no
-// runtime code generation: JITConfig.kernel_type names a precompiled sm_100a
-// variant family ("auto"/"default" = the built-in selection table).
+// existing configuration code keeps compiling.  The library generates no
+// code at run time: JITConfig.kernel_type names a precompiled sm_100a
+// variant family ("auto"/"default" = the built-in selection).
 #pragma once
 
 #include <string>
