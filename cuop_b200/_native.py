@@ -55,6 +55,7 @@ SIGNATURES = [
     ("cuopx_tuning_clear", _int, []),
     ("cuopx_tuning_rows", _int, []),
     ("cuopx_set_gemm_variant", _int, [C.c_char_p]),
+    ("cuopx_set_gemm_variant_thread", _int, [C.c_char_p]),
     ("cuopx_gemm_variant_name", C.c_char_p, [_int]),
     ("cuopx_gemm", _int, [_int, _int, _int, _i64, _i64, _i64, _dbl, _vp, _i64, _vp, _i64, _dbl, _vp, _i64, _vp]),
     ("cuopx_gemm_ex", _int,

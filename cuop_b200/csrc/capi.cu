@@ -1,6 +1,10 @@
 // C-ABI entry points (include/cuopx.h): argument validation, variant
 // selection, launch bookkeeping and the device error word.
+#include <nvtx3/nvToolsExt.h>
+
 #include <atomic>
+#include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -25,6 +29,54 @@ size_t span_bytes(int64_t rows, int64_t cols, int64_t ld, size_t es) {
   return static_cast<size_t>((rows - 1) * ld + cols) * es;
 }
 }  // namespace
+
+// Tracing, off unless asked for: CUOPX_NVTX=1 wraps every compute entry
+// point in an NVTX range (visible to Nsight tools), CUOPX_LOG=1 prints one
+// line per call (entry point, sizes, kernel launched, status) to stderr.
+// Read once; when both are off a call pays one branch.
+struct TraceFlags {
+  bool nvtx = false, log = false;
+  TraceFlags() {
+    const char* n = std::getenv("CUOPX_NVTX");
+    const char* l = std::getenv("CUOPX_LOG");
+    nvtx = n && *n && *n != '0';
+    log = l && *l && *l != '0';
+  }
+};
+const TraceFlags& trace_flags() {
+  static const TraceFlags f;
+  return f;
+}
+
+class ApiScope {
+ public:
+  ApiScope(const char* name, int64_t a, int64_t b, int64_t c, int64_t d = 1) : name_(name) {
+    const TraceFlags& f = trace_flags();
+    on_ = f.nvtx || f.log;
+    if (!on_) return;
+    nvtx_ = f.nvtx;
+    log_ = f.log;
+    dims_[0] = a, dims_[1] = b, dims_[2] = c, dims_[3] = d;
+    if (nvtx_) nvtxRangePushA(name);
+  }
+  int done(int rc) {
+    if (on_) {
+      if (nvtx_) nvtxRangePop();
+      if (log_)
+        std::fprintf(stderr, "cuopx: %s %lld x %lld x %lld (x %lld) -> %s, status %d\n", name_,
+                     static_cast<long long>(dims_[0]), static_cast<long long>(dims_[1]),
+                     static_cast<long long>(dims_[2]), static_cast<long long>(dims_[3]), t_last_kernel, rc);
+      on_ = false;
+    }
+    return rc;
+  }
+  ~ApiScope() { done(0); }
+
+ private:
+  const char* name_;
+  bool on_ = false, nvtx_ = false, log_ = false;
+  int64_t dims_[4] = {0, 0, 0, 0};
+};
 
 int device_sm_count() {
   int dev = 0;
@@ -160,15 +212,17 @@ int cuopx_clear_device_error(void) {
 
 int cuopx_gemm(int dtype, int transA, int transB, int64_t M, int64_t N, int64_t K, double alpha, const void* A,
                int64_t lda, const void* B, int64_t ldb, double beta, void* C, int64_t ldc, void* stream) {
+  ApiScope scope("cuopx_gemm", M, N, K);
   GemmProblem p{dtype, transA != 0, transB != 0, M, N, K, alpha, beta, A, lda, 0, B, ldb, 0, C, ldc, 0, 1};
   const int v = validate_gemm(p);
-  if (v >= 0) return v;
-  return gemm_route(p, static_cast<cudaStream_t>(stream));
+  if (v >= 0) return scope.done(v);
+  return scope.done(gemm_route(p, static_cast<cudaStream_t>(stream)));
 }
 
 int cuopx_gemm_ex(int dtype, int transA, int transB, int64_t M, int64_t N, int64_t K, double alpha, const void* A,
                   int64_t lda, const void* B, int64_t ldb, double beta, void* C, int64_t ldc, const void* bias,
                   int epilogue, void* stream) {
+  ApiScope scope("cuopx_gemm_ex", M, N, K);
   if (epilogue < 0 || epilogue > (CUOPX_EPI_BIAS | CUOPX_EPI_RELU)) return CUOPX_INVALID_ARGUMENT;
   if ((epilogue & CUOPX_EPI_BIAS) && bias == nullptr && M > 0 && N > 0) return CUOPX_INVALID_ARGUMENT;
   GemmProblem p{dtype, transA != 0, transB != 0, M, N, K, alpha, beta, A, lda, 0, B, ldb, 0, C, ldc, 0, 1};
@@ -180,18 +234,19 @@ int cuopx_gemm_ex(int dtype, int transA, int transB, int64_t M, int64_t N, int64
     const size_t es = dtype_size(dtype);
     if (overlaps(C, span_bytes(M, N, ldc, es), bias, static_cast<size_t>(N) * es)) return CUOPX_INVALID_ARGUMENT;
   }
-  return gemm_route(p, static_cast<cudaStream_t>(stream));
+  return scope.done(gemm_route(p, static_cast<cudaStream_t>(stream)));
 }
 
 int cuopx_gemm_strided_batched(int dtype, int transA, int transB, int64_t M, int64_t N, int64_t K, double alpha,
                                const void* A, int64_t lda, int64_t strideA, const void* B, int64_t ldb,
                                int64_t strideB, double beta, void* C, int64_t ldc, int64_t strideC, int64_t batch,
                                void* stream) {
+  ApiScope scope("cuopx_gemm_strided_batched", M, N, K, batch);
   GemmProblem p{dtype, transA != 0, transB != 0, M, N, K, alpha, beta, A, lda, strideA, B, ldb, strideB,
                 C, ldc, strideC, batch};
   const int v = validate_gemm(p);
-  if (v >= 0) return v;
-  return gemm_route(p, static_cast<cudaStream_t>(stream));
+  if (v >= 0) return scope.done(v);
+  return scope.done(gemm_route(p, static_cast<cudaStream_t>(stream)));
 }
 
 size_t cuopx_gemv_workspace_size(int dtype, int trans, int64_t M, int64_t N) {
@@ -201,6 +256,7 @@ size_t cuopx_gemv_workspace_size(int dtype, int trans, int64_t M, int64_t N) {
 
 int cuopx_gemv(int dtype, int trans, int64_t M, int64_t N, double alpha, const void* A, int64_t lda, const void* x,
                double beta, void* y, void* workspace, size_t workspace_bytes, void* stream) {
+  ApiScope scope("cuopx_gemv", M, N, trans);
   if (dtype_size(dtype) == 0) return CUOPX_UNSUPPORTED_TYPE;
   if (M < 0 || N < 0) return CUOPX_INVALID_ARGUMENT;
   if (M == 0) return CUOPX_SUCCESS;
@@ -212,8 +268,8 @@ int cuopx_gemv(int dtype, int trans, int64_t M, int64_t N, double alpha, const v
     const size_t a_span = trans ? span_bytes(N, M, lda, es) : span_bytes(M, N, lda, es);
     if (overlaps(y, M * es, A, a_span) || overlaps(y, M * es, x, N * es)) return CUOPX_INVALID_ARGUMENT;
   }
-  return gemv_dispatch(dtype, trans, M, N, alpha, A, lda, x, beta, y, workspace, workspace_bytes,
-                       static_cast<cudaStream_t>(stream));
+  return scope.done(gemv_dispatch(dtype, trans, M, N, alpha, A, lda, x, beta, y, workspace, workspace_bytes,
+                                  static_cast<cudaStream_t>(stream)));
 }
 
 int cuopx_gather_column_blocks(int dtype, int64_t G, int64_t M, int64_t Nb, const void* blocks, void* out,

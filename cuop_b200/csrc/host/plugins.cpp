@@ -102,13 +102,28 @@ StatusCode BlasPluginBase::ready_to_execute() {
   return StatusCode::SUCCESS;
 }
 
+namespace {
+// kernel_type as a hint into GEMM variant selection: the reference's SIMT
+// variants map to the FFMA kernels (same ascending-k fma chain), everything
+// else to the built-in / tuned choice.
+const char* variant_hint(const std::string& kernel_type) {
+  if (kernel_type == "basic") return "generic";
+  if (kernel_type == "tiled" || kernel_type == "warp_optimized" || kernel_type == "blocked" ||
+      kernel_type == "simt")
+    return "ffma";
+  return nullptr;
+}
+}  // namespace
+
 StatusCode BlasPluginBase::timed(const std::function<int()>& launch, double flops, double bytes,
                                  std::vector<int> dims) {
   cudaEvent_t e0 = nullptr, e1 = nullptr;
   const bool ev = cudaEventCreate(&e0) == cudaSuccess && cudaEventCreate(&e1) == cudaSuccess;
   const auto t0 = std::chrono::steady_clock::now();
   if (ev) cudaEventRecord(e0, stream_);
+  cuopx_set_gemm_variant_thread(variant_hint(config_.kernel_type));
   const int rc = launch();
+  cuopx_set_gemm_variant_thread(nullptr);
   if (ev) cudaEventRecord(e1, stream_);
   const cudaError_t sync = cudaStreamSynchronize(stream_);
   const double secs = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
@@ -124,6 +139,12 @@ StatusCode BlasPluginBase::timed(const std::function<int()>& launch, double flop
     last_error_ = cudaGetErrorString(sync);
     return StatusCode::CUDA_ERROR;
   }
+  int dev_err = 0;
+  if (cuopx_get_device_error(&dev_err) == CUOPX_SUCCESS && dev_err != 0) {
+    // A bounded device-side wait gave up: the kernel returned without its result.
+    last_error_ = "device-side wait timed out (device error " + std::to_string(dev_err) + ")";
+    return StatusCode::EXECUTION_TIMEOUT;
+  }
   ++executions_;
   last_profile_.kernel_time_ms = ms;
   last_profile_.execution_time = secs;
@@ -132,7 +153,8 @@ StatusCode BlasPluginBase::timed(const std::function<int()>& launch, double flop
   last_profile_.throughput = last_profile_.gflops;
   last_profile_.bandwidth_gb_s = ms > 0 ? bytes / (ms * 1e-3) / 1e9 : 0.0;
   last_profile_.kernel_name = cuopx_last_kernel();
-  last_profile_.used_tensor_core = last_profile_.kernel_name.rfind("gemm_tc_", 0) == 0;
+  last_profile_.used_tensor_core = last_profile_.kernel_name.rfind("gemm_tc", 0) == 0 ||
+                                  last_profile_.kernel_name.rfind("gemm_tf32x3", 0) == 0;
   last_profile_.used_tma = last_profile_.used_tensor_core;
   last_profile_.matrix_size = std::move(dims);
   last_profile_.kernel_type = config_.kernel_type;

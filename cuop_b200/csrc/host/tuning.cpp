@@ -53,6 +53,7 @@ using Table = std::vector<Rule>;
 std::mutex g_table_mu;
 std::shared_ptr<const Table> g_table;  // replaced whole; readers take a copy of the pointer
 std::atomic<int> g_forced{kVariantAuto};
+thread_local int t_hint = kVariantAuto;  // per-thread override (plugins' kernel_type)
 
 bool parse_range(const std::string& tok, Range& r) {
   if (tok == "*") return true;
@@ -120,6 +121,7 @@ int parse_table(const char* text, Table& t) {
 const char* gemm_variant_name(int v) { return (v >= 0 && v < kVariantCount) ? kVariantNames[v] : nullptr; }
 
 int select_gemm_variant(const GemmProblem& p) {
+  if (t_hint != kVariantAuto) return t_hint;
   const int forced = g_forced.load(std::memory_order_relaxed);
   if (forced != kVariantAuto) return forced;
   std::shared_ptr<const Table> t;
@@ -180,5 +182,12 @@ int cuopx_set_gemm_variant(const char* name) {
 }
 
 const char* cuopx_gemm_variant_name(int index) { return gemm_variant_name(index); }
+
+int cuopx_set_gemm_variant_thread(const char* name) {
+  const int v = name ? variant_by_name(name) : kVariantAuto;
+  if (v < 0) return CUOPX_INVALID_ARGUMENT;
+  t_hint = v;
+  return CUOPX_SUCCESS;
+}
 
 }  // extern "C"

@@ -91,6 +91,10 @@ int cuopx_tuning_load_file(const char* path);
 int cuopx_tuning_clear(void);
 int cuopx_tuning_rows(void);
 int cuopx_set_gemm_variant(const char* name);
+/* The same override for the calling host thread only (takes precedence over
+ * the process-wide one); the BLAS plugins set it from JITConfig.kernel_type
+ * around their launches.  NULL or "auto" clears it. */
+int cuopx_set_gemm_variant_thread(const char* name);
 const char* cuopx_gemm_variant_name(int index);
 
 /*

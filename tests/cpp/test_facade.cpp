@@ -485,6 +485,76 @@ TEST_GPU(GemmPluginExecute) {
   EXPECT_TRUE(!g->GetPerformanceProfile().kernel_name.empty());
 }
 
+// JITConfig.kernel_type is a hint into variant selection: the reference's
+// SIMT kernel families run the FFMA kernels (bit-identical to the oracle),
+// "tensor_core" keeps the tensor-core choice.
+TEST_GPU(GemmPluginKernelTypeSelectsVariant) {
+  const int M = 384, N = 320, K = 512;  // 3xTF32 by default at this size
+  std::vector<float> a(size_t(M) * K), w(size_t(K) * N), ref(size_t(M) * N, 0.f);
+  oracle_fill_uniform_f32(a.data(), a.size(), 51, -1.f, 1.f);
+  oracle_fill_uniform_f32(w.data(), w.size(), 52, -1.f, 1.f);
+  oracle_gemm_f32(0, 0, M, N, K, 1.f, a.data(), K, w.data(), N, 0.f, ref.data(), N, 4);
+  Tensor<float> W({size_t(K), size_t(N)});
+  W.copy_from_host(w.data());
+  const char* types[] = {"tensor_core", "tiled", "basic"};
+  const char* kernels[] = {"gemm_tf32x3_", "gemm_f32_", "gemm_simt_generic"};
+  for (int i = 0; i < 3; ++i) {
+    auto plugin = CreateBlasJITPlugin("gemm");
+    auto* g = dynamic_cast<GemmJITPlugin*>(plugin.get());
+    EXPECT_TRUE(g && g->Initialize() == StatusCode::SUCCESS);
+    if (!g) return;
+    JITConfig cfg;
+    cfg.kernel_type = types[i];
+    EXPECT_TRUE(g->Compile(cfg) == StatusCode::SUCCESS);
+    g->SetGemmParams(false, false, 1.0f, 0.0f);
+    g->SetWeight(W);
+    std::vector<Tensor<float>> in, out;
+    in.emplace_back(std::vector<size_t>{size_t(M), size_t(K)});
+    in[0].copy_from_host(a.data());
+    out.emplace_back();
+    EXPECT_TRUE(g->Execute(in, out) == StatusCode::SUCCESS);
+    const std::string k = g->GetPerformanceProfile().kernel_name;
+    EXPECT_TRUE(k.rfind(kernels[i], 0) == 0);
+    EXPECT_EQ(g->GetPerformanceProfile().used_tensor_core, i == 0);
+    auto h = to_host(out[0]);
+    if (i > 0) EXPECT_TRUE(std::memcmp(h.data(), ref.data(), h.size() * sizeof(float)) == 0);
+    else EXPECT_TRUE(rel_frobenius(h, ref) <= 1e-5 * std::sqrt(double(K)));
+  }
+  // The hint covered only the plugin's own launches: a direct call is back on 3xTF32.
+  Tensor<float> A({size_t(M), size_t(K)}), C({size_t(M), size_t(N)});
+  A.copy_from_host(a.data());
+  EXPECT_EQ(cuopx_gemm(CUOPX_F32, 0, 0, M, N, K, 1.0, A.data(), K, W.data(), N, 0.0, C.data(), N, nullptr),
+            CUOPX_SUCCESS);
+  EXPECT_TRUE(std::string(cuopx_last_kernel()).rfind("gemm_tf32x3_", 0) == 0);
+}
+
+// A bounded device-side wait that runs out (a cross-GPU barrier whose peer
+// never arrives, ~5 s) is reported by the next plugin call as
+// EXECUTION_TIMEOUT; the context stays usable and clearing the word recovers.
+TEST_GPU(DeviceTimeoutReportedAsExecutionTimeout) {
+  Tensor<unsigned int> s0({size_t(CUOPX_PEER_SIGNAL_BYTES / 4)}), s1({size_t(CUOPX_PEER_SIGNAL_BYTES / 4)});
+  s0.zero();
+  s1.zero();
+  void* sig[2] = {s0.data(), s1.data()};
+  cuopx_clear_device_error();
+  EXPECT_EQ(cuopx_peer_barrier(sig, 2, 0, nullptr), CUOPX_SUCCESS);
+  auto plugin = CreateBlasJITPlugin("gemm");
+  auto* g = dynamic_cast<GemmJITPlugin*>(plugin.get());
+  EXPECT_TRUE(g && g->Initialize() == StatusCode::SUCCESS && g->Compile(JITConfig{}) == StatusCode::SUCCESS);
+  if (!g) return;
+  Tensor<float> W({4, 4});
+  W.zero();
+  g->SetWeight(W);
+  std::vector<Tensor<float>> in, out;
+  in.emplace_back(std::vector<size_t>{4, 4});
+  in[0].zero();
+  out.emplace_back();
+  EXPECT_TRUE(g->Execute(in, out) == StatusCode::EXECUTION_TIMEOUT);
+  EXPECT_TRUE(g->GetLastError().find("timed out") != std::string::npos);
+  EXPECT_EQ(cuopx_clear_device_error(), CUOPX_SUCCESS);
+  EXPECT_TRUE(g->Execute(in, out) == StatusCode::SUCCESS);
+}
+
 TEST_GPU(BatchedAndGemvAndVectorPlugins) {
   // batched: 2 x (2x3 * 3x4) with the known-answer data, registered under "gemm_batched"
   auto pb = CreateBlasJITPlugin("gemm_batched");

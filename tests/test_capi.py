@@ -132,3 +132,19 @@ def test_tuning_table_parsing_without_gpu():
         L.cuopx_tuning_clear()
     assert L.cuopx_tuning_rows() == 0
 
+
+def test_call_log_is_opt_in():
+    """CUOPX_LOG=1 prints one line per C-ABI call; unset, nothing is printed."""
+    import subprocess
+    import sys
+
+    code = ("import sys; sys.path.insert(0, %r); from cuop_b200 import _native as N; "
+            "print(N.lib().cuopx_gemm(0, 0, 0, -1, 4, 4, 1.0, 16, 4, 16, 4, 0.0, 16, 4, None))" % str(ROOT))
+    on = subprocess.run([sys.executable, "-c", code], env={**__import__("os").environ, "CUOPX_LOG": "1"},
+                        capture_output=True, text=True, timeout=120)
+    assert on.returncode == 0 and on.stdout.strip() == str(N.INVALID_ARGUMENT)
+    assert "cuopx: cuopx_gemm -1 x 4 x 4" in on.stderr and "status 4001" in on.stderr
+    env = {k: v for k, v in __import__("os").environ.items() if k != "CUOPX_LOG"}
+    off = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=120)
+    assert off.returncode == 0 and "cuopx:" not in off.stderr
+
