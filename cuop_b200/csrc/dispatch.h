@@ -56,6 +56,9 @@ int gemm_simt_f32(const GemmProblem& p, cudaStream_t stream);
 // bn = 128 / 256: the 1-SM kernel with that tile width.
 bool gemm_tc_supported(const GemmProblem& p);
 int gemm_tc(const GemmProblem& p, cudaStream_t stream, int bn = 0);
+// The 1-SM kernel (bn 128 or 256) with every output chunk also stored to
+// peers[0..npeers) (peer mappings of identically laid out outputs).
+int gemm_tc_peers(const GemmProblem& p, void* const* peers, int npeers, cudaStream_t stream, int bn);
 
 // Two-SM (cta_group::2) tcgen05 back-end (gemm_tc2.cu) for large fp16/bf16.
 bool gemm_tc2_wanted(const GemmProblem& p);

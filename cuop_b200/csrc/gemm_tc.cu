@@ -62,6 +62,10 @@ struct TcParams {
   int64_t ldc, strideC;
   const void* bias;  // CUOPX_EPI_BIAS: N elements of the output type
   int epi;           // CUOPX_EPI_* flags
+  // Peer-store all-gather: each staged output chunk is also written to
+  // peer_C[i] (same row stride ldc, same column offset) for i < npeers.
+  int npeers;
+  void* peer_C[7];
 };
 
 template <int BN, int STAGES>
@@ -123,7 +127,7 @@ __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-template <typename T, int BN, int STAGES, bool A_MN, bool B_MN>
+template <typename T, int BN, int STAGES, bool A_MN, bool B_MN, bool PEERS = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const TcParams p) {
@@ -409,6 +413,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tma_store_3d(&tmC, sbase, n0 + ch * STAGE_CHUNK_COLS, m0 + 32 * q, b);
           bulk_commit_group();
         }
+        if (PEERS && p.npeers > 0) {
+          // Same 32 x 64 chunk to every peer's output: lanes 8r..8r+7 write
+          // the 128 contiguous bytes of one row (four full 128-byte lines per
+          // warp store).  Rows past M and 16-byte groups past N are skipped.
+          const int c16 = lane & 7;
+          const int64_t gcol = static_cast<int64_t>(n0) + ch * STAGE_CHUNK_COLS + 8 * c16;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int r = 4 * i + (lane >> 3);
+            const int64_t grow_r = static_cast<int64_t>(m0) + 32 * q + r;
+            const uint4 w = *reinterpret_cast<const uint4*>(sbase + r * 128 + ((c16 ^ (r & 7)) << 4));
+            if (grow_r < p.M && gcol < p.N) {
+              const int64_t off = grow_r * p.ldc + gcol;
+#pragma unroll
+              for (int d = 0; d < 7; ++d)  // constant indices keep peer_C in the param bank
+                if (d < p.npeers) *reinterpret_cast<uint4*>(static_cast<T*>(p.peer_C[d]) + off) = w;
+            }
+          }
+        }
         sbuf ^= 1;
       }
       if (++acc == ACC_BUFS) acc = 0, acc_phase ^= 1u;
@@ -425,6 +448,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     if (lane == 0) bulk_wait_group<0>();
     __syncwarp();
+    // Peer stores of this thread are ordered before anything the stream runs
+    // after the kernel (the peer barrier's release).
+    if (PEERS && p.npeers > 0) __threadfence_system();
   }
 
   tc_fence_before_sync();
@@ -476,8 +502,9 @@ bool make_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base, int64_
   return make_map_es(map, dt, 2, base, inner, rows, batch, ld, bstride, box_inner, box_rows);
 }
 
-template <typename T, int BN, int STAGES, bool A_MN, bool B_MN>
-int launch_tc(const GemmProblem& p, cudaStream_t stream, const char* name) {
+template <typename T, int BN, int STAGES, bool A_MN, bool B_MN, bool PEERS = false>
+int launch_tc(const GemmProblem& p, cudaStream_t stream, const char* name, void* const* peers = nullptr,
+              int npeers = 0) {
   using L = SmemLayout<BN, STAGES>;
   const CUtensorMapDataType dt =
       std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -512,8 +539,11 @@ int launch_tc(const GemmProblem& p, cudaStream_t stream, const char* name) {
   prm.strideC = p.strideC;
   prm.bias = p.bias;
   prm.epi = p.epi;
+  if (npeers < 0 || npeers > 7) return CUOPX_INVALID_ARGUMENT;
+  prm.npeers = npeers;
+  for (int i = 0; i < 7; ++i) prm.peer_C[i] = i < npeers ? peers[i] : nullptr;
 
-  auto kern = gemm_tc_kernel<T, BN, STAGES, A_MN, B_MN>;
+  auto kern = gemm_tc_kernel<T, BN, STAGES, A_MN, B_MN, PEERS>;
   static bool attr_set[64] = {};  // per instantiation and device
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return CUOPX_CUDA_ERROR;
@@ -573,6 +603,21 @@ int gemm_tc(const GemmProblem& p, cudaStream_t stream, int bn) {
   }
   return wide ? launch_tc_layout<__half, 256, 4>(p, stream, "gemm_tc_128x256")
               : launch_tc_layout<__half, 128, 6>(p, stream, "gemm_tc_128x128");
+}
+
+// Peer stores are compiled only into the row-major layout of the column-
+// sharded linear layer (A K-major, W [K][N] MN-major); other layouts take the
+// 2-SM kernel's peer path.
+int gemm_tc_peers(const GemmProblem& p, void* const* peers, int npeers, cudaStream_t stream, int bn) {
+  if (p.transA || p.transB) return gemm_tc2_peers(p, peers, npeers, stream);
+  const bool wide = bn == 256;
+  const char* name = wide ? "gemm_tc_128x256_peer" : "gemm_tc_128x128_peer";
+  if (p.dtype == CUOPX_BF16) {
+    return wide ? launch_tc<__nv_bfloat16, 256, 4, false, true, true>(p, stream, name, peers, npeers)
+                : launch_tc<__nv_bfloat16, 128, 6, false, true, true>(p, stream, name, peers, npeers);
+  }
+  return wide ? launch_tc<__half, 256, 4, false, true, true>(p, stream, name, peers, npeers)
+              : launch_tc<__half, 128, 6, false, true, true>(p, stream, name, peers, npeers);
 }
 
 }  // namespace cuopx

@@ -17,7 +17,7 @@ import cuop_b200 as cx
 import oracle as O
 from cuop_b200 import _native as N
 from cuop_b200 import peer
-from helpers import fp32_reference_gpu, lowp_bits, to_dev_lowp
+from helpers import forced_variant, fp32_reference_gpu, lowp_bits, to_dev_lowp
 
 pytestmark = pytest.mark.gpu
 LOWP_TOL = 1e-2
@@ -43,9 +43,13 @@ CASES = [  # (world, M, nb, K, tA, tB)
 ]
 
 
+PATHS = [("tc2", "gemm_tc2_256x256"), ("tc_128x128", "gemm_tc_128x128"), ("tc_128x256", "gemm_tc_128x256")]
+
+
+@pytest.mark.parametrize("variant,kernel", PATHS)
 @pytest.mark.parametrize("dt", [O.F16, O.BF16])
 @pytest.mark.parametrize("world,M,nb,K,tA,tB", CASES)
-def test_allgather_every_rank_gets_every_block(dev, dt, world, M, nb, K, tA, tB):
+def test_allgather_every_rank_gets_every_block(dev, dt, world, M, nb, K, tA, tB, variant, kernel):
     A = O.to_lowp(O.normal((K, M) if tA else (M, K), seed=M + K) / np.sqrt(K), dt)
     W = O.to_lowp(O.normal((world * nb, K) if tB else (K, world * nb), seed=nb + 3), dt)
     Ad = to_dev_lowp(A, dt, dev)
@@ -53,8 +57,12 @@ def test_allgather_every_rank_gets_every_block(dev, dt, world, M, nb, K, tA, tB)
     outs = [torch.full((M, world * nb), float("nan"), dtype=TDT[dt], device=dev) for _ in range(world)]
     for r in range(world):
         Wb = (Wd[r * nb:(r + 1) * nb] if tB else Wd[:, r * nb:(r + 1) * nb]).contiguous()
-        assert _call(dt, M, nb, K, Ad, Wb, outs, r, tA, tB, alpha=1.25) == 0
-        assert cx.last_kernel() == ("gemm_tc2_256x256_peer" if world > 1 else "gemm_tc2_256x256")
+        with forced_variant(variant):
+            assert _call(dt, M, nb, K, Ad, Wb, outs, r, tA, tB, alpha=1.25) == 0
+        # The 1-SM peer path is compiled for the row-major layout only;
+        # transposed operands take the 2-SM kernel's peer path.
+        expect = kernel if not (tA or tB) else "gemm_tc2_256x256"
+        assert cx.last_kernel() == expect + ("_peer" if world > 1 else "")
     torch.cuda.synchronize()
     for o in outs[1:]:  # every rank's copy is the same bits
         assert torch.equal(o.view(torch.int16), outs[0].view(torch.int16))
@@ -65,6 +73,17 @@ def test_allgather_every_rank_gets_every_block(dev, dt, world, M, nb, K, tA, tB)
     ref = O.gemm_lowp(dt, A[:, rows] if tA else A[rows], W, transA=tA, transB=tB, alpha=1.25)
     got = O.from_lowp(lowp_bits(outs[world - 1][torch.as_tensor(rows, device=dev)]), dt)
     assert O.max_relative(got, O.from_lowp(ref, dt)) <= LOWP_TOL
+
+
+def test_allgather_tile_choice_follows_the_exchange(dev):
+    """Pair tiles while the GEMM outlasts the exchange; 1-SM 128 x 128 tiles
+    when the exchange is the bound (more ranks, narrower blocks)."""
+    for world, nb, K, kernel in ((2, 4096, 4096, "gemm_tc2_256x256_peer"), (8, 256, 2048, "gemm_tc_128x128_peer")):
+        A = torch.randn(2048, K, device=dev).half()
+        Wb = torch.randn(K, nb, device=dev).half()
+        outs = [torch.empty(2048, world * nb, device=dev, dtype=torch.half) for _ in range(world)]
+        assert _call(O.F16, 2048, nb, K, A, Wb, outs, 0) == 0
+        assert cx.last_kernel() == kernel, (world, cx.last_kernel())
 
 
 def test_allgather_touches_only_its_block(dev):
