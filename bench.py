@@ -526,7 +526,7 @@ def _sharded_gemm(cx, sharding, X, Wl, rank, world, steps, n_total):
     try:
         ms_peer = time_graph(lambda i: pg.forward(X), steps, 3, world, align=lambda: peer.peer_barrier(pg.signals))
         pg.forward(X)
-        kname = "gemm_tc2_256x256_peer"
+        kname = pg.last_kernel
     finally:
         torch.cuda.synchronize()
         pg.close()

@@ -148,6 +148,7 @@ class PeerShardedGemm:
             raise N.CuopError(N.UNSUPPORTED_TYPE, "PeerShardedGemm takes a 2-D fp16/bf16 weight block")
         ops._require_cuda(w_local)
         self.w_local, self.rank, self.world, self.max_rows, self.group = w_local, rank, world, max_rows, group
+        self.last_kernel = ""
         self.nb = w_local.size(1)
         self.n_total = world * self.nb
         es = w_local.element_size()
@@ -170,6 +171,7 @@ class PeerShardedGemm:
                                           self.w_local.data_ptr(), ops._row_ld(self.w_local),
                                           self.out.pointer_array(), self.world, self.rank, self.n_total, s)
         N.check(rc, "cuopx_gemm_allgather")
+        self.last_kernel = ops.last_kernel()  # the GEMM variant (before the barrier's launch)
         peer_barrier(self.signals, s)  # every rank's block has landed here
         return self.out.local_tensor((M, self.n_total), X.dtype, X.device)
 
