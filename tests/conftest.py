@@ -23,6 +23,20 @@ def pytest_collection_modifyitems(config, items):
             item.add_marker(skip)
 
 
+def pytest_sessionstart(session):
+    """Build libcuopx.so (and the oracle) when missing or stale — a no-op on
+    an up-to-date tree — so a fresh checkout runs the suite directly."""
+    import shutil
+    import subprocess
+
+    from cuop_b200 import build
+
+    if shutil.which("nvcc") or os.path.exists("/usr/local/cuda/bin/nvcc"):
+        build.build()
+    if not (ROOT / "oracle" / "liboracle.so").exists():
+        subprocess.run(["make", "-s", "-C", str(ROOT / "oracle"), "all"], check=True)
+
+
 @pytest.fixture(scope="session", autouse=True)
 def _builtin_gemm_selection():
     """Kernel-parity tests name the kernel each shape must reach under the
