@@ -34,7 +34,7 @@ constexpr int GS_THREADS = 256;
 constexpr int GS_WARPS = GS_THREADS / 32;
 constexpr int GS_ROWS_MAX = 64;  // rows per CTA in gemv_n_xreg
 constexpr int GS_T_UNROLL = 16;  // rows in flight per thread in gemv_t_lsu
-constexpr int GS_T_RED_BATCH = 8;  // partial loads issued together in the final reduction
+constexpr int GS_T_RED_BATCH = 16;  // partial loads issued together in the final reduction
 
 __device__ __forceinline__ uint4 ld_nc16(const void* p) {
   uint4 v;
