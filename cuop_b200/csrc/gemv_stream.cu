@@ -34,7 +34,9 @@ constexpr int GS_THREADS = 256;
 constexpr int GS_WARPS = GS_THREADS / 32;
 constexpr int GS_ROWS_MAX = 64;  // rows per CTA in gemv_n_xreg
 constexpr int GS_T_UNROLL = 16;  // rows in flight per thread in gemv_t_lsu
-constexpr int GS_T_RED_BATCH = 16;  // partial loads issued together in the final reduction
+// Final split reduction: partial vectors loaded together per round, sized so
+// they take 64 registers (16 for fp32 / fp64, 8 for 16-bit types).
+constexpr int GS_T_RED_REGS = 64;
 
 __device__ __forceinline__ uint4 ld_nc16(const void* p) {
   uint4 v;
@@ -248,6 +250,7 @@ __global__ void __launch_bounds__(GS_THREADS, 2)
     // aligned bytes (M % V == 0, 256-byte aligned workspace): vector loads.
     constexpr int QN = V * static_cast<int>(sizeof(Acc)) / 16;
     static_assert(QN * 16 == V * static_cast<int>(sizeof(Acc)), "partial vector size");
+    constexpr int GS_T_RED_BATCH = GS_T_RED_REGS / (V * static_cast<int>(sizeof(Acc)) / 4);
     for (unsigned int k0 = 0; k0 < splits; k0 += GS_T_RED_BATCH) {
       Acc pv[GS_T_RED_BATCH][V];
 #pragma unroll
