@@ -172,20 +172,13 @@ int cuopx_gemm_allgather(int dtype, int transA, int transB, int64_t M, int64_t N
     if (!aligned16(C_ranks[r])) return CUOPX_INVALID_ARGUMENT;
     peers[np++] = static_cast<unsigned char*>(C_ranks[r]) + static_cast<size_t>(rank) * N_local * es;
   }
-  // Tile choice.  While the GEMM outlasts the exchange, 2-SM pair tiles (the
-  // fastest GEMM) hide it.  When the exchange is the bound (NVLink time above
-  // the GEMM time: many ranks, narrow column blocks), 1-SM 128 x 128 tiles
-  // finish their first outputs in half the time, so bytes start crossing
-  // NVLink sooner; their slower GEMM stays hidden under the exchange.
-  // Estimates use measured B200 rates: ~700 GB/s of SM-issued peer stores
-  // per direction, ~1.4 PFLOP/s of sustained fp16/bf16 GEMM.  A variant
-  // override (cuopx_set_gemm_variant[_thread]) picks the path explicitly.
+  // Tile choice: 2-SM pair tiles at every rank count.  Measured on B200 at
+  // 8 ranks (same box, same inputs), pair tiles beat the 1-SM peer paths
+  // even where the exchange outlasts the GEMM (C3 8192^3: 271 us vs 285 us
+  // for 128 x 256 and 305 us for 128 x 128 tiles; C5: 401 vs 428 / 450 us).
+  // A variant override (cuopx_set_gemm_variant[_thread]) selects a 1-SM path.
   int v = select_gemm_variant(p);
-  if (v != kVariantTc2 && v != kVariantTc128x256 && v != kVariantTc128x128) {
-    const double link_s = static_cast<double>(np) * M * N_local * es / 7.0e11;
-    const double gemm_s = 2.0 * M * N_local * K / 1.4e15;
-    v = (np > 0 && link_s > gemm_s) ? kVariantTc128x128 : kVariantTc2;
-  }
+  if (v != kVariantTc128x256 && v != kVariantTc128x128) v = kVariantTc2;
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (v == kVariantTc128x256) return gemm_tc_peers(p, peers, np, s, 256);
   if (v == kVariantTc128x128) return gemm_tc_peers(p, peers, np, s, 128);

@@ -75,15 +75,14 @@ def test_allgather_every_rank_gets_every_block(dev, dt, world, M, nb, K, tA, tB,
     assert O.max_relative(got, O.from_lowp(ref, dt)) <= LOWP_TOL
 
 
-def test_allgather_tile_choice_follows_the_exchange(dev):
-    """Pair tiles while the GEMM outlasts the exchange; 1-SM 128 x 128 tiles
-    when the exchange is the bound (more ranks, narrower blocks)."""
-    for world, nb, K, kernel in ((2, 4096, 4096, "gemm_tc2_256x256_peer"), (8, 256, 2048, "gemm_tc_128x128_peer")):
+def test_allgather_uses_pair_tiles_by_default(dev):
+    """Pair tiles at any rank count unless a 1-SM path is forced."""
+    for world, nb, K in ((2, 4096, 4096), (8, 256, 2048)):
         A = torch.randn(2048, K, device=dev).half()
         Wb = torch.randn(K, nb, device=dev).half()
         outs = [torch.empty(2048, world * nb, device=dev, dtype=torch.half) for _ in range(world)]
         assert _call(O.F16, 2048, nb, K, A, Wb, outs, 0) == 0
-        assert cx.last_kernel() == kernel, (world, cx.last_kernel())
+        assert cx.last_kernel() == "gemm_tc2_256x256_peer", (world, cx.last_kernel())
 
 
 def test_allgather_touches_only_its_block(dev):
