@@ -42,7 +42,7 @@ FP32_SIMT_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
 
 # DRAM bytes per launch from the ncu capture summarised in
 # profiles/gemv_f32_8192_ncu.md (dram__bytes_read.sum + dram__bytes_write.sum).
-NCU_TRAFFIC_BYTES = {"gemv_t_lsu": 271942400, "gemv_n_xreg": 271830016}
+NCU_TRAFFIC_BYTES = {"gemv_t_lsu": 271750656, "gemv_n_xreg": 271830016}
 
 
 # --------------------------------------------------------------------------- util
@@ -309,10 +309,12 @@ def run_gemv(args, rank, world, local_rank):
 def gemv_e2e_plugin(args, rank, world, local_rank, An, At):
     """Same metric through the public API in the plugin's usage model
     (GemvJITPlugin: the matrix is the plugin's weight, set once and resident;
-    each Execute takes x and returns y): every step copies a fresh x from
-    pinned host memory, runs both GEMVs on the step's resident matrices,
-    copies both results back to pinned host memory and waits for them on the
-    host."""
+    each Execute takes x and returns y): every step brings a fresh x from
+    pinned host memory to the device, runs both GEMVs on the step's resident
+    matrices, puts both results in pinned host memory and waits for them on
+    the host.  x is staged by the library's copy kernel reading the pinned
+    buffer (cuopx_copy) and the GEMVs write y straight into pinned host
+    memory, so the step is three kernels with no copy-engine transfer."""
     import torch
     import cuop_b200 as cx
 
@@ -320,22 +322,17 @@ def gemv_e2e_plugin(args, rank, world, local_rank, An, At):
     sets = len(An)
     g = torch.Generator().manual_seed(77 + rank)
     hx = [(torch.rand(GEMV_N, generator=g) * 2 - 1).pin_memory() for _ in range(sets)]
-    hyn = torch.empty(GEMV_N, pin_memory=True)
-    hyt = torch.empty(GEMV_N, pin_memory=True)
+    hy = torch.empty(2, GEMV_N, pin_memory=True)
     dx = torch.empty(GEMV_N, device=dev)
-    yn = torch.empty(GEMV_N, device=dev)
-    yt = torch.empty(GEMV_N, device=dev)
     stream = torch.cuda.current_stream()
 
     def body(k):
-        dx.copy_(hx[k], non_blocking=True)
-        cx.gemv(An[k], dx, yn)
-        cx.gemv(At[k], dx, yt, trans=True)
-        hyn.copy_(yn, non_blocking=True)
-        hyt.copy_(yt, non_blocking=True)
+        cx.copy(hx[k], dx)
+        cx.gemv(An[k], dx, hy[0])
+        cx.gemv(At[k], dx, hy[1], trans=True)
 
-    # One CUDA graph per rotation slot holds the step's copies and launches
-    # (host launch cost of one replay instead of five API calls).
+    # One CUDA graph per rotation slot holds the step's three launches (host
+    # launch cost of one replay instead of three API calls).
     graphs = []
     for k in range(sets):
         body(k)
@@ -344,6 +341,17 @@ def gemv_e2e_plugin(args, rank, world, local_rank, An, At):
         with torch.cuda.graph(gk):
             body(k)
         graphs.append(gk)
+
+    # The host copy of the results is the device's answer.
+    yn = torch.empty(GEMV_N, device=dev)
+    yt = torch.empty(GEMV_N, device=dev)
+    graphs[0].replay()
+    stream.synchronize()
+    cx.gemv(An[0], dx, yn)
+    cx.gemv(At[0], dx, yt, trans=True)
+    torch.cuda.synchronize()
+    if not (torch.equal(hy[0], yn.cpu()) and torch.equal(hy[1], yt.cpu())):
+        raise RuntimeError("GEMV results in pinned host memory differ from the device results")
 
     def step(i):
         graphs[i % sets].replay()
@@ -355,8 +363,9 @@ def gemv_e2e_plugin(args, rank, world, local_rank, An, At):
     return {"value": round(world * 2 * GEMV_BYTES / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
             "h2d_bytes_per_step": GEMV_N * 4, "d2h_bytes_per_step": 2 * GEMV_N * 4,
             "ms_per_step": round(ms, 4), "steps": steps,
-            "path": "cuop_b200.gemv (C ABI) with the matrices resident as plugin weights; per step H2D of x, "
-                    "both GEMVs and D2H of both y replayed as one CUDA graph, then host synchronisation"}
+            "path": "cuop_b200.copy + cuop_b200.gemv (C ABI) with the matrices resident as plugin weights; per "
+                    "step x read from pinned host memory by the copy kernel, both GEMVs writing y into pinned host "
+                    "memory, replayed as one CUDA graph, then host synchronisation"}
 
 
 def gemv_e2e(args, rank, world, local_rank, An, At, x):

@@ -14,9 +14,11 @@
 //    would need more scratch (never more than cuopx_gemv_workspace_size)
 //    are rejected with
 //    CUOPX_RESOURCE_UNAVAILABLE.  Where the streaming kernels apply (rows
-//    16-byte aligned and a multiple of 16 bytes long), fp32 and fp64 need
-//    under 1.3 MB at any size; fp16/bf16 transposed GEMV of large matrices
-//    needs ~2.4 MB and is rejected.
+//    16-byte aligned and a multiple of 16 bytes long), the transposed
+//    kernel's partials are at most (2 x resident CTAs) strips of 64 16-byte
+//    groups, under 1.3 MB for every type at any size; the generic split
+//    kernels that take the other shapes can need more (e.g. bf16
+//    transposed 8191 x 8192: ~4.8 MB) and such calls are rejected.
 //  * The first call on a device looks up the array's device address
 //    (cudaGetSymbolAddress) with that device current; make that first call
 //    before any stream capture.

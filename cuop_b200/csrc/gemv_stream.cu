@@ -14,10 +14,10 @@
 //   at a time (fma chains per lane, then a butterfly shuffle); the 8 warp
 //   partials of each row are added in warp order from shared memory.
 // gemv_t_lsu (y = A^T x, A is N x M): the grid is (column strips) x (row
-//   splits); thread t owns the 16-byte column group t of its strip and walks
-//   the split's rows 16 at a time.  Split partials go to the workspace and
-//   the last CTA of a strip adds them in split order, issuing the partial
-//   loads in independent batches so the tail is not one long latency chain.
+//   splits); a strip is 64 16-byte column groups wide and each group is
+//   walked by 4 threads (row phases), 16 rows in flight each.  Split partials
+//   go to the workspace and the last CTA of a strip adds them, so narrow
+//   strips keep that final, serial step short.
 // Both are deterministic: summation order depends only on the shape.
 //
 // Math: y_i = alpha * sum_j op(A)_ij x_j + beta * y_i (the reference's gemv
@@ -34,6 +34,9 @@ constexpr int GS_THREADS = 256;
 constexpr int GS_WARPS = GS_THREADS / 32;
 constexpr int GS_ROWS_MAX = 64;  // rows per CTA in gemv_n_xreg
 constexpr int GS_T_UNROLL = 16;  // rows in flight per thread in gemv_t_lsu
+constexpr int GS_T_SV = 64;      // 16-byte column groups per gemv_t_lsu strip
+constexpr int GS_T_PHASES = GS_THREADS / GS_T_SV;  // row phases per strip
+constexpr int GS_T_WAVES = 1;    // gemv_t_lsu CTAs per resident slot
 // Final split reduction: partial vectors loaded together per round, sized so
 // they take 64 registers (16 for fp32 / fp64, 8 for 16-bit types).
 constexpr int GS_T_RED_REGS = 64;
@@ -151,6 +154,11 @@ __global__ void __launch_bounds__(GS_THREADS, 2)
 }
 
 // ---------------------------------------------------------------------------
+// Thread t of a gemv_t_lsu CTA owns column group t % GS_T_SV of its strip and
+// row phase t / GS_T_SV: it walks rows j0 + phase, j0 + phase + GS_T_PHASES,
+// ... of the split.  The phases are added in order through shared memory, so
+// a strip is only GS_T_SV 16-byte groups wide and the last CTA of a strip has
+// splits x GS_T_SV x 16 bytes of partials to add, not a whole-CTA-wide slab.
 template <typename T>
 __global__ void __launch_bounds__(GS_THREADS, 2)
     gemv_t_lsu(int64_t M, int64_t N, typename AccOf<T>::type alpha, const T* __restrict__ A, int64_t lda,
@@ -159,10 +167,13 @@ __global__ void __launch_bounds__(GS_THREADS, 2)
   using Acc = typename AccOf<T>::type;
   constexpr int V = 16 / sizeof(T);
   constexpr int U = GS_T_UNROLL;
-  constexpr int64_t STRIP = static_cast<int64_t>(GS_THREADS) * V;  // columns per strip
+  constexpr int P = GS_T_PHASES;
+  constexpr int64_t STRIP = static_cast<int64_t>(GS_T_SV) * V;  // columns per strip
+  __shared__ Acc s_phase[P - 1][GS_T_SV * V];
   __shared__ unsigned int s_last;
   const int tid = threadIdx.x;
-  const int64_t col = static_cast<int64_t>(blockIdx.x) * STRIP + static_cast<int64_t>(tid) * V;
+  const int cv = tid % GS_T_SV, ph = tid / GS_T_SV;
+  const int64_t col = static_cast<int64_t>(blockIdx.x) * STRIP + static_cast<int64_t>(cv) * V;
   const bool has = col < M;  // M % V == 0: the group is all in or all out
   const int64_t j0 = static_cast<int64_t>(blockIdx.y) * rows_per_split;
   const int64_t j1 = min(N, j0 + rows_per_split);
@@ -176,14 +187,14 @@ __global__ void __launch_bounds__(GS_THREADS, 2)
 
   if (has) {
     const T* ap = A + col;
-    int64_t j = j0;
-    for (; j + U <= j1; j += U) {
+    int64_t j = j0 + ph;
+    for (; j + (U - 1) * P < j1; j += U * P) {
       uint4 v[U];
       Acc xv[U];
 #pragma unroll
-      for (int u = 0; u < U; ++u) v[u] = ld_nc16(ap + (j + u) * lda);
+      for (int u = 0; u < U; ++u) v[u] = ld_nc16(ap + (j + u * P) * lda);
 #pragma unroll
-      for (int u = 0; u < U; ++u) xv[u] = to_acc<T>(__ldg(x + j + u));
+      for (int u = 0; u < U; ++u) xv[u] = to_acc<T>(__ldg(x + j + u * P));
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         Acc f[V];
@@ -193,19 +204,19 @@ __global__ void __launch_bounds__(GS_THREADS, 2)
       }
     }
     if (j < j1) {
-      // Remainder (< U rows): one predicated batch, all loads in flight at
-      // once, added in the same ascending row order.
+      // Remainder (< U rows of this phase): one predicated batch, all loads
+      // in flight at once, added in the same ascending row order.
       uint4 v[U];
       Acc xv[U];
 #pragma unroll
       for (int u = 0; u < U; ++u) {
-        const bool in = j + u < j1;
-        v[u] = in ? ld_nc16(ap + (j + u) * lda) : make_uint4(0, 0, 0, 0);
-        xv[u] = in ? to_acc<T>(__ldg(x + j + u)) : Acc(0);
+        const bool in = j + u * P < j1;
+        v[u] = in ? ld_nc16(ap + (j + u * P) * lda) : make_uint4(0, 0, 0, 0);
+        xv[u] = in ? to_acc<T>(__ldg(x + j + u * P)) : Acc(0);
       }
 #pragma unroll
       for (int u = 0; u < U; ++u) {
-        if (j + u < j1) {
+        if (j + u * P < j1) {
           Acc f[V];
           unpack_v<T>(v[u], f);
 #pragma unroll
@@ -214,9 +225,21 @@ __global__ void __launch_bounds__(GS_THREADS, 2)
       }
     }
   }
+  // Phase 0 adds phases 1..P-1 in order.
+  if (ph > 0) {
+#pragma unroll
+    for (int i = 0; i < V; ++i) s_phase[ph - 1][cv * V + i] = acc[i];
+  }
+  __syncthreads();
+  if (ph == 0) {
+#pragma unroll
+    for (int q = 0; q < P - 1; ++q)
+#pragma unroll
+      for (int i = 0; i < V; ++i) acc[i] += s_phase[q][cv * V + i];
+  }
 
   if (splits == 1) {
-    if (has) {
+    if (ph == 0 && has) {
 #pragma unroll
       for (int i = 0; i < V; ++i) {
         Acc res = alpha * acc[i];
@@ -226,10 +249,21 @@ __global__ void __launch_bounds__(GS_THREADS, 2)
     }
     return;
   }
-  if (has) {
-    Acc* dst = partials + static_cast<int64_t>(blockIdx.y) * M + col;
+  // V partials of one split are V * sizeof(Acc) contiguous, 16-byte aligned
+  // bytes (M % V == 0, 256-byte aligned workspace): vector stores and loads.
+  constexpr int QN = V * static_cast<int>(sizeof(Acc)) / 16;
+  static_assert(QN * 16 == V * static_cast<int>(sizeof(Acc)), "partial vector size");
+  union PartialVec {
+    uint4 q[QN];
+    Acc a[V];
+  };
+  if (ph == 0 && has) {
+    PartialVec u;
 #pragma unroll
-    for (int i = 0; i < V; ++i) dst[i] = acc[i];
+    for (int i = 0; i < V; ++i) u.a[i] = acc[i];
+    uint4* dst = reinterpret_cast<uint4*>(partials + static_cast<int64_t>(blockIdx.y) * M + col);
+#pragma unroll
+    for (int q = 0; q < QN; ++q) __stcg(dst + q, u.q[q]);
   }
   __threadfence();
   __syncthreads();
@@ -241,25 +275,19 @@ __global__ void __launch_bounds__(GS_THREADS, 2)
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  if (has) {
-    Acc sum[V];
+  // Thread (cv, ph) adds splits ph, ph + P, ... in ascending order, loads
+  // issued GS_T_RED_BATCH at a time; then the phases are added in order.
+  Acc sum[V];
 #pragma unroll
-    for (int i = 0; i < V; ++i) sum[i] = 0;
-    // Split order 0..splits-1; loads issued GS_T_RED_BATCH at a time.
-    // V partials of one split are V * sizeof(Acc) contiguous, 16-byte
-    // aligned bytes (M % V == 0, 256-byte aligned workspace): vector loads.
-    constexpr int QN = V * static_cast<int>(sizeof(Acc)) / 16;
-    static_assert(QN * 16 == V * static_cast<int>(sizeof(Acc)), "partial vector size");
+  for (int i = 0; i < V; ++i) sum[i] = 0;
+  if (has) {
     constexpr int GS_T_RED_BATCH = GS_T_RED_REGS / (V * static_cast<int>(sizeof(Acc)) / 4);
-    for (unsigned int k0 = 0; k0 < splits; k0 += GS_T_RED_BATCH) {
+    for (unsigned int k0 = ph; k0 < splits; k0 += GS_T_RED_BATCH * P) {
       Acc pv[GS_T_RED_BATCH][V];
 #pragma unroll
       for (int b = 0; b < GS_T_RED_BATCH; ++b) {
-        const unsigned int k = k0 + b;
-        union {
-          uint4 q[QN];
-          Acc a[V];
-        } u;
+        const unsigned int k = k0 + b * P;
+        PartialVec u;
         const uint4* src = reinterpret_cast<const uint4*>(partials + static_cast<int64_t>(k) * M + col);
 #pragma unroll
         for (int q = 0; q < QN; ++q) u.q[q] = (k < splits) ? __ldcg(src + q) : make_uint4(0, 0, 0, 0);
@@ -268,10 +296,21 @@ __global__ void __launch_bounds__(GS_THREADS, 2)
       }
 #pragma unroll
       for (int b = 0; b < GS_T_RED_BATCH; ++b)
-        if (k0 + b < splits)
+        if (k0 + b * P < splits)
 #pragma unroll
           for (int i = 0; i < V; ++i) sum[i] += pv[b][i];
     }
+  }
+  if (ph > 0) {
+#pragma unroll
+    for (int i = 0; i < V; ++i) s_phase[ph - 1][cv * V + i] = sum[i];
+  }
+  __syncthreads();
+  if (ph == 0 && has) {
+#pragma unroll
+    for (int q = 0; q < P - 1; ++q)
+#pragma unroll
+      for (int i = 0; i < V; ++i) sum[i] += s_phase[q][cv * V + i];
 #pragma unroll
     for (int i = 0; i < V; ++i) {
       Acc res = alpha * sum[i];
@@ -320,15 +359,16 @@ GemvStreamPlan plan_gemv_stream(int trans, int64_t M, int64_t N, int64_t lda, co
     p.ok = true;
   } else {
     if (M % V || N < 16) return p;
-    const int64_t strip = static_cast<int64_t>(GS_THREADS) * V;
+    const int64_t strip = static_cast<int64_t>(GS_T_SV) * V;
     p.strips = (M + strip - 1) / strip;
     if (p.strips > 4096) return p;
-    int64_t splits = std::max<int64_t>(1, ctas_full / p.strips);
-    splits = std::min<int64_t>(splits, std::max<int64_t>(1, N / GS_T_UNROLL));
+    // Whole batches of GS_T_UNROLL rows per phase in each split (only the
+    // last split may end in a partial batch).
+    const int64_t batch_rows = static_cast<int64_t>(GS_T_UNROLL) * GS_T_PHASES;
+    int64_t splits = std::max<int64_t>(1, GS_T_WAVES * ctas_full / p.strips);
+    splits = std::min<int64_t>(splits, std::max<int64_t>(1, N / batch_rows));
     splits = std::min<int64_t>(splits, 65535);
-    // Whole batches of GS_T_UNROLL rows per split (only the last split may
-    // end in a partial batch).
-    p.rows_per_split = ((N + splits - 1) / splits + GS_T_UNROLL - 1) / GS_T_UNROLL * GS_T_UNROLL;
+    p.rows_per_split = ((N + splits - 1) / splits + batch_rows - 1) / batch_rows * batch_rows;
     p.splits = (N + p.rows_per_split - 1) / p.rows_per_split;
     if (p.splits > 1) p.partial_bytes = (static_cast<size_t>(p.splits) * M * sizeof(Acc) + 255) / 256 * 256;
     p.trans = true;

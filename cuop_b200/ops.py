@@ -33,9 +33,15 @@ def _dtype_code(t: torch.Tensor) -> int:
 
 
 def _require_cuda(*ts: torch.Tensor) -> None:
+    """Every tensor on one CUDA device (the kernels dereference all pointers there)."""
+    dev = None
     for t in ts:
         if not t.is_cuda:
             raise N.CuopError(N.INVALID_ARGUMENT, "tensor is not on a CUDA device (no CPU path exists)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise N.CuopError(N.INVALID_ARGUMENT, f"tensors on {dev} and {t.device}")
 
 
 def _row_ld(t: torch.Tensor) -> int:
@@ -82,7 +88,7 @@ def gemm(A: torch.Tensor, B: torch.Tensor, C: Optional[torch.Tensor] = None, *, 
     if C is None:
         C = torch.empty((M, Nn), dtype=A.dtype, device=A.device)
         beta = 0.0
-    _require_cuda(C)
+    _require_cuda(A, B, C)
     if tuple(C.shape) != (M, Nn) or C.dtype != A.dtype:
         raise N.CuopError(N.SHAPE_MISMATCH, f"gemm: C must be {M}x{Nn} {A.dtype}")
     if bias is None and not relu:
@@ -94,7 +100,7 @@ def gemm(A: torch.Tensor, B: torch.Tensor, C: Optional[torch.Tensor] = None, *, 
     epi = N.EPI_RELU if relu else N.EPI_NONE
     bptr = 0
     if bias is not None:
-        _require_cuda(bias)
+        _require_cuda(A, bias)
         if bias.dtype != A.dtype or bias.numel() != Nn or not bias.is_contiguous():
             raise N.CuopError(N.SHAPE_MISMATCH, f"gemm: bias must be a contiguous [{Nn}] {A.dtype} vector")
         epi |= N.EPI_BIAS
@@ -124,6 +130,7 @@ def batched_gemm(A: torch.Tensor, B: torch.Tensor, C: Optional[torch.Tensor] = N
     if C is None:
         C = torch.empty((batch, M, Nn), dtype=A.dtype, device=A.device)
         beta = 0.0
+    _require_cuda(A, B, C)
     if tuple(C.shape) != (batch, M, Nn) or not C.is_contiguous():
         raise N.CuopError(N.SHAPE_MISMATCH, "batched_gemm: bad C")
     rc = N.lib().cuopx_gemm_strided_batched(
@@ -140,8 +147,12 @@ def gemv(A: torch.Tensor, x: torch.Tensor, y: Optional[torch.Tensor] = None, *, 
 
     trans=False: A is M x N, x has N entries, y has M.
     trans=True:  A is N x M (the reference reads A[col*m+row]); y = A^T x has M.
+    y may also be a pinned host tensor: the kernel then writes the result
+    straight into host memory (zero-copy), with no device-to-host copy.
     """
     _require_cuda(A, x)
+    if x.dtype != A.dtype or not x.is_contiguous():
+        raise N.CuopError(N.INVALID_ARGUMENT, f"gemv: x must be a contiguous {A.dtype} vector")
     if trans:
         Nn, M = A.size(0), A.size(1)
     else:
@@ -153,6 +164,12 @@ def gemv(A: torch.Tensor, x: torch.Tensor, y: Optional[torch.Tensor] = None, *, 
         beta = 0.0
     if y.numel() != M:
         raise N.CuopError(N.SHAPE_MISMATCH, f"gemv: y has {y.numel()} entries, expected {M}")
+    if y.dtype != A.dtype or not y.is_contiguous():
+        raise N.CuopError(N.INVALID_ARGUMENT, f"gemv: y must be a contiguous {A.dtype} vector")
+    if y.is_cuda:
+        _require_cuda(A, y)
+    elif not y.is_pinned():
+        raise N.CuopError(N.INVALID_ARGUMENT, "gemv: y must be on A's device or in pinned host memory")
     dt = _dtype_code(A)
     need = N.lib().cuopx_gemv_workspace_size(dt, int(trans), M, Nn)
     ws, wsb = workspace(need, A.device)
@@ -164,7 +181,10 @@ def gemv(A: torch.Tensor, x: torch.Tensor, y: Optional[torch.Tensor] = None, *, 
 
 def gather_column_blocks(blocks: torch.Tensor, out: torch.Tensor, stream=None) -> torch.Tensor:
     """blocks: [G, M, Nb] contiguous -> out: [M, G*Nb] row-major."""
+    _require_cuda(blocks, out)
     G, M, Nb = blocks.shape
+    if not blocks.is_contiguous() or out.size(0) != M or out.size(1) != G * Nb or out.dtype != blocks.dtype:
+        raise N.CuopError(N.SHAPE_MISMATCH, "gather_column_blocks: out must be [M, G*Nb] of the blocks' dtype")
     rc = N.lib().cuopx_gather_column_blocks(_dtype_code(blocks), G, M, Nb, blocks.data_ptr(), out.data_ptr(),
                                             _row_ld(out), _stream(stream))
     N.check(rc, "cuopx_gather_column_blocks")
@@ -244,7 +264,15 @@ def scal(alpha, x, n=None, incx=1, stream=None):
 
 
 def copy(x, y, n=None, incx=1, incy=1, stream=None):
-    _f32(x, y)
+    """y = x.  One side may be a pinned host tensor: the kernel then reads or
+    writes host memory directly (staging with no copy-engine transfer)."""
+    for t in (x, y):
+        if t.dtype != torch.float32:
+            raise N.CuopError(N.UNSUPPORTED_TYPE, "vector ops are fp32")
+    on_dev = [t for t in (x, y) if t.is_cuda]
+    if not on_dev or any(not t.is_cuda and not t.is_pinned() for t in (x, y)):
+        raise N.CuopError(N.INVALID_ARGUMENT, "copy: one side on a CUDA device, the other there or in pinned host memory")
+    _require_cuda(*on_dev)
     n = x.numel() if n is None else n
     N.check(N.lib().cuopx_copy(n, x.data_ptr(), incx, y.data_ptr(), incy, _stream(stream)), "cuopx_copy")
     return y

@@ -167,8 +167,9 @@ int cuopx_gemv(int dtype, int trans, int64_t M, int64_t N, double alpha, const v
  * hosts that own all device memory, latency-bound serving loops where an
  * allocation can stall or fail).  No counterpart in the reference.
  * Returns CUOPX_RESOURCE_UNAVAILABLE when the kernel chosen for the call
- * needs more than 2 MiB of scratch (fp32/fp64 with 16-byte-aligned rows
- * never do; fp16/bf16 transposed GEMV of large matrices does).  The first call on a device resolves the array's
+ * needs more than 2 MiB of scratch (rows that are 16-byte aligned and a
+ * multiple of 16 bytes long never do, at any size and type; other shapes
+ * can, e.g. bf16 transposed 8191 x 8192).  The first call on a device resolves the array's
  * device address; make it before any stream capture.  Calls share the array:
  * calls that overlap on the GPU race, so order them on one stream.  Each call
  * zeroes the array's counter block on `stream` before its kernels run.

@@ -115,3 +115,43 @@ def test_benchmark_size_vs_cpu_and_reference_operator(dev, trans):
         assert rc == 0
         assert O.rel_frobenius(yr.cpu().numpy(), exact) <= tol
         assert O.rel_frobenius(y.cpu().numpy(), yr.cpu().numpy()) <= tol
+
+
+@pytest.mark.parametrize("M,N", [(1000, 8192), (256, 100000), (8192, 17), (8192, 4099), (4352, 777)])
+def test_transposed_strip_and_split_edges(dev, M, N):
+    """Partial last strip (M not a multiple of the strip width), many splits
+    with a ragged last one, a single split, and rows not a multiple of the
+    per-split batch."""
+    A = O.uniform((N, M), seed=21)
+    x = O.uniform(N, seed=22)
+    y = cx.gemv(to_dev_f32(A, dev), to_dev_f32(x, dev), trans=True)
+    exact = O.gemv_f64acc(A, x, trans=True)
+    assert O.rel_frobenius(y.cpu().numpy(), exact) <= 1e-5 * np.sqrt(N)
+    assert cx.device_error() == 0
+
+
+@pytest.mark.parametrize("trans", [False, True])
+def test_result_into_pinned_host_memory(dev, trans):
+    """y in pinned host memory: the kernel writes the result there directly,
+    bit-identical to a device y."""
+    M, N = 2048, 3072
+    A = to_dev_f32(O.uniform((N, M) if trans else (M, N), seed=23), dev)
+    x = to_dev_f32(O.uniform(N, seed=24), dev)
+    y_dev = cx.gemv(A, x, trans=trans)
+    y_host = torch.full((M,), float("nan")).pin_memory()
+    cx.gemv(A, x, y_host, trans=trans)
+    torch.cuda.synchronize()
+    assert torch.equal(y_host, y_dev.cpu())
+
+
+def test_outputs_that_the_device_cannot_reach_are_refused(dev):
+    A = torch.zeros(64, 64, device=dev)
+    x = torch.zeros(64, device=dev)
+    with pytest.raises(cx.CuopError):
+        cx.gemv(A, x, torch.zeros(64))  # pageable host memory
+    with pytest.raises(cx.CuopError):
+        cx.gemv(A, x.double())  # x of another dtype
+    with pytest.raises(cx.CuopError):
+        cx.gemm(A.half(), A.half(), torch.zeros(64, 64, dtype=torch.half))
+    with pytest.raises(cx.CuopError):
+        cx.batched_gemm(A.half()[None], A.half()[None], torch.zeros(1, 64, 64, dtype=torch.half))

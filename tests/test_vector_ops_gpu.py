@@ -73,3 +73,18 @@ def test_gather_column_blocks(dev):
     cx.gather_column_blocks(blocks, out)
     ref = torch.cat([blocks[g] for g in range(G)], dim=1)
     assert torch.equal(out, ref)
+
+
+def test_copy_stages_through_pinned_host_memory(dev):
+    """copy() with one side in pinned host memory reads or writes it directly."""
+    x = torch.randn(10007).pin_memory()
+    d = torch.empty(10007, device=dev)
+    cx.copy(x, d)
+    back = torch.full((10007,), float("nan")).pin_memory()
+    cx.copy(d, back)
+    torch.cuda.synchronize()
+    assert torch.equal(back, x)
+    with pytest.raises(cx.CuopError):
+        cx.copy(torch.zeros(4), torch.zeros(4, device=dev))  # pageable host memory
+    with pytest.raises(cx.CuopError):
+        cx.copy(x, back)  # neither side on the device

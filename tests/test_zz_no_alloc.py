@@ -69,8 +69,9 @@ def test_noalloc_matches_workspace_entry_point_twice(dev, M, Nn, trans, kernel):
 
 
 def test_noalloc_rejects_scratch_beyond_limit(dev):
-    """bf16 transposed GEMV of 8192^2 needs more than the 2 MiB scratch."""
-    M = Nn = 8192
+    """bf16 transposed GEMV whose rows are not a multiple of 16 bytes (M = 8191)
+    runs the generic split kernel, which needs more than the 2 MiB scratch."""
+    M, Nn = 8191, 8192
     need = N.lib().cuopx_gemv_workspace_size(N.BF16, 1, M, Nn)
     assert need > (2 << 20)
     A = torch.zeros(Nn, M, dtype=torch.bfloat16, device=dev)
@@ -80,3 +81,18 @@ def test_noalloc_rejects_scratch_beyond_limit(dev):
     assert rc == N.RESOURCE_UNAVAILABLE
     torch.cuda.synchronize()
     assert torch.all(y == 7.0)  # nothing was launched
+
+
+def test_noalloc_streaming_transposed_fits_at_any_size(dev):
+    """The streaming transposed kernel's partials are bounded by the resident
+    CTA count times one strip, so even bf16 8192^2 fits the scratch."""
+    M = Nn = 8192
+    A = torch.randn(Nn, M, device=dev).bfloat16()
+    x = torch.randn(Nn, device=dev).bfloat16()
+    y_ref = torch.empty(M, dtype=torch.bfloat16, device=dev)
+    assert _with_workspace(A, x, y_ref, True, M, Nn, M, dtype=N.BF16) == N.SUCCESS
+    y = torch.empty(M, dtype=torch.bfloat16, device=dev)
+    assert _noalloc(A, x, y, True, M, Nn, M, dtype=N.BF16) == N.SUCCESS
+    assert cx.last_kernel() == "gemv_t_lsu"
+    torch.cuda.synchronize()
+    assert torch.equal(y, y_ref)
