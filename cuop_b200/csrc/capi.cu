@@ -119,7 +119,8 @@ int run_variant(int v, const GemmProblem& p, cudaStream_t stream) {
   const bool x3_ok = p.K > 0 && gemm_tf32x3_supported(p) && mode != CUOPX_FP32_FFMA;
   const bool ffma_ok = p.K > 0 && gemm_simt_f32_supported(p) && mode != CUOPX_FP32_TF32X3;
   switch (v) {
-    case kVariantTc2: return tc_ok ? gemm_tc2(p, stream) : -1;
+    case kVariantTc2: return tc_ok ? gemm_tc2(p, stream, 256) : -1;
+    case kVariantTc2x512: return tc_ok ? gemm_tc2(p, stream, 512) : -1;
     case kVariantTc128x256: return tc_ok ? gemm_tc(p, stream, 256) : -1;
     case kVariantTc128x128: return tc_ok ? gemm_tc(p, stream, 128) : -1;
     case kVariantTf32x3_64: return x3_ok ? gemm_tf32x3(p, stream, 64) : -1;

@@ -62,10 +62,12 @@ int gemm_tc_peers(const GemmProblem& p, void* const* peers, int npeers, cudaStre
 
 // Two-SM (cta_group::2) tcgen05 back-end (gemm_tc2.cu) for large fp16/bf16.
 bool gemm_tc2_wanted(const GemmProblem& p);
-int gemm_tc2(const GemmProblem& p, cudaStream_t stream);
+// pbn: pair tile width, 256 or 512; 0 = choose (gemm_tc2_pick_width).
+int gemm_tc2_pick_width(const GemmProblem& p);
+int gemm_tc2(const GemmProblem& p, cudaStream_t stream, int pbn = 0);
 // Same kernel; every output chunk is also stored to peers[0..npeers) (peer
 // mappings of identically laid out outputs, offset to this block's columns).
-int gemm_tc2_peers(const GemmProblem& p, void* const* peers, int npeers, cudaStream_t stream);
+int gemm_tc2_peers(const GemmProblem& p, void* const* peers, int npeers, cudaStream_t stream, int pbn = 0);
 
 // 3xTF32 tcgen05 back-end (gemm_tf32x3.cu) for fp32.
 bool gemm_tf32x3_supported(const GemmProblem& p);
@@ -82,7 +84,8 @@ enum GemmVariant : int {
   kVariantTf32x3_128 = 5,
   kVariantFfma = 6,        // register-blocked fp32 FFMA
   kVariantGeneric = 7,     // any dtype / layout
-  kVariantCount = 8,
+  kVariantTc2x512 = 8,     // 2-SM tcgen05, 256 x 512 pair tiles
+  kVariantCount = 9,
 };
 const char* gemm_variant_name(int v);
 // The override (set by cuopx_set_gemm_variant) if any, else the first

@@ -1,20 +1,29 @@
 // Two-SM tcgen05 GEMM (cta_group::2) for large fp16/bf16 problems.
 //
-// A cluster of two CTAs on two SMs owns a 256 x 256 output tile.  CTA r of the
-// pair loads rows [128r, 128r+128) of the A tile and columns [128r, 128r+128)
+// A cluster of two CTAs on two SMs owns a 256 x PBN output tile (PBN = 256 or
+// 512).  CTA r of the pair loads rows [128r, 128r+128) of the A tile and, for
+// each 256-column slot h of the tile, columns [256h + 128r, 256h + 128r + 128)
 // of the B tile into its own shared memory; one tcgen05.mma.cta_group::2
-// (M=256, N=256, K=16) issued by the even CTA reads both CTAs' halves and
-// writes each CTA's 128 accumulator rows into that CTA's TMEM.  Per SM this
-// halves the shared-memory operand traffic of the 1-SM 128 x 256 kernel
-// (32 KB instead of 48 KB per 64-deep K block).
+// (M=256, N=256, K=16) per slot, issued by the even CTA, reads both CTAs'
+// halves and writes each CTA's 128 accumulator rows of that slot into the
+// CTA's TMEM (slot h = columns [256h, 256h+256) of the 512).  Per SM this
+// halves the shared-memory operand traffic of the 1-SM 128 x 256 kernel.
+//   PBN = 256: 6-stage ring of 32 KB; the two TMEM slots alternate between
+//              tiles, so the epilogue of a tile overlaps the next one.
+//   PBN = 512: 4-stage ring of 48 KB; a tile fills both slots, so each K
+//              block pulls 25 % fewer operand bytes from L2 per FLOP and
+//              covers twice the MMA time per stage.  The epilogue drains
+//              slot 0, releases it, then slot 1; the next tile's MMAs into
+//              slot 0 start as soon as slot 0 is free and its first MMAs
+//              into slot 1 wait only for the rest of the drain.
 //
 //   warp 0      TMA producer (both CTAs): loads complete on the LEADER's
 //               `full` mbarrier (.cta_group::2); the leader posts the
 //               expected byte count for both halves.
 //   warp 1      TMEM allocation (cta_group::2, both CTAs); on the leader, the
-//               MMA issuer: waits `full`, issues 4 MMAs per stage, commits
-//               stage release to `empty` and tile completion to `acc_full`
-//               in BOTH CTAs (tcgen05.commit multicast).
+//               MMA issuer: waits `full`, issues 4 MMAs per slot per stage,
+//               commits stage release to `empty` and tile completion to
+//               `acc_full` in BOTH CTAs (tcgen05.commit multicast).
 //   warps 2..5  epilogue (both CTAs): own TMEM rows -> alpha/beta -> swizzled
 //               staging -> TMA store; then arrive on the leader's `acc_empty`.
 // Tile scheduling: one cluster per pair tile is launched; the leader asks the
@@ -33,32 +42,41 @@ namespace cuopx {
 
 namespace {
 
-constexpr int P_BM = 128;   // rows per CTA (pair: 256)
-constexpr int P_BN = 256;   // pair tile columns; each CTA holds 128 of B
+constexpr int P_BM = 128;  // rows per CTA (pair: 256)
 constexpr int P_BK = 64;
-constexpr int P_STAGES = 6;
 constexpr int P_THREADS = 192;
 constexpr int P_EPI_WARPS = 4;
 constexpr int P_CHUNK = 64;
 constexpr uint32_t P_TMEM_COLS = 512;
-constexpr int P_ACC_BUFS = 2;
-constexpr int P_GROUP_M = 8;  // pair-row tiles per raster group
+constexpr int P_SLOT_COLS = 256;  // accumulator columns of one MMA (N = 256)
+constexpr int P_SLOTS = 2;        // TMEM holds two slots
+constexpr int P_GROUP_M = 8;      // pair-row tiles per raster group
 // Scheduler ring depth (> the producers' lead over the epilogue, in tiles).
 constexpr int P_CLC_SLOTS = 16;
 // Arrivals on the leader's clc_empty per slot: leader producer, MMA issuer and
 // epilogue warps, plus the partner's producer and epilogue warps (remote).
 constexpr int P_CLC_READERS = (2 + P_EPI_WARPS) + (1 + P_EPI_WARPS);
 
+template <int PBN>
+struct PairCfg {
+  static_assert(PBN == 256 || PBN == 512, "pair tile width");
+  static constexpr int SPT = PBN / P_SLOT_COLS;  // TMEM slots per tile
+  static constexpr int STAGES = SPT == 1 ? 6 : 4;
+};
+
+template <int PBN>
 struct PairSmem {
-  static constexpr int A_STAGE = P_BM * P_BK * 2;            // 16 KB
-  static constexpr int B_STAGE = (P_BN / 2) * P_BK * 2;      // 16 KB (this CTA's half)
-  static constexpr int C_STAGE = 32 * P_CHUNK * 2;           // 4 KB
+  static constexpr int STAGES = PairCfg<PBN>::STAGES;
+  static constexpr int A_STAGE = P_BM * P_BK * 2;               // 16 KB
+  static constexpr int B_PIECE = (P_SLOT_COLS / 2) * P_BK * 2;  // 16 KB: this CTA's half of one slot
+  static constexpr int B_STAGE = PairCfg<PBN>::SPT * B_PIECE;
+  static constexpr int C_STAGE = 32 * P_CHUNK * 2;              // 4 KB
   static constexpr int OFF_A = 0;
-  static constexpr int OFF_B = P_STAGES * A_STAGE;
-  static constexpr int OFF_C = OFF_B + P_STAGES * B_STAGE;
+  static constexpr int OFF_B = STAGES * A_STAGE;
+  static constexpr int OFF_C = OFF_B + STAGES * B_STAGE;
   static constexpr int OFF_BAR = OFF_C + P_EPI_WARPS * 2 * C_STAGE;
   // full[S], empty[S], acc_full[2], acc_empty[2], drain
-  static constexpr int NUM_BARS = 2 * P_STAGES + 2 * P_ACC_BUFS + 1;
+  static constexpr int NUM_BARS = 2 * STAGES + 2 * P_SLOTS + 1;
   // Tile-scheduler ring: P_CLC_SLOTS 16-byte launch-control responses, then
   // clc_full[P_CLC_SLOTS] and clc_empty[P_CLC_SLOTS] mbarriers.
   static constexpr int OFF_CLC = (OFF_BAR + NUM_BARS * 8 + 15) / 16 * 16;
@@ -72,7 +90,7 @@ constexpr int P_MAX_PEERS = 7;  // one node: up to 8 ranks
 
 struct PairParams {
   int M, N, K, batch;
-  int tiles_m, tiles_n, num_tiles, k_blocks;  // tiles are 256 x 256 pair tiles
+  int tiles_m, tiles_n, num_tiles, k_blocks;  // tiles are 256 x PBN pair tiles
   float alpha, beta;
   const void* C_in;
   int64_t ldc, strideC;
@@ -214,14 +232,17 @@ __device__ __forceinline__ uint32_t pack2_pair<__half>(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-template <typename T, bool A_MN, bool B_MN>
+template <typename T, bool A_MN, bool B_MN, int PBN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmC, const PairParams p) {
-  using L = PairSmem;
+  using L = PairSmem<PBN>;
+  constexpr int SPT = PairCfg<PBN>::SPT;
+  constexpr int P_STAGES = PairCfg<PBN>::STAGES;
+  constexpr int CHUNKS_PER_SLOT = P_SLOT_COLS / P_CHUNK;
   constexpr uint32_t PAIR_TX = 2u * static_cast<uint32_t>(L::A_STAGE + L::B_STAGE);
   constexpr uint32_t AB_FMT = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
-  constexpr uint32_t IDESC = make_idesc(AB_FMT, A_MN, B_MN, 2 * P_BM, P_BN);
+  constexpr uint32_t IDESC = make_idesc(AB_FMT, A_MN, B_MN, 2 * P_BM, P_SLOT_COLS);
 
   extern __shared__ __align__(1024) unsigned char pair_smem_raw[];
   unsigned char* smem = align_smem_1024(pair_smem_raw);
@@ -229,8 +250,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
   uint64_t* full = bars;
   uint64_t* empty = bars + P_STAGES;
   uint64_t* acc_full = bars + 2 * P_STAGES;
-  uint64_t* acc_empty = bars + 2 * P_STAGES + P_ACC_BUFS;
-  uint64_t* drain = bars + 2 * P_STAGES + 2 * P_ACC_BUFS;
+  uint64_t* acc_empty = bars + 2 * P_STAGES + P_SLOTS;
+  uint64_t* drain = bars + 2 * P_STAGES + 2 * P_SLOTS;
   unsigned char* clc_resp = smem + L::OFF_CLC;
   uint64_t* clc_full = reinterpret_cast<uint64_t*>(smem + L::OFF_CLC_BAR);
   uint64_t* clc_empty = clc_full + P_CLC_SLOTS;
@@ -248,7 +269,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
       mbar_init(&full[s], 1);   // leader: its own arrive.expect_tx; both CTAs' bytes
       mbar_init(&empty[s], 1);  // one multicast commit per phase
     }
-    for (int a = 0; a < P_ACC_BUFS; ++a) {
+    for (int a = 0; a < P_SLOTS; ++a) {
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], 2 * P_EPI_WARPS);  // leader's copy: 4 local + 4 remote arrivals
     }
@@ -307,7 +328,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
         int b, mt, nt;
         pair_tile_coords(t, p, b, mt, nt);
         const int m0 = mt * 2 * P_BM + static_cast<int>(rank) * P_BM;
-        const int n0 = nt * P_BN + static_cast<int>(rank) * (P_BN / 2);
+        const int n0 = nt * PBN + static_cast<int>(rank) * (P_SLOT_COLS / 2);
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, kDevErrWaitTimeoutEmpty, abort_flag)) {
             ok = false;
@@ -324,12 +345,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
           } else {
             tma_load_3d_pair(sa, &tmA, mbar, k0, m0, b);
           }
-          if constexpr (B_MN) {
 #pragma unroll
-            for (int j = 0; j < (P_BN / 2) / 64; ++j)
-              tma_load_3d_pair(sb + j * (64 * P_BK * 2), &tmB, mbar, n0 + 64 * j, k0, b);
-          } else {
-            tma_load_3d_pair(sb, &tmB, mbar, k0, n0, b);
+          for (int h = 0; h < SPT; ++h) {
+            unsigned char* sbh = sb + h * L::B_PIECE;
+            const int n0h = n0 + h * P_SLOT_COLS;
+            if constexpr (B_MN) {
+#pragma unroll
+              for (int j = 0; j < (P_SLOT_COLS / 2) / 64; ++j)
+                tma_load_3d_pair(sbh + j * (64 * P_BK * 2), &tmB, mbar, n0h + 64 * j, k0, b);
+            } else {
+              tma_load_3d_pair(sbh, &tmB, mbar, k0, n0h, b);
+            }
           }
           issued_mask |= 1u << stage;
           phase_mask = (phase_mask & ~(1u << stage)) | (phase << stage);
@@ -403,16 +429,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     if (leader && lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      int acc = 0;
-      uint32_t acc_phase = 0;
+      int acc = 0;              // first TMEM slot of the tile (alternates when SPT == 1)
+      uint32_t empty_bits = 0;  // bit s: parity of slot s's next acc_empty phase
       bool ok = true, issued = false;
       for (int seq = 0; ok; ++seq) {
-        if (!mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1u, kDevErrWaitTimeoutAccEmpty, abort_flag)) {
+        const int s0 = SPT == 1 ? acc : 0;
+        if (!mbar_wait_bounded(&acc_empty[s0], ((empty_bits >> s0) & 1u) ^ 1u, kDevErrWaitTimeoutAccEmpty,
+                               abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after_sync();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * P_BN);
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!mbar_wait_bounded(&full[stage], phase, kDevErrWaitTimeoutFull, abort_flag)) {
             ok = false;
@@ -422,20 +449,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
           const uint32_t sa = smem_u32(smem + L::OFF_A + stage * L::A_STAGE);
           const uint32_t sb = smem_u32(smem + L::OFF_B + stage * L::B_STAGE);
 #pragma unroll
-          for (int kk = 0; kk < P_BK / 16; ++kk) {
-            const uint64_t ad = A_MN ? make_smem_desc_sw128(sa + kk * 2048, 64 * P_BK * 2, 1024)
-                                     : make_smem_desc_sw128(sa + kk * 32, 16, 1024);
-            const uint64_t bd = B_MN ? make_smem_desc_sw128(sb + kk * 2048, 64 * P_BK * 2, 1024)
-                                     : make_smem_desc_sw128(sb + kk * 32, 16, 1024);
-            umma_f16_pair(d_tmem, ad, bd, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+          for (int h = 0; h < SPT; ++h) {
+            const int slot = s0 + h;
+            if (h > 0 && kb == 0) {
+              // The rest of the previous tile's drain: the epilogue releases
+              // slot h after slot 0.
+              if (!mbar_wait_bounded(&acc_empty[slot], ((empty_bits >> slot) & 1u) ^ 1u, kDevErrWaitTimeoutAccEmpty,
+                                     abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after_sync();
+            }
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(slot * P_SLOT_COLS);
+            const uint32_t sbh = sb + static_cast<uint32_t>(h * L::B_PIECE);
+#pragma unroll
+            for (int kk = 0; kk < P_BK / 16; ++kk) {
+              const uint64_t ad = A_MN ? make_smem_desc_sw128(sa + kk * 2048, 64 * P_BK * 2, 1024)
+                                       : make_smem_desc_sw128(sa + kk * 32, 16, 1024);
+              const uint64_t bd = B_MN ? make_smem_desc_sw128(sbh + kk * 2048, 64 * P_BK * 2, 1024)
+                                       : make_smem_desc_sw128(sbh + kk * 32, 16, 1024);
+              umma_f16_pair(d_tmem, ad, bd, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+            }
+            issued = true;
           }
-          issued = true;
+          if (!ok) break;
           umma_commit_pair(&empty[stage]);
           if (++stage == P_STAGES) stage = 0, phase ^= 1u;
         }
         if (!ok) break;
-        umma_commit_pair(&acc_full[acc]);
-        if (++acc == P_ACC_BUFS) acc = 0, acc_phase ^= 1u;
+        umma_commit_pair(&acc_full[s0]);
+#pragma unroll
+        for (int h = 0; h < SPT; ++h) empty_bits ^= 1u << (s0 + h);
+        if (SPT == 1) acc ^= 1;
         const int cs = seq % P_CLC_SLOTS;
         if (!mbar_wait_bounded(&clc_full[cs], static_cast<uint32_t>(seq / P_CLC_SLOTS) & 1u, kDevErrWaitTimeoutFull,
                                abort_flag))
@@ -462,8 +508,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     const int q = warp & 3;
     const int row_in_tile = 32 * q + lane;
     unsigned char* const stage_base = smem + L::OFF_C + (warp - 2) * 2 * L::C_STAGE;  // two buffers
-    int acc = 0;
-    uint32_t acc_phase = 0;
+    int acc = 0;             // first TMEM slot of the tile (alternates when SPT == 1)
+    uint32_t full_bits = 0;  // bit s: parity of slot s's next acc_full phase
     int sbuf = 0;
     const T* Cin = static_cast<const T*>(p.C_in);
     int t = pair;
@@ -471,21 +517,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
       int b, mt, nt;
       pair_tile_coords(t, p, b, mt, nt);
       const int m0 = mt * 2 * P_BM + static_cast<int>(rank) * P_BM;
-      const int n0 = nt * P_BN;
-      if (!mbar_wait_bounded(&acc_full[acc], acc_phase, kDevErrWaitTimeoutAccFull, abort_flag)) break;
+      const int n0 = nt * PBN;
+      const int s0 = SPT == 1 ? acc : 0;
+      if (!mbar_wait_bounded(&acc_full[s0], (full_bits >> s0) & 1u, kDevErrWaitTimeoutAccFull, abort_flag)) break;
       tc_fence_after_sync();
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(acc * P_BN);
+      const uint32_t t_row =
+          tmem_base + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(s0 * P_SLOT_COLS);
       const int64_t grow = static_cast<int64_t>(m0) + row_in_tile;
 #pragma unroll 1
-      for (int ch = 0; ch < P_BN / P_CHUNK; ++ch) {
+      for (int ch = 0; ch < PBN / P_CHUNK; ++ch) {
+        // Chunk ch is TMEM columns [64ch, 64ch+64) of the tile's slots.
         uint32_t r0[32], r1[32];
         tmem_ld_32x32b_x32(t_row + ch * P_CHUNK, r0);
         tmem_ld_32x32b_x32(t_row + ch * P_CHUNK + 32, r1);
         tmem_wait_ld();
-        if (ch == P_BN / P_CHUNK - 1) {
+        if (ch % CHUNKS_PER_SLOT == CHUNKS_PER_SLOT - 1) {
+          // Last read of this slot: the MMA issuer may overwrite it.
           tc_fence_before_sync();
           __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(map_to_rank(&acc_empty[acc], 0));
+          if (lane == 0) mbar_arrive_cluster(map_to_rank(&acc_empty[s0 + ch / CHUNKS_PER_SLOT], 0));
         }
         float v[64];
 #pragma unroll
@@ -546,7 +596,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
         }
         sbuf ^= 1;
       }
-      if (++acc == P_ACC_BUFS) acc = 0, acc_phase ^= 1u;
+      full_bits ^= 1u << s0;
+      if (SPT == 1) acc ^= 1;
       const int cs = seq % P_CLC_SLOTS;
       const uint32_t cpar = static_cast<uint32_t>(seq / P_CLC_SLOTS) & 1u;
       const bool got = leader ? mbar_wait_bounded(&clc_full[cs], cpar, kDevErrWaitTimeoutAccFull, abort_flag)
@@ -576,10 +627,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
   }
 }
 
-template <typename T, bool A_MN, bool B_MN>
+template <typename T, bool A_MN, bool B_MN, int PBN>
 int launch_tc2(const GemmProblem& p, cudaStream_t stream, const char* name, void* const* peers = nullptr,
                int npeers = 0) {
-  using L = PairSmem;
+  using L = PairSmem<PBN>;
   const CUtensorMapDataType dt =
       std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap mA, mB, mC;
@@ -587,7 +638,7 @@ int launch_tc2(const GemmProblem& p, cudaStream_t stream, const char* name, void
   if (A_MN) ok &= make_map(&mA, dt, p.A, p.M, p.K, p.batch, p.lda, p.strideA, 64, P_BK);
   else ok &= make_map(&mA, dt, p.A, p.K, p.M, p.batch, p.lda, p.strideA, P_BK, P_BM);
   if (B_MN) ok &= make_map(&mB, dt, p.B, p.N, p.K, p.batch, p.ldb, p.strideB, 64, P_BK);
-  else ok &= make_map(&mB, dt, p.B, p.K, p.N, p.batch, p.ldb, p.strideB, P_BK, P_BN / 2);
+  else ok &= make_map(&mB, dt, p.B, p.K, p.N, p.batch, p.ldb, p.strideB, P_BK, P_SLOT_COLS / 2);
   ok &= make_map(&mC, dt, p.C, p.N, p.M, p.batch, p.ldc, p.strideC, P_CHUNK, 32);
   if (!ok) return CUOPX_CUDA_ERROR;
   PairParams prm;
@@ -596,7 +647,7 @@ int launch_tc2(const GemmProblem& p, cudaStream_t stream, const char* name, void
   prm.K = static_cast<int>(p.K);
   prm.batch = static_cast<int>(p.batch);
   prm.tiles_m = static_cast<int>((p.M + 2 * P_BM - 1) / (2 * P_BM));
-  prm.tiles_n = static_cast<int>((p.N + P_BN - 1) / P_BN);
+  prm.tiles_n = static_cast<int>((p.N + PBN - 1) / PBN);
   prm.num_tiles = prm.tiles_m * prm.tiles_n * prm.batch;
   prm.k_blocks = static_cast<int>((p.K + P_BK - 1) / P_BK);
   prm.alpha = static_cast<float>(p.alpha);
@@ -609,7 +660,7 @@ int launch_tc2(const GemmProblem& p, cudaStream_t stream, const char* name, void
   if (npeers < 0 || npeers > P_MAX_PEERS) return CUOPX_INVALID_ARGUMENT;
   prm.npeers = npeers;
   for (int i = 0; i < P_MAX_PEERS; ++i) prm.peer_C[i] = i < npeers ? peers[i] : nullptr;
-  auto kern = gemm_tc2_kernel<T, A_MN, B_MN>;
+  auto kern = gemm_tc2_kernel<T, A_MN, B_MN, PBN>;
   static bool attr_set[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return CUOPX_CUDA_ERROR;
@@ -641,21 +692,42 @@ bool gemm_tc2_wanted(const GemmProblem& p) {
   return (p.K >= 6144 && tiles >= 64) || (p.K >= 4096 && tiles >= 512);
 }
 
-int gemm_tc2(const GemmProblem& p, cudaStream_t stream) { return gemm_tc2_peers(p, nullptr, 0, stream); }
+int gemm_tc2(const GemmProblem& p, cudaStream_t stream, int pbn) { return gemm_tc2_peers(p, nullptr, 0, stream, pbn); }
 
-int gemm_tc2_peers(const GemmProblem& p, void* const* peers, int npeers, cudaStream_t stream) {
+namespace {
+
+template <int PBN>
+int launch_tc2_layout(const GemmProblem& p, void* const* peers, int npeers, cudaStream_t stream) {
   const bool a_mn = p.transA, b_mn = !p.transB;
-  const char* name = npeers > 0 ? "gemm_tc2_256x256_peer" : "gemm_tc2_256x256";
+  const char* name = PBN == 512 ? (npeers > 0 ? "gemm_tc2_256x512_peer" : "gemm_tc2_256x512")
+                                : (npeers > 0 ? "gemm_tc2_256x256_peer" : "gemm_tc2_256x256");
   if (p.dtype == CUOPX_BF16) {
-    if (!a_mn && b_mn) return launch_tc2<__nv_bfloat16, false, true>(p, stream, name, peers, npeers);
-    if (!a_mn && !b_mn) return launch_tc2<__nv_bfloat16, false, false>(p, stream, name, peers, npeers);
-    if (a_mn && b_mn) return launch_tc2<__nv_bfloat16, true, true>(p, stream, name, peers, npeers);
-    return launch_tc2<__nv_bfloat16, true, false>(p, stream, name, peers, npeers);
+    if (!a_mn && b_mn) return launch_tc2<__nv_bfloat16, false, true, PBN>(p, stream, name, peers, npeers);
+    if (!a_mn && !b_mn) return launch_tc2<__nv_bfloat16, false, false, PBN>(p, stream, name, peers, npeers);
+    if (a_mn && b_mn) return launch_tc2<__nv_bfloat16, true, true, PBN>(p, stream, name, peers, npeers);
+    return launch_tc2<__nv_bfloat16, true, false, PBN>(p, stream, name, peers, npeers);
   }
-  if (!a_mn && b_mn) return launch_tc2<__half, false, true>(p, stream, name, peers, npeers);
-  if (!a_mn && !b_mn) return launch_tc2<__half, false, false>(p, stream, name, peers, npeers);
-  if (a_mn && b_mn) return launch_tc2<__half, true, true>(p, stream, name, peers, npeers);
-  return launch_tc2<__half, true, false>(p, stream, name, peers, npeers);
+  if (!a_mn && b_mn) return launch_tc2<__half, false, true, PBN>(p, stream, name, peers, npeers);
+  if (!a_mn && !b_mn) return launch_tc2<__half, false, false, PBN>(p, stream, name, peers, npeers);
+  if (a_mn && b_mn) return launch_tc2<__half, true, true, PBN>(p, stream, name, peers, npeers);
+  return launch_tc2<__half, true, false, PBN>(p, stream, name, peers, npeers);
+}
+
+}  // namespace
+
+int gemm_tc2_pick_width(const GemmProblem& p) {
+  // 256 x 512 pair tiles when there are at least two waves of them (every
+  // pair of SMs takes two or more); below that the narrower tile's extra
+  // tiles balance the last wave better.
+  const int pairs = device_sm_count() / 2;
+  const int64_t tiles512 = ((p.M + 255) / 256) * ((p.N + 511) / 512) * p.batch;
+  return (p.N >= 512 && tiles512 >= 2 * pairs) ? 512 : 256;
+}
+
+int gemm_tc2_peers(const GemmProblem& p, void* const* peers, int npeers, cudaStream_t stream, int pbn) {
+  if (pbn == 0) pbn = gemm_tc2_pick_width(p);
+  return pbn == 512 ? launch_tc2_layout<512>(p, peers, npeers, stream)
+                    : launch_tc2_layout<256>(p, peers, npeers, stream);
 }
 
 }  // namespace cuopx

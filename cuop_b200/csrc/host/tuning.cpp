@@ -34,7 +34,7 @@ namespace {
 
 const char* const kVariantNames[kVariantCount] = {"auto",          "tc2",           "tc_128x256",
                                                   "tc_128x128",    "tf32x3_128x64", "tf32x3_128x128",
-                                                  "ffma",          "generic"};
+                                                  "ffma",          "generic",       "tc2_256x512"};
 
 struct Range {
   int64_t lo = 0, hi = INT64_MAX;

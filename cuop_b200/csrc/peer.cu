@@ -176,12 +176,15 @@ int cuopx_gemm_allgather(int dtype, int transA, int transB, int64_t M, int64_t N
   // 8 ranks (same box, same inputs), pair tiles beat the 1-SM peer paths
   // even where the exchange outlasts the GEMM (C3 8192^3: 271 us vs 285 us
   // for 128 x 256 and 305 us for 128 x 128 tiles; C5: 401 vs 428 / 450 us).
-  // A variant override (cuopx_set_gemm_variant[_thread]) selects a 1-SM path.
-  int v = select_gemm_variant(p);
-  if (v != kVariantTc128x256 && v != kVariantTc128x128) v = kVariantTc2;
+  // The pair tile width follows the block's size (256 x 512 tiles when
+  // there are two waves of them).  A variant override
+  // (cuopx_set_gemm_variant[_thread]) selects a width or a 1-SM path.
+  const int v = select_gemm_variant(p);
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (v == kVariantTc128x256) return gemm_tc_peers(p, peers, np, s, 256);
   if (v == kVariantTc128x128) return gemm_tc_peers(p, peers, np, s, 128);
+  if (v == kVariantTc2) return gemm_tc2_peers(p, peers, np, s, 256);
+  if (v == kVariantTc2x512) return gemm_tc2_peers(p, peers, np, s, 512);
   return gemm_tc2_peers(p, peers, np, s);
 }
 

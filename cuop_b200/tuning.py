@@ -27,8 +27,8 @@ _DT_NAME = {N.F32: "f32", N.F64: "f64", N.F16: "f16", N.BF16: "bf16"}
 
 # Candidate variants per element type (the table may name any of them).
 CANDIDATES = {
-    N.F16: ["tc2", "tc_128x256", "tc_128x128"],
-    N.BF16: ["tc2", "tc_128x256", "tc_128x128"],
+    N.F16: ["tc2", "tc2_256x512", "tc_128x256", "tc_128x128"],
+    N.BF16: ["tc2", "tc2_256x512", "tc_128x256", "tc_128x128"],
     N.F32: ["tf32x3_128x64", "tf32x3_128x128", "ffma"],
 }
 
@@ -118,7 +118,7 @@ def time_variant(variant: str, A, B, C, batch: int, launches: int = 10) -> Optio
 
 
 def _kernel_matches(variant: str, kernel: str) -> bool:
-    expect = {"tc2": "gemm_tc2_", "tc_128x256": "gemm_tc_128x256", "tc_128x128": "gemm_tc_128x128",
+    expect = {"tc2": "gemm_tc2_256x256", "tc2_256x512": "gemm_tc2_256x512", "tc_128x256": "gemm_tc_128x256", "tc_128x128": "gemm_tc_128x128",
               "tf32x3_128x64": "gemm_tf32x3_128x64", "tf32x3_128x128": "gemm_tf32x3_128x128",
               "ffma": "gemm_f32_", "generic": "gemm_simt_generic"}[variant]
     return kernel.startswith(expect)

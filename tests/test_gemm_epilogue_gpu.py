@@ -81,14 +81,15 @@ def test_f64_epilogue_bit_exact(dev):
 
 @pytest.mark.parametrize("dt", [O.F16, O.BF16])
 @pytest.mark.parametrize("bias,relu", EPIS)
-@pytest.mark.parametrize("M,N,K,kernel", [(320, 200, 256, "gemm_tc_"), (4096, 2560, 512, "gemm_tc2_")])
+@pytest.mark.parametrize("M,N,K,kernel", [(320, 200, 256, "gemm_tc_"), (4096, 2560, 512, "gemm_tc2_256x256"),
+                                           (4096, 2600, 512, "gemm_tc2_256x512")])
 def test_lowp_epilogue_vs_oracle(dev, dt, M, N, K, kernel, bias, relu):
     A = O.to_lowp(O.normal((M, K), seed=M) / np.sqrt(K), dt)
     B = O.to_lowp(O.normal((K, N), seed=N), dt)
     b = O.to_lowp(O.normal(N, seed=K), dt) if bias else None
     C0 = O.to_lowp(O.normal((M, N), seed=11), dt)
     Cd = to_dev_lowp(C0, dt, dev)
-    with forced_variant("tc2" if kernel == "gemm_tc2_" else None):
+    with forced_variant({"gemm_tc2_256x256": "tc2", "gemm_tc2_256x512": "tc2_256x512"}.get(kernel)):
         cx.gemm(to_dev_lowp(A, dt, dev), to_dev_lowp(B, dt, dev), Cd, alpha=1.25, beta=0.5,
                 bias=None if b is None else to_dev_lowp(b, dt, dev), relu=relu)
     assert cx.last_kernel().startswith(kernel), cx.last_kernel()

@@ -170,16 +170,17 @@ PAIR_CASES = [  # the two-SM (cta_group::2) kernel, forced (ragged and transpose
 ]
 
 
+@pytest.mark.parametrize("variant,kernel", [("tc2", "gemm_tc2_256x256"), ("tc2_256x512", "gemm_tc2_256x512")])
 @pytest.mark.parametrize("dt", [O.F16, O.BF16])
 @pytest.mark.parametrize("M,N,K,tA,tB", PAIR_CASES)
-def test_lowp_pair_kernel_vs_oracle(dev, dt, M, N, K, tA, tB):
+def test_lowp_pair_kernel_vs_oracle(dev, dt, M, N, K, tA, tB, variant, kernel):
     A = O.to_lowp(O.normal((K, M) if tA else (M, K), seed=M + 11) / np.sqrt(K), dt)
     B = O.to_lowp(O.normal((N, K) if tB else (K, N), seed=N + 13), dt)
     C0 = O.to_lowp(O.normal((M, N), seed=17), dt)
     Cd = to_dev_lowp(C0, dt, dev)
-    with forced_variant("tc2"):
+    with forced_variant(variant):
         cx.gemm(to_dev_lowp(A, dt, dev), to_dev_lowp(B, dt, dev), Cd, transA=tA, transB=tB, alpha=1.5, beta=0.5)
-    assert cx.last_kernel() == "gemm_tc2_256x256", cx.last_kernel()
+    assert cx.last_kernel() == kernel, cx.last_kernel()
     full = 1.5 * fp32_reference_gpu(to_dev_lowp(A, dt, dev), to_dev_lowp(B, dt, dev), tA, tB) + \
         0.5 * to_dev_lowp(C0, dt, dev).float()
     assert O.max_relative(Cd.float().cpu().numpy(), full.cpu().numpy()) <= LOWP_TOL
@@ -187,6 +188,25 @@ def test_lowp_pair_kernel_vs_oracle(dev, dt, M, N, K, tA, tB):
     ref = O.gemm_lowp(dt, A[:, rows] if tA else A[rows], B, C0[rows], transA=tA, transB=tB, alpha=1.5, beta=0.5)
     got = O.from_lowp(lowp_bits(Cd[torch.as_tensor(rows, device=dev)]), dt)
     assert O.max_relative(got, O.from_lowp(ref, dt)) <= LOWP_TOL
+
+
+@pytest.mark.parametrize("M,N,K,kernel", [(8192, 8192, 4096, "gemm_tc2_256x512"), (8192, 1024, 8192, "gemm_tc2_256x256"),
+                                           (4096, 28672, 8192, "gemm_tc2_256x512")])
+def test_pair_tile_width_follows_size(dev, M, N, K, kernel):
+    """Built-in choice: 256 x 512 pair tiles when there are two waves of them,
+    else 256 x 256; both agree with an fp32 reference on sampled rows and
+    columns."""
+    g = torch.Generator(device=dev).manual_seed(M + N + K)
+    A = (torch.randn(M, K, device=dev, generator=g) / np.sqrt(K)).bfloat16()
+    B = torch.randn(K, N, device=dev, generator=g).bfloat16()
+    C = cx.gemm(A, B)
+    assert cx.last_kernel() == kernel, cx.last_kernel()
+    rows = torch.tensor([0, 1, 255, 256, 511, 4095, M - 1], device=dev)
+    ref = A[rows].float() @ B.float()
+    assert O.max_relative(C[rows].float().cpu().numpy(), ref.cpu().numpy()) <= LOWP_TOL
+    cols = torch.tensor([0, 255, 256, 511, 512, N - 1], device=dev)
+    ref_c = A.float() @ B[:, cols].float()
+    assert O.max_relative(C[:, cols].float().cpu().numpy(), ref_c.cpu().numpy()) <= LOWP_TOL
 
 
 @pytest.mark.parametrize("dt", [O.F16, O.BF16])
@@ -243,7 +263,7 @@ def test_c3_fp16_8192_full(dev):
     B16 = O.to_lowp(O.normal((n, n), seed=1) / np.sqrt(n), dt)
     A, B = to_dev_lowp(A16, dt, dev), to_dev_lowp(B16, dt, dev)
     C = cx.gemm(A, B)
-    assert cx.last_kernel() == "gemm_tc2_256x256"
+    assert cx.last_kernel() == "gemm_tc2_256x512"
     full = fp32_reference_gpu(A, B)
     assert O.max_relative(C.float().cpu().numpy(), full.cpu().numpy()) <= LOWP_TOL
     rng = np.random.default_rng(0)

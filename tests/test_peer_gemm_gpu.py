@@ -43,7 +43,8 @@ CASES = [  # (world, M, nb, K, tA, tB)
 ]
 
 
-PATHS = [("tc2", "gemm_tc2_256x256"), ("tc_128x128", "gemm_tc_128x128"), ("tc_128x256", "gemm_tc_128x256")]
+PATHS = [("tc2", "gemm_tc2_256x256"), ("tc2_256x512", "gemm_tc2_256x512"), ("tc_128x128", "gemm_tc_128x128"),
+         ("tc_128x256", "gemm_tc_128x256")]
 
 
 @pytest.mark.parametrize("variant,kernel", PATHS)
@@ -61,7 +62,7 @@ def test_allgather_every_rank_gets_every_block(dev, dt, world, M, nb, K, tA, tB,
             assert _call(dt, M, nb, K, Ad, Wb, outs, r, tA, tB, alpha=1.25) == 0
         # The 1-SM peer path is compiled for the row-major layout only;
         # transposed operands take the 2-SM kernel's peer path.
-        expect = kernel if not (tA or tB) else "gemm_tc2_256x256"
+        expect = kernel if not (tA or tB) or kernel.startswith("gemm_tc2") else "gemm_tc2_256x256"
         assert cx.last_kernel() == expect + ("_peer" if world > 1 else "")
     torch.cuda.synchronize()
     for o in outs[1:]:  # every rank's copy is the same bits

@@ -71,7 +71,8 @@ def test_fp32_mode_wins_over_table(dev, table, fp32_ffma):
     assert np.array_equal(C.cpu().numpy(), O.gemm_f32(A32, B32))  # still the bit-exact FFMA chain
 
 
-@pytest.mark.parametrize("variant,kernel", [("tc2", "gemm_tc2_256x256"), ("tc_128x256", "gemm_tc_128x256"),
+@pytest.mark.parametrize("variant,kernel", [("tc2", "gemm_tc2_256x256"), ("tc2_256x512", "gemm_tc2_256x512"),
+                                            ("tc_128x256", "gemm_tc_128x256"),
                                             ("tc_128x128", "gemm_tc_128x128"), ("generic", "gemm_simt_generic")])
 def test_forced_variant_runs_and_agrees(dev, table, variant, kernel):
     dt = O.F16
