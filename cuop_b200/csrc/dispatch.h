@@ -63,7 +63,7 @@ int gemm_tc_peers(const GemmProblem& p, void* const* peers, int npeers, cudaStre
 // Two-SM (cta_group::2) tcgen05 back-end (gemm_tc2.cu) for large fp16/bf16.
 bool gemm_tc2_wanted(const GemmProblem& p);
 // pbn: pair tile width, 256 or 512; 0 = choose (gemm_tc2_pick_width).
-int gemm_tc2_pick_width(const GemmProblem& p);
+int gemm_tc2_pick_width(const GemmProblem& p, bool peers);
 int gemm_tc2(const GemmProblem& p, cudaStream_t stream, int pbn = 0);
 // Same kernel; every output chunk is also stored to peers[0..npeers) (peer
 // mappings of identically laid out outputs, offset to this block's columns).

@@ -683,13 +683,19 @@ int launch_tc2(const GemmProblem& p, cudaStream_t stream, const char* name, void
 
 bool gemm_tc2_wanted(const GemmProblem& p) {
   // Pair tiles halve shared-memory operand traffic per FLOP, which pays off
-  // over long K loops (measured on B200: from K ~ 8192 with at least 64 pair
-  // tiles, or from K = 4096 on very large outputs); shorter K loops are
-  // faster on the 1-SM 128 x 256 tile, whose epilogue overlaps better.
+  // over long K loops.  Measured on B200 against the 1-SM 128 x 256 kernel:
+  // 256 x 512 pair tiles win from K = 4096 once there are about as many of
+  // them as SM pairs (e.g. 1024 x 8192 x 4096: 50.7 vs 53.7 us), 256 x 256
+  // pair tiles from K ~ 8192 with 64 tiles; at K = 1024 the 1-SM kernel,
+  // whose epilogue overlaps better, is faster.
   if (!gemm_tc_supported(p)) return false;
   if (p.M < 256 || p.N < 256 || p.K < 256) return false;
-  const int64_t tiles = ((p.M + 255) / 256) * ((p.N + 255) / 256) * p.batch;
-  return (p.K >= 6144 && tiles >= 64) || (p.K >= 4096 && tiles >= 512);
+  const int64_t rows = (p.M + 255) / 256;
+  const int64_t tiles256 = rows * ((p.N + 255) / 256) * p.batch;
+  const int64_t tiles512 = rows * ((p.N + 511) / 512) * p.batch;
+  const int pairs = device_sm_count() / 2;
+  return (p.K >= 4096 && p.N >= 512 && tiles512 >= (pairs * 3) / 4) || (p.K >= 6144 && tiles256 >= 64) ||
+         (p.K >= 4096 && tiles256 >= 512);
 }
 
 int gemm_tc2(const GemmProblem& p, cudaStream_t stream, int pbn) { return gemm_tc2_peers(p, nullptr, 0, stream, pbn); }
@@ -715,17 +721,25 @@ int launch_tc2_layout(const GemmProblem& p, void* const* peers, int npeers, cuda
 
 }  // namespace
 
-int gemm_tc2_pick_width(const GemmProblem& p) {
-  // 256 x 512 pair tiles when there are at least two waves of them (every
-  // pair of SMs takes two or more); below that the narrower tile's extra
-  // tiles balance the last wave better.
-  const int pairs = device_sm_count() / 2;
-  const int64_t tiles512 = ((p.M + 255) / 256) * ((p.N + 511) / 512) * p.batch;
-  return (p.N >= 512 && tiles512 >= 2 * pairs) ? 512 : 256;
+int gemm_tc2_pick_width(const GemmProblem& p, bool peers) {
+  if (p.N < 512) return 256;
+  const int64_t pairs = device_sm_count() / 2;
+  const int64_t rows = (p.M + 255) / 256;
+  const int64_t tiles256 = rows * ((p.N + 255) / 256) * p.batch;
+  const int64_t tiles512 = rows * ((p.N + 511) / 512) * p.batch;
+  // With peer stores, the epilogue of a wave overlaps the next wave's
+  // MMAs only when there is a next wave: 256 x 512 tiles from two waves.
+  if (peers) return tiles512 >= 2 * pairs ? 512 : 256;
+  // Otherwise by waves of pair tiles: a 256 x 512 tile takes twice as long
+  // as a 256 x 256 one less ~5 % (fewer operand bytes from L2, measured),
+  // so it wins when 2 * 0.95 * waves512 <= waves256.
+  const int64_t w256 = (tiles256 + pairs - 1) / pairs;
+  const int64_t w512 = (tiles512 + pairs - 1) / pairs;
+  return 2 * w512 * 19 <= w256 * 20 ? 512 : 256;
 }
 
 int gemm_tc2_peers(const GemmProblem& p, void* const* peers, int npeers, cudaStream_t stream, int pbn) {
-  if (pbn == 0) pbn = gemm_tc2_pick_width(p);
+  if (pbn == 0) pbn = gemm_tc2_pick_width(p, npeers > 0);
   return pbn == 512 ? launch_tc2_layout<512>(p, peers, npeers, stream)
                     : launch_tc2_layout<256>(p, peers, npeers, stream);
 }

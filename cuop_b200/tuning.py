@@ -102,9 +102,17 @@ def time_variant(variant: str, A, B, C, batch: int, launches: int = 10) -> Optio
         with torch.cuda.graph(g):
             for _ in range(launches):
                 run()
-        g.replay()
-        torch.cuda.synchronize()
+        # Warm-up of at least ~20 ms of device work, so that the clock has
+        # settled before the timed replays whatever ran before.
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        one = max(e0.elapsed_time(e1), 1e-3)
+        for _ in range(min(200, int(20.0 / one))):
+            g.replay()
+        torch.cuda.synchronize()
         ts = []
         for _ in range(3):
             e0.record()
@@ -128,6 +136,7 @@ def sweep(dtypes: Iterable[int] = (N.F16, N.BF16, N.F32), cap: int = 8192, log=p
     """Time the built-in choice and every candidate on the sweep grid; returns
     table lines (rules only where a candidate wins by more than MARGIN)."""
     import torch
+    from . import ops
 
     dev = torch.device("cuda", torch.cuda.current_device())
     tdt = {N.F16: torch.float16, N.BF16: torch.bfloat16, N.F32: torch.float32}
@@ -143,13 +152,18 @@ def sweep(dtypes: Iterable[int] = (N.F16, N.BF16, N.F32), cap: int = 8192, log=p
             B = torch.randn(*((batch, K, Nn) if batch > 1 else (K, Nn)), device=dev).to(tdt[dt])
             C = torch.empty(*((batch, M, Nn) if batch > 1 else (M, Nn)), device=dev, dtype=tdt[dt])
             t_auto = time_variant("auto", A, B, C, batch)
+            auto_kernel = ops.last_kernel()
             times = {v: t for v in CANDIDATES[dt] if (t := time_variant(v, A, B, C, batch)) is not None}
+            # The built-in choice again after the candidates: the better of
+            # its two times, so a clock change across the candidates does
+            # not turn into a rule.
+            t_auto = min(t_auto, time_variant("auto", A, B, C, batch))
             del A, B, C
             if not times:
                 continue
             best = min(times, key=times.get)
-            desc = f"{M}x{Nn}x{K} batch {batch}: built-in {t_auto:.4f}, {best} {times[best]:.4f}"
-            if times[best] < (1.0 - MARGIN) * t_auto:
+            desc = f"{M}x{Nn}x{K} batch {batch}: built-in {t_auto:.4f} ({auto_kernel}), {best} {times[best]:.4f}"
+            if times[best] < (1.0 - MARGIN) * t_auto and not _kernel_matches(best, auto_kernel):
                 bat = "1:1" if batch == 1 else "2:"
                 lines.append(f"{_DT_NAME[dt]} 0 0 {_around(M)} {_around(Nn)} {_around(K)} {bat} {best}   # {desc}")
                 log(lines[-1])
