@@ -14,10 +14,11 @@
 //               "hi" buffers of a STAGES-deep ring: 128-byte swizzle for
 //               K-major operands, 128-byte swizzle with 32-byte atoms for
 //               MN-major ones (the only MN-major layout tf32 MMAs accept).
-//   warps 6..13 converters: wait for a landed stage; split K-major A straight
-//               into TMEM (tcgen05.st, one tile row per thread, the MMAs read
-//               A from TMEM), split B (and an MN-major A) in place in shared
-//               memory with lo next to it (same swizzled layout: the split is
+//   warps 6..13 converters, two groups of 4 taking alternate K blocks: wait
+//               for a landed stage; split K-major A straight into TMEM
+//               (tcgen05.st, one tile row per thread, the MMAs read A from
+//               TMEM), split B (and an MN-major A) in place in shared memory
+//               with lo next to it (same swizzled layout: the split is
 //               elementwise); fence, signal the MMA warp.
 //   warp 1      TMEM allocator + MMA issuer: 3 x (BK/8) MMAs (M=128, N=BN,
 //               K=8) per stage, commit frees the stage / hands off the tile.
@@ -35,6 +36,12 @@ constexpr int X3_BK = 32;  // 32 fp32 = 128 bytes = one swizzle row
 constexpr int X3_THREADS = 448;
 constexpr int X3_EPI_WARPS = 4;
 constexpr int X3_CONV_WARPS = 8;
+// Converter groups: group g splits the K blocks whose sequence number is g
+// modulo the group count, so consecutive stages are split concurrently (the
+// split of one stage ends in a TMEM-store wait, which one group alone would
+// serialise).
+constexpr int X3_CONV_GROUPS = 2;
+constexpr int X3_CONV_PER_GROUP = X3_CONV_WARPS / X3_CONV_GROUPS;
 constexpr int X3_CHUNK = 32;  // epilogue columns per TMA store (32 fp32 = 128 bytes)
 
 struct X3Params {
@@ -150,7 +157,7 @@ __global__ void __launch_bounds__(X3_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&conv[s], X3_CONV_WARPS);
+      mbar_init(&conv[s], X3_CONV_PER_GROUP);
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -234,48 +241,60 @@ __global__ void __launch_bounds__(X3_THREADS, 1)
     }
   } else if (warp >= 6) {
     // ------------------------------------------------------------ converters
-    const int ctid = threadIdx.x - 6 * 32;
+    constexpr int W = X3_CONV_PER_GROUP;
+    constexpr int CPW = X3_BK * 4 / W;  // A columns per warp (TMEM split): 32 or 16
+    const int cw = warp - 6;
+    const int grp = cw / W;
+    const int gtid = threadIdx.x - (6 + grp * W) * 32;  // thread index within the group
     int stage = 0;
     uint32_t phase = 0;
+    int seq = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
-      for (int kb = 0; kb < p.k_blocks; ++kb) {
-        if (!mbar_wait_bounded(&full[stage], phase, kDevErrWaitTimeoutFull, abort_flag)) {
-          ok = false;
-          break;
-        }
-        if constexpr (A_TMEM) {
-          // This warp owns TMEM lane quarter q (tile rows 32q..32q+31) and
-          // K columns 16h..16h+15 of the stage; each thread splits its row.
-          const int q = warp & 3;
-          const int h = (warp - 6) >> 2;
-          const int r = 32 * q + lane;
-          const unsigned char* arow = L::a_hi(smem, stage) + r * 128;  // 128-byte swizzled row
-          uint32_t hi[16], lo[16];
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const float4 v = *reinterpret_cast<const float4*>(arow + (((4 * h + c) ^ (r & 7)) << 4));
-            const float e[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              hi[4 * c + i] = to_tf32_rna(e[i]);
-              lo[4 * c + i] = __float_as_uint(__fsub_rn(e[i], __uint_as_float(hi[4 * c + i])));
-            }
+      for (int kb = 0; kb < p.k_blocks; ++kb, ++seq) {
+        if (seq % X3_CONV_GROUPS == grp) {
+          if (!mbar_wait_bounded(&full[stage], phase, kDevErrWaitTimeoutFull, abort_flag)) {
+            ok = false;
+            break;
           }
-          const uint32_t tcol = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + A_COL0 +
-                                static_cast<uint32_t>(stage * 2 * X3_BK + 16 * h);
-          tmem_st_32x32b_x16(tcol, hi);
-          tmem_st_32x32b_x16(tcol + X3_BK, lo);
-          split_tf32<L::B_BYTES, X3_CONV_WARPS * 32>(L::b_hi(smem, stage), L::b_lo(smem, stage), ctid);
-          tmem_wait_st();
-          tc_fence_before_sync();
-        } else {
-          split_tf32<L::A_BYTES, X3_CONV_WARPS * 32>(L::a_hi(smem, stage), L::a_lo(smem, stage), ctid);
-          split_tf32<L::B_BYTES, X3_CONV_WARPS * 32>(L::b_hi(smem, stage), L::b_lo(smem, stage), ctid);
+          if constexpr (A_TMEM) {
+            // This warp owns TMEM lane quarter q (tile rows 32q..32q+31) and
+            // K columns CPW*h..CPW*h+CPW-1 of the stage; each thread splits
+            // its row.
+            const int q = warp & 3;
+            const int h = (cw % W) >> 2;
+            const int r = 32 * q + lane;
+            const unsigned char* arow = L::a_hi(smem, stage) + r * 128;  // 128-byte swizzled row
+            uint32_t hi[CPW / 16][16], lo[CPW / 16][16];
+#pragma unroll
+            for (int c = 0; c < CPW / 4; ++c) {
+              const float4 v = *reinterpret_cast<const float4*>(arow + ((((CPW / 4) * h + c) ^ (r & 7)) << 4));
+              const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int j = 4 * c + i;
+                hi[j / 16][j % 16] = to_tf32_rna(e[i]);
+                lo[j / 16][j % 16] = __float_as_uint(__fsub_rn(e[i], __uint_as_float(hi[j / 16][j % 16])));
+              }
+            }
+            const uint32_t tcol = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + A_COL0 +
+                                  static_cast<uint32_t>(stage * 2 * X3_BK + CPW * h);
+#pragma unroll
+            for (int u = 0; u < CPW / 16; ++u) {
+              tmem_st_32x32b_x16(tcol + 16 * u, hi[u]);
+              tmem_st_32x32b_x16(tcol + X3_BK + 16 * u, lo[u]);
+            }
+            split_tf32<L::B_BYTES, W * 32>(L::b_hi(smem, stage), L::b_lo(smem, stage), gtid);
+            tmem_wait_st();
+            tc_fence_before_sync();
+          } else {
+            split_tf32<L::A_BYTES, W * 32>(L::a_hi(smem, stage), L::a_lo(smem, stage), gtid);
+            split_tf32<L::B_BYTES, W * 32>(L::b_hi(smem, stage), L::b_lo(smem, stage), gtid);
+          }
+          fence_proxy_async_shared();  // generic-proxy writes -> visible to the tensor cores
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&conv[stage]);
         }
-        fence_proxy_async_shared();  // generic-proxy writes -> visible to the tensor cores
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&conv[stage]);
         if (++stage == STAGES) stage = 0, phase ^= 1u;
       }
     }
