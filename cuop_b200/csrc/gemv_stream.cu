@@ -41,6 +41,18 @@ constexpr int GS_T_WAVES = 1;    // gemv_t_lsu CTAs per resident slot
 // they take 64 registers (16 for fp32 / fp64, 8 for 16-bit types).
 constexpr int GS_T_RED_REGS = 64;
 
+// Rows of A each CTA asks L2 to fetch before waiting for the previous kernel
+// on the stream (programmatic dependent launch): the launch then starts on
+// L2 hits while the previous grid's last CTAs still drain.  A prefetch only
+// warms L2, the device's point of coherence, so it cannot return data from
+// before the previous kernel's writes.
+constexpr int GS_N_PREFETCH_ROWS = 2;  // gemv_n_xreg: first rows of the CTA's block
+constexpr bool GS_T_PREFETCH = true;   // gemv_t_lsu: first batch of each thread's rows
+
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 __device__ __forceinline__ uint4 ld_nc16(const void* p) {
   uint4 v;
   asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -75,6 +87,14 @@ __global__ void __launch_bounds__(GS_THREADS, 2)
   const int64_t nvec = N / V;
   const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_cta;
   const int64_t r1 = min(M, r0 + rows_per_cta);
+  if ((lane & 7) == 0) {  // one request per 128-byte line of the warp's slice
+    for (int64_t r = r0; r < min(r1, r0 + GS_N_PREFETCH_ROWS); ++r) {
+      const uint4* a = reinterpret_cast<const uint4*>(A + r * lda) + static_cast<int64_t>(warp) * 32 * KV + lane;
+#pragma unroll
+      for (int k = 0; k < KV; ++k)
+        if (static_cast<int64_t>(warp) * 32 * KV + k * 32 + lane < nvec) prefetch_l2(a + k * 32);
+    }
+  }
   // The next kernel may start launching once every CTA of this grid has
   // started (its CTAs then take slots freed by exiting CTAs and wait for
   // this grid's completion before touching memory).
@@ -178,6 +198,11 @@ __global__ void __launch_bounds__(GS_THREADS, 2)
   const int64_t j0 = static_cast<int64_t>(blockIdx.y) * rows_per_split;
   const int64_t j1 = min(N, j0 + rows_per_split);
   const unsigned int splits = gridDim.y;
+  if (GS_T_PREFETCH && has && (tid & 7) == 0) {  // one request per 128-byte line
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (j0 + ph + u * P < j1) prefetch_l2(A + col + (j0 + ph + u * P) * lda);
+  }
   grid_dependency_wait();
   grid_launch_dependents();
 
