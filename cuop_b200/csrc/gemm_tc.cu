@@ -48,6 +48,7 @@ constexpr int EPI_WARPS = 4;
 constexpr int STAGE_CHUNK_COLS = 64;  // epilogue column chunk (one TMA store box)
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int GROUP_M = 16;  // raster: walk 16 M-tiles per N step for L2 reuse
+constexpr bool TC_PREFETCH_FIRST_TILE = true;
 // Scheduler ring depth: more than the producer's lead over the epilogue
 // (STAGES + accumulator buffers, in tiles), so the producer never waits on it.
 constexpr int CLC_SLOTS = 16;
@@ -173,6 +174,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
     prefetch_tmap(&tmC);
+    if (TC_PREFETCH_FIRST_TILE) {
+      // L2 prefetch of this CTA's first tile (up to STAGES K blocks) while
+      // the previous kernel on the stream may still be draining; it only
+      // warms L2, the loads stay after the dependent-launch wait.
+      int b, mt, nt;
+      tile_coords(blockIdx.x, p, b, mt, nt);
+      const int m0 = mt * BM, n0 = nt * BN;
+      for (int kb = 0; kb < min(p.k_blocks, STAGES); ++kb) {
+        const int k0 = kb * BK;
+        if constexpr (A_MN) {
+#pragma unroll
+          for (int j = 0; j < BM / 64; ++j) tma_prefetch_3d(&tmA, m0 + 64 * j, k0, b);
+        } else {
+          tma_prefetch_3d(&tmA, k0, m0, b);
+        }
+        if constexpr (B_MN) {
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j) tma_prefetch_3d(&tmB, n0 + 64 * j, k0, b);
+        } else {
+          tma_prefetch_3d(&tmB, k0, n0, b);
+        }
+      }
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, TMEM_COLS);
