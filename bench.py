@@ -42,7 +42,7 @@ FP32_SIMT_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
 
 # DRAM bytes per launch from the ncu capture summarised in
 # profiles/gemv_f32_8192_ncu.md (dram__bytes_read.sum + dram__bytes_write.sum).
-NCU_TRAFFIC_BYTES = {"gemv_t_lsu": 271750656, "gemv_n_xreg": 271830016}
+NCU_TRAFFIC_BYTES = {"gemv_t_lsu": 272088832, "gemv_n_xreg": 272280576}
 
 
 # --------------------------------------------------------------------------- util
