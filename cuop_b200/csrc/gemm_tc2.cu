@@ -727,9 +727,11 @@ int gemm_tc2_pick_width(const GemmProblem& p, bool peers) {
   const int64_t rows = (p.M + 255) / 256;
   const int64_t tiles256 = rows * ((p.N + 255) / 256) * p.batch;
   const int64_t tiles512 = rows * ((p.N + 511) / 512) * p.batch;
-  // With peer stores, the epilogue of a wave overlaps the next wave's
-  // MMAs only when there is a next wave: 256 x 512 tiles from two waves.
-  if (peers) return tiles512 >= 2 * pairs ? 512 : 256;
+  // With peer stores the epilogue of a tile is several times longer, and
+  // only the double-buffered 256 x 256 tiles overlap it with the next
+  // tile's MMAs (measured on 2 B200s, C3 8192^3 column-sharded: 0.419 ms
+  // with 256 x 256 tiles, 0.494 ms with 256 x 512 tiles).
+  if (peers) return 256;
   // Otherwise by waves of pair tiles: a 256 x 512 tile takes twice as long
   // as a 256 x 256 one less ~5 % (fewer operand bytes from L2, measured),
   // so it wins when 2 * 0.95 * waves512 <= waves256.
