@@ -1,8 +1,12 @@
 /*
  * cuopx.h — C ABI of the B200 (sm_100a) dense BLAS hot path.
  *
- * Plain pointers and sizes only: every matrix/vector argument is a DEVICE
- * pointer, every size is int64_t, every call is asynchronous on the given
+ * Plain pointers and sizes only: every matrix/vector argument is a pointer
+ * the GPU can dereference — device memory, or pinned (page-locked) host
+ * memory, which the kernels reach through unified addressing (a GEMV's y
+ * or one side of cuopx_copy, for instance); pageable host memory is not
+ * checked for and must not be passed.  Every size is int64_t, every call is
+ * asynchronous on the given
  * cudaStream_t (passed as void*, NULL = legacy default stream) and returns
  * a cuOP StatusCode integer (same numeric values as the reference's
  * `enum class StatusCode`, include/util/status_code.hpp:28-161).  No compute
