@@ -224,16 +224,17 @@ int cuopx_gemm_ex(int dtype, int transA, int transB, int64_t M, int64_t N, int64
                   int64_t lda, const void* B, int64_t ldb, double beta, void* C, int64_t ldc, const void* bias,
                   int epilogue, void* stream) {
   ApiScope scope("cuopx_gemm_ex", M, N, K);
-  if (epilogue < 0 || epilogue > (CUOPX_EPI_BIAS | CUOPX_EPI_RELU)) return CUOPX_INVALID_ARGUMENT;
-  if ((epilogue & CUOPX_EPI_BIAS) && bias == nullptr && M > 0 && N > 0) return CUOPX_INVALID_ARGUMENT;
+  if (epilogue < 0 || epilogue > (CUOPX_EPI_BIAS | CUOPX_EPI_RELU)) return scope.done(CUOPX_INVALID_ARGUMENT);
+  if ((epilogue & CUOPX_EPI_BIAS) && bias == nullptr && M > 0 && N > 0) return scope.done(CUOPX_INVALID_ARGUMENT);
   GemmProblem p{dtype, transA != 0, transB != 0, M, N, K, alpha, beta, A, lda, 0, B, ldb, 0, C, ldc, 0, 1};
   p.bias = (epilogue & CUOPX_EPI_BIAS) ? bias : nullptr;
   p.epi = epilogue;
   const int v = validate_gemm(p);
-  if (v >= 0) return v;
+  if (v >= 0) return scope.done(v);
   if (epilogue & CUOPX_EPI_BIAS) {
     const size_t es = dtype_size(dtype);
-    if (overlaps(C, span_bytes(M, N, ldc, es), bias, static_cast<size_t>(N) * es)) return CUOPX_INVALID_ARGUMENT;
+    if (overlaps(C, span_bytes(M, N, ldc, es), bias, static_cast<size_t>(N) * es))
+      return scope.done(CUOPX_INVALID_ARGUMENT);
   }
   return scope.done(gemm_route(p, static_cast<cudaStream_t>(stream)));
 }
@@ -258,16 +259,16 @@ size_t cuopx_gemv_workspace_size(int dtype, int trans, int64_t M, int64_t N) {
 int cuopx_gemv(int dtype, int trans, int64_t M, int64_t N, double alpha, const void* A, int64_t lda, const void* x,
                double beta, void* y, void* workspace, size_t workspace_bytes, void* stream) {
   ApiScope scope("cuopx_gemv", M, N, trans);
-  if (dtype_size(dtype) == 0) return CUOPX_UNSUPPORTED_TYPE;
-  if (M < 0 || N < 0) return CUOPX_INVALID_ARGUMENT;
-  if (M == 0) return CUOPX_SUCCESS;
-  if (y == nullptr) return CUOPX_INVALID_ARGUMENT;
+  if (dtype_size(dtype) == 0) return scope.done(CUOPX_UNSUPPORTED_TYPE);
+  if (M < 0 || N < 0) return scope.done(CUOPX_INVALID_ARGUMENT);
+  if (M == 0) return scope.done(CUOPX_SUCCESS);
+  if (y == nullptr) return scope.done(CUOPX_INVALID_ARGUMENT);
   if (N > 0) {
-    if (A == nullptr || x == nullptr) return CUOPX_INVALID_ARGUMENT;
-    if (lda < (trans ? M : N)) return CUOPX_INVALID_ARGUMENT;
+    if (A == nullptr || x == nullptr) return scope.done(CUOPX_INVALID_ARGUMENT);
+    if (lda < (trans ? M : N)) return scope.done(CUOPX_INVALID_ARGUMENT);
     const size_t es = dtype_size(dtype);
     const size_t a_span = trans ? span_bytes(N, M, lda, es) : span_bytes(M, N, lda, es);
-    if (overlaps(y, M * es, A, a_span) || overlaps(y, M * es, x, N * es)) return CUOPX_INVALID_ARGUMENT;
+    if (overlaps(y, M * es, A, a_span) || overlaps(y, M * es, x, N * es)) return scope.done(CUOPX_INVALID_ARGUMENT);
   }
   return scope.done(gemv_dispatch(dtype, trans, M, N, alpha, A, lda, x, beta, y, workspace, workspace_bytes,
                                   static_cast<cudaStream_t>(stream)));

@@ -138,12 +138,17 @@ def test_call_log_is_opt_in():
     import subprocess
     import sys
 
-    code = ("import sys; sys.path.insert(0, %r); from cuop_b200 import _native as N; "
-            "print(N.lib().cuopx_gemm(0, 0, 0, -1, 4, 4, 1.0, 16, 4, 16, 4, 0.0, 16, 4, None))" % str(ROOT))
+    code = ("import sys; sys.path.insert(0, %r); from cuop_b200 import _native as N; L = N.lib(); "
+            "print(L.cuopx_gemm(0, 0, 0, -1, 4, 4, 1.0, 16, 4, 16, 4, 0.0, 16, 4, None), "
+            "L.cuopx_gemv(0, 0, 4, 8, 1.0, 4096, 4, 8192, 0.0, 16384, None, 0, None), "
+            "L.cuopx_gemm_ex(0, 0, 0, 4, 4, 4, 1.0, 16, 4, 16, 4, 0.0, 64, 4, None, 1, None))" % str(ROOT))
     on = subprocess.run([sys.executable, "-c", code], env={**__import__("os").environ, "CUOPX_LOG": "1"},
                         capture_output=True, text=True, timeout=120)
-    assert on.returncode == 0 and on.stdout.strip() == str(N.INVALID_ARGUMENT)
-    assert "cuopx: cuopx_gemm -1 x 4 x 4" in on.stderr and "status 4001" in on.stderr
+    assert on.returncode == 0 and on.stdout.split() == [str(N.INVALID_ARGUMENT)] * 3
+    lines = [ln for ln in on.stderr.splitlines() if ln.startswith("cuopx: ")]
+    assert len(lines) == 3 and all(ln.endswith("status 4001") for ln in lines), on.stderr
+    assert lines[0].startswith("cuopx: cuopx_gemm -1 x 4 x 4")
+    assert lines[1].startswith("cuopx: cuopx_gemv 4 x 8") and lines[2].startswith("cuopx: cuopx_gemm_ex 4 x 4 x 4")
     env = {k: v for k, v in __import__("os").environ.items() if k != "CUOPX_LOG"}
     off = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=120)
     assert off.returncode == 0 and "cuopx:" not in off.stderr
