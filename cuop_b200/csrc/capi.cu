@@ -15,7 +15,7 @@ namespace cuopx {
 namespace {
 thread_local const char* t_last_kernel = "none";
 std::atomic<int64_t> g_launches{0};
-int g_sm_count[64] = {0};
+std::atomic<int> g_sm_count[64] = {};
 
 bool overlaps(const void* a, size_t abytes, const void* b, size_t bbytes) {
   if (!a || !b || abytes == 0 || bbytes == 0) return false;
@@ -81,12 +81,12 @@ class ApiScope {
 int device_sm_count() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (g_sm_count[dev] == 0) {
-    int n = 0;
+  int n = g_sm_count[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    g_sm_count[dev] = n;
+    g_sm_count[dev].store(n, std::memory_order_relaxed);
   }
-  return g_sm_count[dev];
+  return n;
 }
 
 void note_launch(const char* name) {

@@ -568,13 +568,13 @@ int launch_tc(const GemmProblem& p, cudaStream_t stream, const char* name, void*
   for (int i = 0; i < 7; ++i) prm.peer_C[i] = i < npeers ? peers[i] : nullptr;
 
   auto kern = gemm_tc_kernel<T, BN, STAGES, A_MN, B_MN, PEERS>;
-  static bool attr_set[64] = {};  // per instantiation and device
+  static std::atomic<bool> attr_set[64] = {};  // per instantiation and device
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return CUOPX_CUDA_ERROR;
-  if (!attr_set[dev]) {
+  if (!attr_set[dev].load(std::memory_order_relaxed)) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) != cudaSuccess)
       return CUOPX_CUDA_ERROR;
-    attr_set[dev] = true;
+    attr_set[dev].store(true, std::memory_order_relaxed);
   }
   // One CTA per tile; running CTAs take over unlaunched ones' tiles.  The
   // launch may overlap the previous kernel's tail (programmatic dependent

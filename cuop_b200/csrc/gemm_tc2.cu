@@ -661,13 +661,13 @@ int launch_tc2(const GemmProblem& p, cudaStream_t stream, const char* name, void
   prm.npeers = npeers;
   for (int i = 0; i < P_MAX_PEERS; ++i) prm.peer_C[i] = i < npeers ? peers[i] : nullptr;
   auto kern = gemm_tc2_kernel<T, A_MN, B_MN, PBN>;
-  static bool attr_set[64] = {};
+  static std::atomic<bool> attr_set[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return CUOPX_CUDA_ERROR;
-  if (!attr_set[dev]) {
+  if (!attr_set[dev].load(std::memory_order_relaxed)) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) != cudaSuccess)
       return CUOPX_CUDA_ERROR;
-    attr_set[dev] = true;
+    attr_set[dev].store(true, std::memory_order_relaxed);
   }
   // One cluster per pair tile; running clusters take over unlaunched ones.
   if (launch_pdl(kern, dim3(static_cast<unsigned>(prm.num_tiles * 2)), dim3(P_THREADS), L::ALLOC, stream, mA, mB, mC,

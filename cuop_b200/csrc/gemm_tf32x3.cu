@@ -468,13 +468,13 @@ int launch_x3(const GemmProblem& p, cudaStream_t stream, const char* name) {
   prm.bias = p.bias;
   prm.epi = p.epi;
   auto kern = gemm_tf32x3_kernel<BN, STAGES, A_MN, B_MN>;
-  static bool attr_set[64] = {};
+  static std::atomic<bool> attr_set[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return CUOPX_CUDA_ERROR;
-  if (!attr_set[dev]) {
+  if (!attr_set[dev].load(std::memory_order_relaxed)) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) != cudaSuccess)
       return CUOPX_CUDA_ERROR;
-    attr_set[dev] = true;
+    attr_set[dev].store(true, std::memory_order_relaxed);
   }
   const int grid = std::min(prm.num_tiles, device_sm_count());
   if (launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(X3_THREADS), L::ALLOC, stream, mA, mB, mC, prm) !=
