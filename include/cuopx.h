@@ -13,6 +13,14 @@
  * call allocates device memory (scratch is passed in by the caller); only
  * the set-up call cuopx_peer_alloc does.
  *
+ * Threads: compute calls may come from several host threads at once, on
+ * one device or several; the library's per-device caches and its tuning
+ * table are synchronised.  The GEMM variant override and the fp32 GEMM mode
+ * are process-wide settings; cuopx_set_gemm_variant_thread and
+ * cuopx_last_kernel are per host thread.  Work is ordered only by the
+ * streams the caller passes, so two calls that share a scratch buffer must
+ * share a stream (or be ordered by events).
+ *
  * Layout convention: row-major, like the reference operators
  * (src/cuda_op/detail/cuBlas/gemm.cu:14-42, gemv.cu:10-23).
  */
