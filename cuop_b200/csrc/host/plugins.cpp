@@ -7,6 +7,9 @@
 //   PluginRegistrar / PluginManager / GlobalJITManager
 //                                 reference src/jit/global_jit_manager.cu:14-400
 //   BlasJITPluginManager          reference src/jit/Blas/blas_jit_plugin_manager.cu:7-66
+//   ExecuteTyped (GEMM, batched GEMM, GEMV plugins): the same calls for
+//                                 fp16/bf16/fp64 buffers; no reference
+//                                 counterpart (its Execute is float-only)
 #include <algorithm>
 #include <cctype>
 #include <chrono>
@@ -181,6 +184,19 @@ void GemmJITPlugin::BindWeight(const Tensor<float>& w) {
   memory_usage_ = 0;
 }
 
+namespace {
+// Bytes per element of a DataType; 0 for a value outside the enum.
+size_t typed_size(DataType dt) {
+  switch (dt) {
+    case DataType::FLOAT32: return 4;
+    case DataType::FLOAT64: return 8;
+    case DataType::FLOAT16:
+    case DataType::BFLOAT16: return 2;
+  }
+  return 0;
+}
+}  // namespace
+
 StatusCode GemmJITPlugin::Execute(const std::vector<Tensor<float>>& inputs, std::vector<Tensor<float>>& outputs) {
   const StatusCode r = ready_to_execute();
   if (r != StatusCode::SUCCESS) return r;
@@ -218,6 +234,33 @@ StatusCode GemmJITPlugin::Execute(const std::vector<Tensor<float>>& inputs, std:
       2.0 * M * N * K, bytes, {static_cast<int>(M), static_cast<int>(N), static_cast<int>(K)});
 }
 
+StatusCode GemmJITPlugin::ExecuteTyped(DataType dtype, int64_t M, int64_t N, int64_t K, const void* A,
+                                       const void* W, void* C) {
+  const StatusCode r = ready_to_execute();
+  if (r != StatusCode::SUCCESS) return r;
+  const size_t es = typed_size(dtype);
+  if (es == 0) {
+    last_error_ = "unsupported element type";
+    return StatusCode::UNSUPPORTED_TYPE;
+  }
+  if (M < 0 || N < 0 || K < 0) {
+    last_error_ = "negative matrix dimension";
+    return StatusCode::INVALID_ARGUMENT;
+  }
+  if (M > 0 && N > 0 && (C == nullptr || (K > 0 && (A == nullptr || W == nullptr)))) {
+    last_error_ = "ExecuteTyped needs A, W and C buffers";
+    return StatusCode::INVALID_ARGUMENT;
+  }
+  const int64_t lda = std::max<int64_t>(1, transA_ ? M : K), ldb = std::max<int64_t>(1, transB_ ? K : N);
+  const double bytes = double(es) * (double(M) * K + double(K) * N + double(M) * N * (beta_ != 0.f ? 2 : 1));
+  return timed(
+      [&] {
+        return cuopx_gemm(static_cast<int>(dtype), transA_, transB_, M, N, K, alpha_, A, lda, W, ldb, beta_, C,
+                          std::max<int64_t>(1, N), stream_);
+      },
+      2.0 * M * N * K, bytes, {static_cast<int>(M), static_cast<int>(N), static_cast<int>(K)});
+}
+
 // ----------------------------------------------------------------- batched GEMM
 StatusCode GemmBatchedJITPlugin::Execute(const std::vector<Tensor<float>>& inputs,
                                          std::vector<Tensor<float>>& outputs) {
@@ -246,6 +289,33 @@ StatusCode GemmBatchedJITPlugin::Execute(const std::vector<Tensor<float>>& input
       [&] {
         return cuopx_gemm_strided_batched(CUOPX_F32, transA_, transB_, m_, n_, k_, alpha_, A.data(), lda, sA,
                                           B.data(), ldb, sB, beta_, C.data(), n_, sC, batch_, stream_);
+      },
+      2.0 * batch_ * m_ * n_ * double(k_), bytes, {m_, n_, k_});
+}
+
+StatusCode GemmBatchedJITPlugin::ExecuteTyped(DataType dtype, const void* A, const void* B, void* C) {
+  const StatusCode r = ready_to_execute();
+  if (r != StatusCode::SUCCESS) return r;
+  const size_t es = typed_size(dtype);
+  if (es == 0) {
+    last_error_ = "unsupported element type";
+    return StatusCode::UNSUPPORTED_TYPE;
+  }
+  if (batch_ <= 0 || m_ <= 0 || n_ <= 0 || k_ <= 0) {
+    last_error_ = "batch size and matrix dimensions must be set";
+    return StatusCode::INVALID_ARGUMENT;
+  }
+  if (A == nullptr || B == nullptr || C == nullptr) {
+    last_error_ = "ExecuteTyped needs A, B and C buffers";
+    return StatusCode::INVALID_ARGUMENT;
+  }
+  const int64_t sA = sA_ ? sA_ : int64_t(m_) * k_, sB = sB_ ? sB_ : int64_t(k_) * n_, sC = sC_ ? sC_ : int64_t(m_) * n_;
+  const int64_t lda = transA_ ? m_ : k_, ldb = transB_ ? k_ : n_;
+  const double bytes = double(es) * batch_ * (double(m_) * k_ + double(k_) * n_ + double(m_) * n_);
+  return timed(
+      [&] {
+        return cuopx_gemm_strided_batched(static_cast<int>(dtype), transA_, transB_, m_, n_, k_, alpha_, A, lda, sA,
+                                          B, ldb, sB, beta_, C, n_, sC, batch_, stream_);
       },
       2.0 * batch_ * m_ * n_ * double(k_), bytes, {m_, n_, k_});
 }
@@ -306,6 +376,37 @@ StatusCode GemvJITPlugin::Execute(const std::vector<Tensor<float>>& inputs, std:
                           workspace_.data(), workspace_.numel(), stream_);
       },
       2.0 * m * n, 4.0 * (double(m) * n + n + m), {static_cast<int>(m), static_cast<int>(n), 1});
+}
+
+StatusCode GemvJITPlugin::ExecuteTyped(DataType dtype, int64_t M, int64_t N, const void* A, const void* x, void* y) {
+  const StatusCode r = ready_to_execute();
+  if (r != StatusCode::SUCCESS) return r;
+  const size_t es = typed_size(dtype);
+  if (es == 0) {
+    last_error_ = "unsupported element type";
+    return StatusCode::UNSUPPORTED_TYPE;
+  }
+  if (M < 0 || N < 0) {
+    last_error_ = "negative matrix dimension";
+    return StatusCode::INVALID_ARGUMENT;
+  }
+  if (M > 0 && (y == nullptr || (N > 0 && (A == nullptr || x == nullptr)))) {
+    last_error_ = "ExecuteTyped needs A, x and y buffers";
+    return StatusCode::INVALID_ARGUMENT;
+  }
+  const size_t need = cuopx_gemv_workspace_size(static_cast<int>(dtype), transA_, M, N);
+  if (need > workspace_.numel()) {
+    workspace_ = Tensor<unsigned char>({need});
+    workspace_.zero();
+  }
+  memory_usage_ = weight_.bytes() + workspace_.bytes();
+  const int64_t lda = std::max<int64_t>(1, transA_ ? M : N);
+  return timed(
+      [&] {
+        return cuopx_gemv(static_cast<int>(dtype), transA_, M, N, alpha_, A, lda, x, beta_, y, workspace_.data(),
+                          workspace_.numel(), stream_);
+      },
+      2.0 * M * N, double(es) * (double(M) * N + N + M), {static_cast<int>(M), static_cast<int>(N), 1});
 }
 
 // ----------------------------------------------------------------- vector ops

@@ -12,6 +12,7 @@
 // "gemm_jit" key JITWrapper asks for.
 #pragma once
 
+#include <cstdint>
 #include <functional>
 #include <memory>
 #include <string>
@@ -21,6 +22,10 @@
 #include "jit/ijit_plugin.hpp"
 
 namespace cu_op_mem {
+
+// Element type of the ExecuteTyped calls below.  The values are the
+// CUOPX_F32 / CUOPX_F64 / CUOPX_F16 / CUOPX_BF16 codes of cuopx.h.
+enum class DataType { FLOAT32 = 0, FLOAT64 = 1, FLOAT16 = 2, BFLOAT16 = 3 };
 
 // Shared state and bookkeeping of the BLAS plugins.
 class BlasPluginBase : public IJITPlugin {
@@ -67,6 +72,15 @@ class GemmJITPlugin : public BlasPluginBase {
   void SetWeight(const Tensor<float>& weight);
   // Uses W in place; the caller keeps it alive while the plugin runs.
   void BindWeight(const Tensor<float>& weight);
+  // The same product for any element type, on raw buffers: the reference's
+  // Execute carries only float tensors, so fp16/bf16 operands (fp32
+  // accumulation, one rounding of C) come through here.  op(A) is M x K and
+  // op(W) is K x N, densely packed row-major buffers of `dtype` (A stored
+  // K x M when transA, W stored N x K when transB), C is M x N; transposes
+  // and alpha/beta from SetGemmParams, the weight from SetWeight/BindWeight
+  // is not used.  Synchronous on the plugin's stream, like Execute.  No
+  // counterpart in the reference.
+  StatusCode ExecuteTyped(DataType dtype, int64_t M, int64_t N, int64_t K, const void* A, const void* W, void* C);
   static bool SupportsOperator(const std::string& op_name) { return op_name == "gemm" || op_name == "Gemm"; }
 
  private:
@@ -86,6 +100,11 @@ class GemmBatchedJITPlugin : public BlasPluginBase {
   void SetAlphaBeta(float alpha, float beta) { alpha_ = alpha, beta_ = beta; }
   // 0 (the default) means densely packed.
   void SetBatchStride(int strideA, int strideB, int strideC) { sA_ = strideA, sB_ = strideB, sC_ = strideC; }
+  // Execute for any element type on raw buffers of `dtype` (fp16/bf16 with
+  // fp32 accumulation, which float tensors cannot carry); batch, dimensions,
+  // strides, transposes and alpha/beta from the setters.  No counterpart in
+  // the reference.
+  StatusCode ExecuteTyped(DataType dtype, const void* A, const void* B, void* C);
   static bool SupportsOperator(const std::string& op_name) {
     return op_name == "gemm_batched" || op_name == "GemmBatched" || op_name == "batched_gemm" ||
            op_name == "BatchedGemm";
@@ -107,6 +126,13 @@ class GemvJITPlugin : public BlasPluginBase {
   void SetGemvParams(bool transA, float alpha, float beta);
   void SetWeight(const Tensor<float>& weight);   // copies A
   void BindWeight(const Tensor<float>& weight);  // uses A in place
+  // Execute for any element type on raw buffers of `dtype`: y (M) =
+  // alpha * op(A) x (N) + beta * y, A densely packed M x N row-major (stored
+  // N x M when transA, as the float weight is read); transA and alpha/beta
+  // from SetGemvParams, split-K scratch from the plugin's own workspace.
+  // The weight from SetWeight/BindWeight is not used.  No counterpart in the
+  // reference.
+  StatusCode ExecuteTyped(DataType dtype, int64_t M, int64_t N, const void* A, const void* x, void* y);
   void Cleanup() override;
   static bool SupportsOperator(const std::string& op_name) { return op_name == "gemv" || op_name == "Gemv"; }
 

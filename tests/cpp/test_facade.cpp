@@ -621,6 +621,140 @@ TEST_GPU(BatchedAndGemvAndVectorPlugins) {
   for (int i = 0; i < 4; ++i) EXPECT_NEAR(ha[i], 2 * hx[i] + hy2[i], 1e-6);
 }
 
+TEST_HOST(TypedPluginExecuteRequiresCompile) {
+  int dummy = 0;
+  GemmJITPlugin g;
+  EXPECT_TRUE(g.ExecuteTyped(DataType::FLOAT16, 4, 4, 4, &dummy, &dummy, &dummy) == StatusCode::NOT_COMPILED);
+  GemmBatchedJITPlugin b;
+  EXPECT_TRUE(b.ExecuteTyped(DataType::FLOAT16, &dummy, &dummy, &dummy) == StatusCode::NOT_COMPILED);
+  GemvJITPlugin v;
+  EXPECT_TRUE(v.ExecuteTyped(DataType::BFLOAT16, 4, 4, &dummy, &dummy, &dummy) == StatusCode::NOT_COMPILED);
+}
+
+// Argument checks of ExecuteTyped, all rejected before any launch.
+TEST_GPU(TypedPluginExecuteValidatesArguments) {
+  RegisterBlasJITPlugins();  // self-contained when run alone (filter argument)
+  int dummy = 0;
+  auto pg = CreateBlasJITPlugin("gemm");
+  auto* g = dynamic_cast<GemmJITPlugin*>(pg.get());
+  EXPECT_TRUE(g && g->Initialize() == StatusCode::SUCCESS && g->Compile(JITConfig()) == StatusCode::SUCCESS);
+  if (!g) return;
+  EXPECT_TRUE(g->ExecuteTyped(static_cast<DataType>(9), 4, 4, 4, &dummy, &dummy, &dummy) ==
+              StatusCode::UNSUPPORTED_TYPE);
+  EXPECT_TRUE(g->ExecuteTyped(DataType::BFLOAT16, -1, 4, 4, &dummy, &dummy, &dummy) == StatusCode::INVALID_ARGUMENT);
+  EXPECT_TRUE(g->ExecuteTyped(DataType::BFLOAT16, 4, 4, 4, nullptr, &dummy, &dummy) == StatusCode::INVALID_ARGUMENT);
+  EXPECT_TRUE(!g->GetLastError().empty());
+  auto pb = CreateBlasJITPlugin("gemm_batched");
+  auto* b = dynamic_cast<GemmBatchedJITPlugin*>(pb.get());
+  EXPECT_TRUE(b && b->Initialize() == StatusCode::SUCCESS && b->Compile(JITConfig()) == StatusCode::SUCCESS);
+  if (b) EXPECT_TRUE(b->ExecuteTyped(DataType::FLOAT16, &dummy, &dummy, &dummy) == StatusCode::INVALID_ARGUMENT);
+  auto pv = CreateBlasJITPlugin("gemv");
+  auto* v = dynamic_cast<GemvJITPlugin*>(pv.get());
+  EXPECT_TRUE(v && v->Initialize() == StatusCode::SUCCESS && v->Compile(JITConfig()) == StatusCode::SUCCESS);
+  if (v) EXPECT_TRUE(v->ExecuteTyped(DataType::BFLOAT16, 4, 4, &dummy, nullptr, &dummy) == StatusCode::INVALID_ARGUMENT);
+}
+
+// ExecuteTyped runs the kernels the C ABI runs: results bit-identical to
+// direct cuopx calls on the same fp16/bf16 buffers, and within the 16-bit
+// tolerance (max|C-R| / max|R| <= 1e-2) of an fp64 product of the widened inputs.
+TEST_GPU(TypedPluginExecuteMatchesCAbi) {
+  RegisterBlasJITPlugins();  // self-contained when run alone (filter argument)
+  const int M = 256, N = 320, K = 192, batch = 3;
+  std::vector<float> a(size_t(batch) * M * K), b(size_t(batch) * K * N);
+  oracle_fill_uniform_f32(a.data(), a.size(), 41, -1.f, 1.f);
+  oracle_fill_uniform_f32(b.data(), b.size(), 42, -1.f, 1.f);
+  std::vector<__half> ah(a.size()), bh(b.size());
+  for (size_t i = 0; i < a.size(); ++i) ah[i] = __float2half(a[i]);
+  for (size_t i = 0; i < b.size(); ++i) bh[i] = __float2half(b[i]);
+  Tensor<__half> A({size_t(batch), size_t(M), size_t(K)}), B({size_t(batch), size_t(K), size_t(N)});
+  Tensor<__half> C1({size_t(batch), size_t(M), size_t(N)}), C2({size_t(batch), size_t(M), size_t(N)});
+  A.copy_from_host(ah.data());
+  B.copy_from_host(bh.data());
+
+  // GEMM plugin on batch 0
+  auto pg = CreateBlasJITPlugin("gemm");
+  auto* g = dynamic_cast<GemmJITPlugin*>(pg.get());
+  EXPECT_TRUE(g && g->Initialize() == StatusCode::SUCCESS && g->Compile(JITConfig()) == StatusCode::SUCCESS);
+  if (!g) return;
+  g->SetGemmParams(false, false, 1.0f, 0.0f);
+  EXPECT_TRUE(g->ExecuteTyped(DataType::FLOAT16, M, N, K, A.data(), B.data(), C1.data()) == StatusCode::SUCCESS);
+  EXPECT_TRUE(std::string(cuopx_last_kernel()).rfind("gemm_tc", 0) == 0);
+  EXPECT_EQ(cuopx_gemm(CUOPX_F16, 0, 0, M, N, K, 1.0, A.data(), K, B.data(), N, 0.0, C2.data(), N, nullptr),
+            CUOPX_SUCCESS);
+  EXPECT_TRUE(cudaDeviceSynchronize() == cudaSuccess);
+  auto h1 = to_host(C1), h2 = to_host(C2);
+  EXPECT_TRUE(std::memcmp(h1.data(), h2.data(), size_t(M) * N * sizeof(__half)) == 0);
+  double maxref = 0, maxerr = 0;
+  for (int i = 0; i < M; ++i)
+    for (int j = 0; j < N; ++j) {
+      double s = 0;
+      for (int k = 0; k < K; ++k) s += double(__half2float(ah[size_t(i) * K + k])) * __half2float(bh[size_t(k) * N + j]);
+      maxref = std::max(maxref, std::fabs(s));
+      maxerr = std::max(maxerr, std::fabs(s - double(__half2float(h1[size_t(i) * N + j]))));
+    }
+  EXPECT_TRUE(maxref > 0 && maxerr / maxref <= 1e-2);
+
+  // batched plugin, all batches, alpha/beta
+  auto pb = CreateBlasJITPlugin("batched_gemm");
+  auto* bp = dynamic_cast<GemmBatchedJITPlugin*>(pb.get());
+  EXPECT_TRUE(bp && bp->Initialize() == StatusCode::SUCCESS && bp->Compile(JITConfig()) == StatusCode::SUCCESS);
+  if (!bp) return;
+  bp->SetBatchSize(batch);
+  bp->SetMatrixDimensions(M, N, K);
+  bp->SetAlphaBeta(0.5f, 0.25f);
+  const std::vector<__half> ones(C1.numel(), __float2half(1.f));
+  C1.copy_from_host(ones.data());
+  C2.copy_from_host(ones.data());
+  EXPECT_TRUE(bp->ExecuteTyped(DataType::FLOAT16, A.data(), B.data(), C1.data()) == StatusCode::SUCCESS);
+  EXPECT_EQ(cuopx_gemm_strided_batched(CUOPX_F16, 0, 0, M, N, K, 0.5, A.data(), K, int64_t(M) * K, B.data(), N,
+                                       int64_t(K) * N, 0.25, C2.data(), N, int64_t(M) * N, batch, nullptr),
+            CUOPX_SUCCESS);
+  EXPECT_TRUE(cudaDeviceSynchronize() == cudaSuccess);
+  h1 = to_host(C1);
+  h2 = to_host(C2);
+  EXPECT_TRUE(std::memcmp(h1.data(), h2.data(), h1.size() * sizeof(__half)) == 0);
+
+  // GEMV plugin, bf16, plain and transposed
+  const int gm = 768, gn = 1024;
+  std::vector<float> ga(size_t(gm) * gn), gx(gm > gn ? gm : gn);
+  oracle_fill_uniform_f32(ga.data(), ga.size(), 43, -1.f, 1.f);
+  oracle_fill_uniform_f32(gx.data(), gx.size(), 44, -1.f, 1.f);
+  std::vector<__nv_bfloat16> gah(ga.size()), gxh(gx.size());
+  for (size_t i = 0; i < ga.size(); ++i) gah[i] = __float2bfloat16(ga[i]);
+  for (size_t i = 0; i < gx.size(); ++i) gxh[i] = __float2bfloat16(gx[i]);
+  Tensor<__nv_bfloat16> GA({size_t(gm) * gn}), GX({gx.size()}), Y1({size_t(gm)}), Y2({size_t(gm)});
+  GA.copy_from_host(gah.data());
+  GX.copy_from_host(gxh.data());
+  auto pv = CreateBlasJITPlugin("gemv");
+  auto* v = dynamic_cast<GemvJITPlugin*>(pv.get());
+  EXPECT_TRUE(v && v->Initialize() == StatusCode::SUCCESS && v->Compile(JITConfig()) == StatusCode::SUCCESS);
+  if (!v) return;
+  for (int trans = 0; trans < 2; ++trans) {
+    v->SetGemvParams(trans != 0, 1.0f, 0.0f);
+    EXPECT_TRUE(v->ExecuteTyped(DataType::BFLOAT16, gm, gn, GA.data(), GX.data(), Y1.data()) == StatusCode::SUCCESS);
+    const size_t ws = cuopx_gemv_workspace_size(CUOPX_BF16, trans, gm, gn);
+    Tensor<unsigned char> W({ws > 0 ? ws : 1});
+    W.zero();
+    EXPECT_EQ(cuopx_gemv(CUOPX_BF16, trans, gm, gn, 1.0, GA.data(), trans ? gm : gn, GX.data(), 0.0, Y2.data(),
+                         W.data(), ws, nullptr),
+              CUOPX_SUCCESS);
+    EXPECT_TRUE(cudaDeviceSynchronize() == cudaSuccess);
+    auto y1 = to_host(Y1), y2 = to_host(Y2);
+    EXPECT_TRUE(std::memcmp(y1.data(), y2.data(), y1.size() * sizeof(__nv_bfloat16)) == 0);
+    double mr = 0, me = 0;
+    for (int i = 0; i < gm; ++i) {
+      double s = 0;
+      for (int j = 0; j < gn; ++j) {
+        const size_t idx = trans ? size_t(j) * gm + i : size_t(i) * gn + j;
+        s += double(__bfloat162float(gah[idx])) * __bfloat162float(gxh[j]);
+      }
+      mr = std::max(mr, std::fabs(s));
+      me = std::max(me, std::fabs(s - double(__bfloat162float(y1[i]))));
+    }
+    EXPECT_TRUE(mr > 0 && me / mr <= 1e-2);
+  }
+}
+
 TEST_GPU(JitWrapperRoutesGemmThroughPlugin) {
   // test/JIT_test/test_jit_system.cpp:99-141 style: original vs wrapper on the same inputs
   const int n = 512;
