@@ -191,6 +191,63 @@ TEST_GPU(GemvForwardFloatNoTranspose) {  // test/cuBlas/test_gemv/test_gemv.cpp:
   EXPECT_NEAR(h[1], 32, 1e-5);
 }
 
+// The reference's known answers (test_gemm.cpp:19-43, test_gemv.cpp:19-44,
+// test_matmul.cpp:45-67) through Gemm<T>, Gemv<T> and BatchMatMul<T> for the
+// element types the reference does not instantiate.  Every input, product
+// and sum is a small integer, exact in fp16, bf16 and fp64, so the results
+// must match exactly.
+template <typename T>
+static std::vector<T> cast_vec(const float* v, size_t n) {
+  std::vector<T> out(n);
+  for (size_t i = 0; i < n; ++i) out[i] = T(v[i]);
+  return out;
+}
+template <typename T>
+static float as_float(T v) {
+  return float(v);
+}
+template <typename T>
+static void known_answers_for_type() {
+  const float h_input[6] = {1, 2, 3, 4, 5, 6}, h_weight[12] = {1, 0, 0, 0, 0, 1, 0, 0, 0, 0, 1, 0};
+  Tensor<T> input({2, 3}), weight({3, 4}), output({2, 4});
+  input.copy_from_host(cast_vec<T>(h_input, 6).data());
+  weight.copy_from_host(cast_vec<T>(h_weight, 12).data());
+  Gemm<T> gemm(false, false);
+  gemm.SetWeight(weight);
+  EXPECT_TRUE(gemm.Forward(input, output) == StatusCode::SUCCESS);
+  auto h = to_host(output);
+  const float expected[8] = {1, 2, 3, 0, 4, 5, 6, 0};
+  for (int i = 0; i < 8; ++i) EXPECT_EQ(as_float(h[i]), expected[i]);
+
+  const float h_x[3] = {1, 2, 3};
+  Tensor<T> x({3}), y({2});
+  x.copy_from_host(cast_vec<T>(h_x, 3).data());
+  y.zero();
+  Gemv<T> gemv(false);
+  gemv.SetWeight(x);
+  EXPECT_TRUE(gemv.Forward(input, y) == StatusCode::SUCCESS);
+  auto hy = to_host(y);
+  EXPECT_EQ(as_float(hy[0]), 14.f);
+  EXPECT_EQ(as_float(hy[1]), 32.f);
+
+  const float h_a3[12] = {1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12};
+  const float h_b3[24] = {1, 0, 0, 0, 0, 1, 0, 0, 0, 0, 1, 0, 2, 0, 0, 0, 0, 2, 0, 0, 0, 0, 2, 0};
+  Tensor<T> A3({2, 2, 3}), B3({2, 3, 4}), C3({2, 2, 4});
+  A3.copy_from_host(cast_vec<T>(h_a3, 12).data());
+  B3.copy_from_host(cast_vec<T>(h_b3, 24).data());
+  BatchMatMul<T> bmm;
+  EXPECT_TRUE(bmm.Forward(A3, B3, C3) == StatusCode::SUCCESS);
+  auto hc = to_host(C3);
+  const float e3[16] = {1, 2, 3, 0, 4, 5, 6, 0, 14, 16, 18, 0, 20, 22, 24, 0};
+  for (int i = 0; i < 16; ++i) EXPECT_EQ(as_float(hc[i]), e3[i]);
+}
+
+TEST_GPU(KnownAnswersForDoubleHalfAndBf16) {
+  known_answers_for_type<double>();
+  known_answers_for_type<__half>();
+  known_answers_for_type<__nv_bfloat16>();
+}
+
 TEST_GPU(MatMulForward2DAndBatch3D) {  // test/cuDNN/test_matmul/test_matmul.cpp:21-67
   float h_A[6] = {1, 2, 3, 4, 5, 6}, h_B[12] = {1, 0, 0, 0, 0, 1, 0, 0, 0, 0, 1, 0};
   Tensor<float> A({2, 3}), B({3, 4}), C({2, 4});
