@@ -195,6 +195,36 @@ def gemm_sample_f64(A, B, rows, cols, transA=False, transB=False, nthreads=None)
     return out
 
 
+def gemm_rows_cols_f64(A, B, rows, cols, block: int = 2048):
+    """fp64 A @ B on complete rows and complete columns, for full-size error
+    norms: returns (R, Q) with R = (A @ B)[rows, :] and Q = (A @ B)[:, cols].
+
+    A [M, K] and B [K, N] are fp32 arrays (16-bit inputs already widened,
+    exactly).  Every fp32 x fp32 product is exact in fp64, so this is the
+    same fp64 reference value as gemm_sample_f64 up to fp64 summation order
+    (~1e-16 relative); it runs as blocked fp64 matrix products, because a
+    per-element loop over complete 8192-long rows and columns is far too
+    slow on strided B.  Blocks of `block` columns (rows) bound the fp64
+    copies to K x block."""
+    A = np.asarray(A, np.float32)
+    B = np.asarray(B, np.float32)
+    M, K = A.shape
+    N = B.shape[1]
+    rows = np.asarray(rows, np.int64)
+    cols = np.asarray(cols, np.int64)
+    Ar = A[rows].astype(np.float64)
+    R = np.empty((rows.size, N), np.float64)
+    for j0 in range(0, N, block):
+        j1 = min(N, j0 + block)
+        R[:, j0:j1] = Ar @ B[:, j0:j1].astype(np.float64)
+    Bc = B[:, cols].astype(np.float64)
+    Q = np.empty((M, cols.size), np.float64)
+    for i0 in range(0, M, block):
+        i1 = min(M, i0 + block)
+        Q[i0:i1] = A[i0:i1].astype(np.float64) @ Bc
+    return R, Q
+
+
 def gemv_f32(A, x, y=None, trans=False, alpha=1.0, beta=0.0, nthreads=None):
     A = np.ascontiguousarray(A, np.float32)
     x = np.ascontiguousarray(x, np.float32)

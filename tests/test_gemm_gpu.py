@@ -251,10 +251,13 @@ def test_lowp_unaligned_uses_generic(dev):
     assert O.max_relative(O.from_lowp(lowp_bits(C), dt), O.from_lowp(ref, dt)) <= LOWP_TOL
 
 
-def _sampled_check(C, A32, B32, rows, cols, tol):
-    ref = O.gemm_sample_f64(A32, B32, rows, cols)
-    got = C[rows][:, cols].float().cpu().numpy()
-    return O.max_relative(got, ref)
+def _rows_cols_check(C, A32, B32, rows, cols):
+    """Max-relative error of complete rows and complete columns of C against
+    the fp64 oracle (the worse of the two sets)."""
+    R, Q = O.gemm_rows_cols_f64(A32, B32, rows, cols)
+    got_rows = C[torch.as_tensor(rows, device=C.device)].float().cpu().numpy()
+    got_cols = C[:, torch.as_tensor(cols, device=C.device)].float().cpu().numpy()
+    return max(O.max_relative(got_rows, R), O.max_relative(got_cols, Q))
 
 
 def test_c3_fp16_8192_full(dev):
@@ -268,10 +271,11 @@ def test_c3_fp16_8192_full(dev):
     assert cx.last_kernel() == "gemm_tc2_256x512"
     full = fp32_reference_gpu(A, B)
     assert O.max_relative(C.float().cpu().numpy(), full.cpu().numpy()) <= LOWP_TOL
+    # 256 complete rows and 256 complete columns against the fp64 oracle
     rng = np.random.default_rng(0)
-    rows = np.sort(rng.choice(n, 8, replace=False))
+    rows = np.sort(rng.choice(n, 256, replace=False))
     cols = np.sort(rng.choice(n, 256, replace=False))
-    assert _sampled_check(C, O.from_lowp(A16, dt), O.from_lowp(B16, dt), rows, cols, LOWP_TOL) <= LOWP_TOL
+    assert _rows_cols_check(C, O.from_lowp(A16, dt), O.from_lowp(B16, dt), rows, cols) <= LOWP_TOL
 
 
 def test_c5_bf16_linear_full(dev):
@@ -285,10 +289,11 @@ def test_c5_bf16_linear_full(dev):
     full = fp32_reference_gpu(X, W)
     assert O.max_relative(Y.float().cpu().numpy(), full.cpu().numpy()) <= LOWP_TOL
     del full
+    # 256 complete rows and 256 complete columns against the fp64 oracle
     rng = np.random.default_rng(1)
-    rows = np.sort(rng.choice(M, 4, replace=False))
-    cols = np.sort(rng.choice(N, 128, replace=False))
-    assert _sampled_check(Y, O.from_lowp(X16, dt), O.from_lowp(W16, dt), rows, cols, LOWP_TOL) <= LOWP_TOL
+    rows = np.sort(rng.choice(M, 256, replace=False))
+    cols = np.sort(rng.choice(N, 256, replace=False))
+    assert _rows_cols_check(Y, O.from_lowp(X16, dt), O.from_lowp(W16, dt), rows, cols) <= LOWP_TOL
 
 
 def test_deterministic_lowp(dev):

@@ -177,3 +177,15 @@ def test_gemm_sample_matches_full():
     full = A.astype(np.float64) @ B.astype(np.float64)
     rows, cols = np.array([0, 7, 49]), np.array([3, 69])
     np.testing.assert_allclose(O.gemm_sample_f64(A, B, rows, cols), full[np.ix_(rows, cols)], rtol=1e-12)
+
+
+def test_gemm_rows_cols_matches_the_per_element_sampler():
+    """The blocked fp64 rows/columns helper against the C per-element fp64
+    sampler (ascending-k sums) on complete rows and columns, with blocks
+    smaller than the matrix so the block edges are covered."""
+    A = O.uniform((70, 300), seed=3)
+    B = O.uniform((300, 90), seed=4)
+    rows, cols = np.array([0, 5, 69]), np.array([1, 44, 89])
+    R, Q = O.gemm_rows_cols_f64(A, B, rows, cols, block=32)
+    np.testing.assert_allclose(R, O.gemm_sample_f64(A, B, rows, np.arange(90)), rtol=1e-12, atol=1e-12)
+    np.testing.assert_allclose(Q, O.gemm_sample_f64(A, B, np.arange(70), cols), rtol=1e-12, atol=1e-12)
