@@ -39,6 +39,9 @@ GEMV_BYTES = (GEMV_N * GEMV_N + 2 * GEMV_N) * 4  # A + x + y (beta = 0: y not re
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 FP32_SIMT_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
+# Nominal B200 figures, reported beside the measured-peak fractions.
+SPEC_HBM_GBS = 8000.0
+SPEC_DENSE_16BIT_TFLOPS = 2250.0
 
 # DRAM bytes per launch from the ncu capture summarised in
 # profiles/gemv_f32_8192_ncu.md (dram__bytes_read.sum + dram__bytes_write.sum).
@@ -294,7 +297,8 @@ def run_gemv(args, rank, world, local_rank):
                    "bytes_per_step": 2 * GEMV_BYTES},
         "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": round(achieved, 1), "peak": hbm,
                      "peak_source": f"{peak_src} hbm_gbs (burst copy)", "unit": "GB/s",
-                     "frac": round(achieved / hbm, 4), "traffic": NCU_TRAFFIC_BYTES.get(dom_name),
+                     "frac": round(achieved / hbm, 4), "frac_spec": round(achieved / SPEC_HBM_GBS, 4),
+                     "spec_peak": SPEC_HBM_GBS, "traffic": NCU_TRAFFIC_BYTES.get(dom_name),
                      "algorithmic_bytes": GEMV_BYTES},
         "kernels": kernels,
         "gpu_launches": launches,
@@ -569,7 +573,7 @@ def _config_c3(cx, sharding, dev, g, steps, rank, world, bf16_peak, peak_src):
     res = {
         "tflops_total": round(2 * n ** 3 / (ms * 1e-3) / 1e12, 1), "ms": round(ms, 4), "kernel": kname,
         "gemm_only_tflops_per_gpu": round(tf_local, 1), "frac_gemm_only": round(tf_local / bf16_peak, 4),
-        "peak_tflops": bf16_peak, "peak_source": f"{peak_src} bf16_tflops (burst)",
+        "frac_spec_gemm_only": round(tf_local / SPEC_DENSE_16BIT_TFLOPS, 4), "peak_tflops": bf16_peak, "peak_source": f"{peak_src} bf16_tflops (burst)",
         "parallelism": "single GPU" if world == 1 else
         f"N-sharded x{world}; GEMM epilogue stores every tile into all ranks' outputs over NVLink", **res}
     del A, Wl
@@ -595,7 +599,8 @@ def _config_c4(cx, sharding, dev, g, steps, rank, world, hbm):
     res = {
         "gbs_total": round(bytes_total / (ms * 1e-3) / 1e9, 1), "ms": round(ms, 5), "kernel": cx.last_kernel(),
         "tflops_total": round(2 * batch * M * N_ * K / (ms * 1e-3) / 1e12, 2),
-        "frac_hbm_per_gpu": round(gbs_local / hbm, 4), "l2": f"{sets} rotated input sets > L2",
+        "frac_hbm_per_gpu": round(gbs_local / hbm, 4), "frac_spec_hbm_per_gpu": round(gbs_local / SPEC_HBM_GBS, 4),
+        "l2": f"{sets} rotated input sets > L2",
         "parallelism": f"batch-sharded x{world}, no collective"}
     del As, Bs, Cs
     torch.cuda.empty_cache()
@@ -625,6 +630,7 @@ def _config_c5(cx, sharding, dev, g, steps, rank, world, bf16_peak):
     res = {
         "tflops_total": round(2 * M * K * N_ / (ms * 1e-3) / 1e12, 1), "ms": round(ms, 4), "kernel": kname,
         "gemm_only_tflops_per_gpu": round(tf_local, 1), "frac_gemm_only": round(tf_local / bf16_peak, 4),
+        "frac_spec_gemm_only": round(tf_local / SPEC_DENSE_16BIT_TFLOPS, 4),
         "parallelism": "single GPU" if world == 1 else
         f"W column-sharded x{world}; GEMM epilogue stores every tile of Y into all ranks' outputs over NVLink",
         **res}
