@@ -25,7 +25,16 @@ from typing import Callable, Optional
 import torch
 import torch.distributed as dist
 
-from . import ops
+from . import _native, ops
+
+
+class CollectiveError(RuntimeError):
+    """A collective of the column-sharded path did not complete: a rank died,
+    left, or did not join within the process group's timeout.  `status` is
+    cuOP's TIMEOUT StatusCode value.  The process group is unusable after
+    it: destroy it and build a new one before the next sharded call."""
+
+    status = _native.TIMEOUT
 
 
 def shard_range(total: int, rank: int, world: int) -> tuple[int, int]:
@@ -91,12 +100,23 @@ class ColumnShardedGemm:
                 continue
             self._gemm(X[r0:r1], self.w_local, local_blk[r0:r1])
             recv = torch.empty((G * (r1 - r0), nb), dtype=X.dtype, device=X.device)
-            h = dist.all_gather_into_tensor(recv, local_blk[r0:r1], group=self.group, async_op=True)
+            try:
+                h = dist.all_gather_into_tensor(recv, local_blk[r0:r1], group=self.group, async_op=True)
+            except Exception as e:  # the backend refused the collective (a peer is gone)
+                raise self._failed(r0, r1, e) from e
             pending.append((r0, r1, recv.view(G, r1 - r0, nb), h))
         for r0, r1, recv, h in pending:
-            h.wait()  # the current stream waits for this chunk's collective
+            try:
+                h.wait()  # the current stream waits for this chunk's collective
+            except Exception as e:  # timed out, peer connection closed, or communicator aborted
+                raise self._failed(r0, r1, e) from e
             self._gather(recv, out[r0:r1])
         return out
+
+    @staticmethod
+    def _failed(r0: int, r1: int, e: Exception) -> CollectiveError:
+        return CollectiveError(f"all-gather of output rows {r0}:{r1} did not complete: a rank died, left or did not "
+                               f"join within the process group's timeout ({type(e).__name__}: {e})")
 
 
 def split_columns(W: torch.Tensor, rank: int, world: int) -> torch.Tensor:

@@ -76,3 +76,45 @@ def test_column_sharded_gather_and_batch_sharding_two_ranks():
         ok_full, ok_local, counts = results[r]
         assert ok_full and ok_local
         assert counts == [1] * 10
+
+
+def _absent_rank_worker(rank, world, port, results):
+    """Rank 1 initialises the group and then never joins the all-gather
+    (it stays alive past rank 0's timeout); rank 0 must get a
+    CollectiveError after the group's 2 s timeout, not hang."""
+    import datetime
+    import time
+
+    from cuop_b200.sharding import CollectiveError
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=2))
+    try:
+        if rank == 1:
+            time.sleep(8)
+            results[rank] = "absent"
+            return
+        g = torch.Generator().manual_seed(0)
+        X = torch.randn(8, 4, generator=g, dtype=torch.float64)
+        Wl = torch.randn(4, 3, generator=g, dtype=torch.float64)
+        sg = ColumnShardedGemm(Wl, world, chunks=2, gemm_fn=_cpu_gemm, gather_fn=_cpu_gather)
+        t0 = time.monotonic()
+        try:
+            sg.forward(X)
+            results[rank] = ("no error", time.monotonic() - t0, 0)
+        except CollectiveError as e:
+            results[rank] = ("CollectiveError", time.monotonic() - t0, e.status)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_column_sharded_gather_reports_a_rank_that_never_joins():
+    world = 2
+    mgr = mp.get_context("spawn").Manager()
+    results = mgr.dict()
+    mp.start_processes(_absent_rank_worker, args=(world, _free_port(), results), nprocs=world, join=True,
+                       start_method="spawn")
+    kind, elapsed, status = results[0]
+    assert kind == "CollectiveError" and status == 1003
+    assert elapsed < 30
+    assert results[1] == "absent"
