@@ -2,6 +2,7 @@
 #include "base/memory_pool.hpp"
 
 #include <algorithm>
+#include <cstdio>
 #include <memory>
 
 namespace cu_op_mem {
@@ -157,6 +158,35 @@ void CudaMemoryPool::release_idle_locked(bool only_completed) {
 void CudaMemoryPool::ReleaseCached() {
   std::lock_guard<std::mutex> lock(mu_);
   release_idle_locked(false);
+}
+
+void CudaMemoryPool::ReleaseAll() { ReleaseCached(); }
+
+void CudaMemoryPool::Defragment() { ReleaseCached(); }
+
+void CudaMemoryPool::TrimCache() {
+  std::lock_guard<std::mutex> lock(mu_);
+  release_idle_locked(true);
+}
+
+void CudaMemoryPool::Preallocate(std::size_t block_size, std::size_t count) {
+  std::vector<void*> blocks;
+  blocks.reserve(count);
+  for (std::size_t i = 0; i < count; ++i) {
+    void* p = Alloc(block_size);
+    if (!p) break;
+    blocks.push_back(p);
+  }
+  for (void* p : blocks) Free(p, block_size);
+}
+
+void CudaMemoryPool::PrintStats() const {
+  const MemoryStats s = GetStats();
+  std::fprintf(stderr,
+               "cuop memory pool, device %d: reserved %zu B, in use %zu B, peak %zu B; %zu allocs (%zu cache hits, "
+               "%zu from cudaMalloc, %zu failed), %zu frees\n",
+               device_, s.bytes_reserved, s.bytes_in_use, s.peak_in_use, s.alloc_calls, s.cache_hits,
+               s.cache_misses, s.failed_allocs, s.free_calls);
 }
 
 void CudaMemoryPool::SetConfig(const MemoryPoolConfig& c) {

@@ -59,8 +59,21 @@ class CudaMemoryPool {
   void SetMemoryLimit(std::size_t bytes);  // 0 removes the limit
   MemoryStats GetStats() const;
   void ResetStats();
-  // Frees every idle cached block whose last use has completed.
+  // Frees every idle cached block, first waiting for the last use of any
+  // block whose stream work is still pending.  Blocks in use are untouched.
   void ReleaseCached();
+  // The reference pool's maintenance calls (include/base/memory_pool.hpp:93-111).
+  // Each block here is its own cudaMalloc, so there is nothing to merge or
+  // compact inside the pool; these map onto releasing idle blocks:
+  void ReleaseAll();   // = ReleaseCached()
+  void Defragment();   // = ReleaseCached(): idle blocks go back to the driver
+  void TrimCache();    // frees idle blocks whose last use has completed (no waiting)
+  // Allocates `count` blocks of `block_size` bytes into the idle cache, so
+  // later requests of that size class are cache hits (stops at the first
+  // allocation that fails or would pass the memory limit).
+  void Preallocate(std::size_t block_size, std::size_t count);
+  // One line of statistics on stderr.
+  void PrintStats() const;
   int Device() const { return device_; }
 
   // Size class a request of `bytes` is served from.

@@ -834,6 +834,33 @@ TEST_GPU(JitWrapperRoutesGemmThroughPlugin) {
   EXPECT_TRUE(std::memcmp(h1.data(), h2.data(), h1.size() * sizeof(float)) == 0);
 }
 
+// The reference pool's maintenance calls (memory_pool.hpp:93-111):
+// Preallocate fills the idle cache, TrimCache / Defragment / ReleaseAll hand
+// idle blocks back to the driver, PrintStats reports.
+TEST_GPU(MemoryPoolMaintenanceCalls) {
+  auto& pool = CudaMemoryPool::Instance();
+  pool.ReleaseAll();
+  pool.ResetStats();
+  const auto base = pool.GetStats().bytes_reserved;
+  pool.Preallocate(size_t(1) << 20, 3);
+  EXPECT_EQ(pool.GetStats().bytes_reserved, base + (size_t(3) << 20));
+  void* p = pool.Alloc(size_t(1) << 20);
+  EXPECT_TRUE(p != nullptr);
+  EXPECT_TRUE(pool.GetStats().cache_hits >= 1 && pool.GetStats().cache_misses == 3);
+  pool.Free(p, size_t(1) << 20);
+  EXPECT_TRUE(cudaDeviceSynchronize() == cudaSuccess);
+  pool.TrimCache();  // every last use has completed: all idle blocks go
+  EXPECT_EQ(pool.GetStats().bytes_reserved, base);
+  pool.Preallocate(4096, 2);
+  EXPECT_EQ(pool.GetStats().bytes_reserved, base + 2 * 4096);
+  pool.Defragment();
+  EXPECT_EQ(pool.GetStats().bytes_reserved, base);
+  pool.Preallocate(4096, 1);
+  pool.ReleaseAll();
+  EXPECT_EQ(pool.GetStats().bytes_reserved, base);
+  pool.PrintStats();
+}
+
 TEST_GPU(MemoryPoolReusesAndLimits) {
   auto& pool = CudaMemoryPool::Instance();
   pool.ResetStats();
