@@ -42,6 +42,10 @@ HardwareSpec QueryHardwareSpec() {
   hw.max_blocks_per_sm = p.maxBlocksPerMultiProcessor;
   hw.total_global_memory = p.totalGlobalMem;
   hw.memory_bus_width = p.memoryBusWidth;
+  int khz = 0;
+  if (cudaDeviceGetAttribute(&khz, cudaDevAttrMemoryClockRate, dev) == cudaSuccess) hw.memory_clock_rate = khz / 1000;
+  if (cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, dev) == cudaSuccess) hw.sm_clock_rate = khz / 1000;
+  cudaGetLastError();
   hw.supports_tensor_core = p.major >= 7;
   hw.supports_tma = p.major >= 9;
   hw.gpu_name = p.name;

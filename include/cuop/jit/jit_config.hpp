@@ -98,8 +98,9 @@ struct HardwareSpec {
   int max_threads_per_block = 0;
   int max_blocks_per_sm = 0;
   size_t total_global_memory = 0;
-  int memory_clock_rate = 0;
-  int memory_bus_width = 0;
+  int memory_clock_rate = 0;  // MHz
+  int memory_bus_width = 0;   // bits
+  int sm_clock_rate = 0;      // MHz (peak)
   bool supports_tensor_core = false;
   bool supports_tma = false;
   std::string gpu_name;
@@ -108,6 +109,14 @@ struct HardwareSpec {
   std::string GetComputeCapabilityString() const {
     return std::to_string(compute_capability_major) + "." + std::to_string(compute_capability_minor);
   }
+  // FP32 FFMA peak in GFLOP/s: SMs x FP32 lanes per SM (128 from compute
+  // capability 9.0 on, 64 before) x 2 FLOP per FMA x peak SM clock.
+  double GetTheoreticalPeakGFLOPS() const {
+    const double lanes = compute_capability_major >= 9 ? 128.0 : 64.0;
+    return num_sms * lanes * 2.0 * sm_clock_rate / 1000.0;
+  }
+  // DRAM bandwidth in GB/s: two transfers per memory clock across the bus.
+  double GetTheoreticalMemoryBandwidth() const { return memory_clock_rate * 2.0 * memory_bus_width / 8.0 / 1000.0; }
 };
 
 // Probe of the current device (empty spec when there is none).

@@ -138,6 +138,18 @@ TEST_HOST(CompileRequiresInitializeAndKnownKernelType) {
   EXPECT_TRUE(p.Execute(in, out) == StatusCode::NOT_COMPILED);
 }
 
+TEST_HOST(HardwareSpecTheoreticalPeaks) {  // B200: 148 SMs at 1965 MHz, 8192-bit HBM3e at 3996 MHz
+  HardwareSpec hw;
+  hw.compute_capability_major = 10;
+  hw.num_sms = 148;
+  hw.sm_clock_rate = 1965;
+  hw.memory_clock_rate = 3996;
+  hw.memory_bus_width = 8192;
+  EXPECT_NEAR(hw.GetTheoreticalPeakGFLOPS(), 148 * 128 * 2 * 1.965, 1e-6);
+  EXPECT_NEAR(hw.GetTheoreticalMemoryBandwidth(), 3996 * 2 * 1024 / 1000.0, 1e-6);
+  EXPECT_EQ(HardwareSpec().GetTheoreticalPeakGFLOPS(), 0.0);
+}
+
 TEST_HOST(MemoryPoolSizeClasses) {
   EXPECT_EQ(CudaMemoryPool::SizeClass(1), 256u);
   EXPECT_EQ(CudaMemoryPool::SizeClass(257), 512u);
@@ -837,6 +849,18 @@ TEST_GPU(JitWrapperRoutesGemmThroughPlugin) {
 // The reference pool's maintenance calls (memory_pool.hpp:93-111):
 // Preallocate fills the idle cache, TrimCache / Defragment / ReleaseAll hand
 // idle blocks back to the driver, PrintStats reports.
+TEST_GPU(HardwareProbeFillsClocks) {
+  const HardwareSpec hw = QueryHardwareSpec();
+  EXPECT_EQ(hw.compute_capability_major, 10);
+  EXPECT_TRUE(hw.num_sms >= 100 && hw.sm_clock_rate > 1000 && hw.memory_clock_rate > 1000);
+  const double gbs = hw.GetTheoreticalMemoryBandwidth(), gflops = hw.GetTheoreticalPeakGFLOPS();
+  std::printf("    %s: %d SMs, %d MHz SM, %d MHz x %d-bit memory -> %.0f GB/s, %.0f FP32 GFLOP/s\n",
+              hw.gpu_name.c_str(), hw.num_sms, hw.sm_clock_rate, hw.memory_clock_rate, hw.memory_bus_width, gbs,
+              gflops);
+  EXPECT_TRUE(gbs > 4000 && gbs < 12000);  // HBM3e-class
+  EXPECT_TRUE(gflops > 40000 && gflops < 120000);
+}
+
 TEST_GPU(MemoryPoolMaintenanceCalls) {
   auto& pool = CudaMemoryPool::Instance();
   pool.ReleaseAll();
