@@ -116,6 +116,8 @@ class Status {
   void SetDetails(const std::string& d) { info_.details = d; }
   explicit operator bool() const { return IsSuccess(); }
   std::string ToString() const;
+  // ToString plus the details, one field per line.
+  std::string ToDetailedString() const;
 
  private:
   StatusCode code_ = StatusCode::SUCCESS;
@@ -130,6 +132,25 @@ inline Status Error(StatusCode code, const std::string& message, const std::stri
 }
 Status CudaError(cudaError_t err, const std::string& function = "", const std::string& file = "", int line = 0);
 std::string GetStatusCodeString(StatusCode code);
+// One-sentence description of a code for messages and logs.
+std::string GetErrorDescription(StatusCode code);
+// Critical: the device or process state may be damaged (CUDA device,
+// context or launch failures, memory corruption); stop using the GPU path.
+bool IsCriticalError(StatusCode code);
+// Recoverable: the call can be retried or corrected by the caller (bad
+// arguments or shapes, memory pressure, time-outs, unsupported requests).
+bool IsRecoverableError(StatusCode code);
+// Status objects of one category, with a message and the call site.
+Status SystemError(const std::string& message, const std::string& function = "", const std::string& file = "",
+                   int line = 0);
+Status ValidationError(const std::string& message, const std::string& function = "", const std::string& file = "",
+                       int line = 0);
+Status MemoryError(const std::string& message, const std::string& function = "", const std::string& file = "",
+                   int line = 0);
+Status CompilationError(const std::string& message, const std::string& function = "", const std::string& file = "",
+                        int line = 0);
+Status ExecutionError(const std::string& message, const std::string& function = "", const std::string& file = "",
+                      int line = 0);
 }  // namespace ErrorUtils
 
 }  // namespace cu_op_mem

@@ -108,6 +108,31 @@ TEST_HOST(StatusCodesMatchReferenceValues) {
   EXPECT_TRUE(s.ToString().find("INVALID_ARGUMENT") != std::string::npos);
 }
 
+TEST_HOST(ErrorUtilsClassifyAndDescribe) {
+  using namespace ErrorUtils;
+  EXPECT_TRUE(IsRecoverableError(StatusCode::INVALID_ARGUMENT) && !IsCriticalError(StatusCode::INVALID_ARGUMENT));
+  EXPECT_TRUE(IsRecoverableError(StatusCode::SHAPE_MISMATCH));
+  EXPECT_TRUE(IsRecoverableError(StatusCode::OUT_OF_MEMORY) && IsRecoverableError(StatusCode::EXECUTION_TIMEOUT));
+  EXPECT_TRUE(IsRecoverableError(StatusCode::NOT_COMPILED));
+  EXPECT_TRUE(IsCriticalError(StatusCode::CUDA_ERROR) && !IsRecoverableError(StatusCode::CUDA_ERROR));
+  EXPECT_TRUE(IsCriticalError(StatusCode::CUDA_LAUNCH_FAILED));
+  EXPECT_TRUE(!IsCriticalError(StatusCode::CUDA_OUT_OF_MEMORY) && IsRecoverableError(StatusCode::CUDA_OUT_OF_MEMORY));
+  EXPECT_TRUE(!IsCriticalError(StatusCode::SUCCESS) && !IsRecoverableError(StatusCode::SUCCESS));
+  // no code is both
+  for (int v : {0, 1000, 1003, 2000, 2013, 3001, 4001, 5000, 6002, 7003, 8002, 9001, 10002, 11001})
+    EXPECT_TRUE(!(IsCriticalError(static_cast<StatusCode>(v)) && IsRecoverableError(static_cast<StatusCode>(v))));
+  EXPECT_TRUE(GetErrorDescription(StatusCode::TENSOR_SHAPE_MISMATCH).rfind("TENSOR_SHAPE_MISMATCH: ", 0) == 0);
+  const Status v = ValidationError("K differs", "Gemm::Forward", "gemm.cpp", 42);
+  EXPECT_TRUE(v.GetCode() == StatusCode::VALIDATION_ERROR && v.GetCategory() == ErrorCategory::VALIDATION);
+  EXPECT_TRUE(MemoryError("x").GetCategory() == ErrorCategory::MEMORY);
+  EXPECT_TRUE(ExecutionError("x").GetCategory() == ErrorCategory::EXECUTION);
+  EXPECT_TRUE(CompilationError("x").GetCategory() == ErrorCategory::COMPILATION);
+  EXPECT_TRUE(SystemError("x").GetCategory() == ErrorCategory::SYSTEM);
+  const std::string d = v.ToDetailedString();
+  EXPECT_TRUE(d.find("VALIDATION_ERROR (4000)") != std::string::npos && d.find("K differs") != std::string::npos &&
+              d.find("gemm.cpp:42") != std::string::npos);
+}
+
 TEST_HOST(BlasPluginManagerRegistersEveryOperatorName) {
   RegisterBlasJITPlugins();
   for (const char* n : {"gemm", "Gemm", "gemv", "Gemv", "gemm_batched", "GemmBatched", "batched_gemm",
