@@ -13,6 +13,7 @@
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
 
+#include <random>
 #include <sstream>
 #include <stdexcept>
 #include <string>
@@ -176,6 +177,20 @@ PYBIND11_MODULE(core, m) {
     t.fill(1.0f);
     return t;
   });
+  // Normal(mean, std) samples (the reference's binding fills with `mean`
+  // only); `seed` < 0 draws a fresh seed.
+  m.def(
+      "randn",
+      [](const std::vector<std::size_t>& shape, float mean, float stddev, long long seed) {
+        Tensor<float> t(shape);
+        std::mt19937_64 gen(seed < 0 ? std::random_device{}() : static_cast<std::uint64_t>(seed));
+        std::normal_distribution<float> dist(mean, stddev);
+        std::vector<float> h(t.numel());
+        for (auto& v : h) v = dist(gen);
+        if (!h.empty()) t.copy_from_host(h.data());
+        return t;
+      },
+      py::arg("shape"), py::arg("mean") = 0.0f, py::arg("std") = 1.0f, py::arg("seed") = -1);
   m.def("get_device_count", []() {
     int n = 0;
     if (cudaGetDeviceCount(&n) != cudaSuccess) {

@@ -11,7 +11,7 @@ from .core import (  # noqa: F401
     AxpyDouble, AxpyFloat, BatchMatMulDouble, BatchMatMulFloat, CopyDouble, CopyFloat, DotDouble, DotFloat,
     GemmDouble, GemmFloat, GemvDouble, GemvFloat, GlobalJITConfig, JITConfig, JITGemmFloat, JITGemvFloat,
     MatMulDouble, MatMulFloat, PerformanceProfile, ScalDouble, ScalFloat, TensorDouble, TensorFloat, empty_cache,
-    get_device, get_device_count, get_memory_info, ones, set_device, synchronize, tensor, zeros,
+    get_device, get_device_count, get_memory_info, ones, randn, set_device, synchronize, tensor, zeros,
 )
 
 Tensor = TensorFloat

@@ -108,3 +108,13 @@ def test_double_and_errors(cuop):
         g2.forward(bad, cuop.zeros([3, 4]))  # K mismatch: SHAPE_MISMATCH -> RuntimeError
     with pytest.raises(RuntimeError):
         cuop.DotDouble().forward(cuop.TensorDouble([4]), cuop.TensorDouble([4]))  # fp64 vector ops: unsupported
+
+
+def test_randn_is_normal_and_seeded(cuop):
+    t = cuop.randn([256, 512], 0.5, 2.0, seed=7)
+    a = t.to_numpy()
+    assert a.shape == (256, 512)
+    assert abs(a.mean() - 0.5) < 0.05 and abs(a.std() - 2.0) < 0.05
+    np.testing.assert_array_equal(cuop.randn([256, 512], 0.5, 2.0, seed=7).to_numpy(), a)
+    assert not np.array_equal(cuop.randn([256, 512], 0.5, 2.0, seed=8).to_numpy(), a)
+    assert cuop.randn([3]).size() == 3
