@@ -6,6 +6,9 @@
 #include <fstream>
 #include <random>
 #include <sstream>
+#include <thread>
+
+#include <cuda_runtime.h>
 
 namespace cu_op_mem {
 
@@ -82,8 +85,15 @@ std::vector<ParameterSet> AutoTuner::candidate_sets(const TuningConfig& cfg) con
 }
 
 TuningResult AutoTuner::Tune(const std::string& operator_name, BenchmarkFunction benchmark_func) {
+  struct Active {
+    std::atomic<int>& n;
+    explicit Active(std::atomic<int>& c) : n(c) { ++n; }
+    ~Active() { --n; }
+  } active(active_);
   TuningConfig cfg = GetTuningConfig();
   TuningResult r;
+  auto last_report = std::chrono::steady_clock::now();
+  bool stopped = false;
   r.tuning_start_time = std::chrono::high_resolution_clock::now();
   std::vector<ParameterSet> sets = candidate_sets(cfg);
   if (cfg.tuning_strategy == "random") {
@@ -94,6 +104,10 @@ TuningResult AutoTuner::Tune(const std::string& operator_name, BenchmarkFunction
   std::size_t since_improvement = 0;
   bool have = false;
   for (std::size_t i = 0; i < limit && benchmark_func; ++i) {
+    if (stop_.load()) {
+      stopped = true;
+      break;
+    }
     const double v = benchmark_func(sets[i]);
     r.performance_history.push_back(v);
     r.parameter_history.push_back(sets[i]);
@@ -109,8 +123,15 @@ TuningResult AutoTuner::Tune(const std::string& operator_name, BenchmarkFunction
       r.converged = true;
       break;
     }
+    if (monitoring_.load()) {
+      const auto now = std::chrono::steady_clock::now();
+      if (now - last_report >= std::chrono::milliseconds(monitor_ms_.load())) {
+        last_report = now;
+        notify(r);
+      }
+    }
   }
-  if (r.iterations_used == limit) r.converged = true;
+  if (r.iterations_used == limit && !stopped) r.converged = true;
   r.convergence_rate = sets.empty() ? 0.0 : static_cast<double>(r.iterations_used) / static_cast<double>(sets.size());
   r.tuning_end_time = std::chrono::high_resolution_clock::now();
   std::ostringstream sum;
@@ -122,7 +143,76 @@ TuningResult AutoTuner::Tune(const std::string& operator_name, BenchmarkFunction
     history_.push_back(r);
   }
   if (!cfg.result_save_path.empty()) SaveTuningHistory(cfg.result_save_path);
+  notify(r);
   return r;
+}
+
+TuningResult AutoTuner::TuneAsync(const std::string& operator_name, BenchmarkFunction benchmark_func) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    dev = -1;
+  }
+  TuningResult r;
+  std::thread worker([&] {
+    if (dev >= 0 && cudaSetDevice(dev) != cudaSuccess) cudaGetLastError();
+    r = Tune(operator_name, benchmark_func);
+  });
+  worker.join();
+  return r;
+}
+
+void AutoTuner::RegisterCallback(std::function<void(const TuningResult&)> callback) {
+  if (!callback) return;
+  std::lock_guard<std::mutex> lk(mu_);
+  callbacks_.push_back(std::move(callback));
+}
+
+void AutoTuner::notify(const TuningResult& r) {
+  std::vector<std::function<void(const TuningResult&)>> cbs;
+  {
+    std::lock_guard<std::mutex> lk(mu_);
+    cbs = callbacks_;
+  }
+  for (const auto& cb : cbs) cb(r);
+}
+
+namespace {
+std::string format_params(const ParameterSet& p, const char* sep) {
+  std::vector<std::pair<std::string, std::string>> kv(p.begin(), p.end());
+  std::sort(kv.begin(), kv.end());
+  std::string out;
+  for (const auto& e : kv) {
+    if (!out.empty()) out += sep;
+    out += e.first + "=" + e.second;
+  }
+  return out;
+}
+}  // namespace
+
+std::string AutoTuner::GenerateTuningReport(const TuningResult& r) const {
+  std::ostringstream o;
+  const double secs = std::chrono::duration<double>(r.tuning_end_time - r.tuning_start_time).count();
+  o << "Tuning report\n"
+    << "  summary:     " << r.optimization_summary << "\n"
+    << "  best:        " << r.best_performance << "  [" << format_params(r.best_parameters, ", ") << "]\n"
+    << "  evaluations: " << r.iterations_used << (r.converged ? " (converged)" : " (stopped early)") << "\n"
+    << "  wall time:   " << secs << " s\n";
+  if (!r.performance_history.empty()) {
+    const auto mm = std::minmax_element(r.performance_history.begin(), r.performance_history.end());
+    o << "  range:       " << *mm.first << " .. " << *mm.second << "\n";
+  }
+  for (const auto& rec : r.recommendations) o << "  note:        " << rec << "\n";
+  return o.str();
+}
+
+void AutoTuner::ExportResults(const TuningResult& r, const std::string& filename) const {
+  std::ofstream f(filename);
+  f << "iteration,performance,parameters\n";
+  for (std::size_t i = 0; i < r.performance_history.size(); ++i) {
+    f << i << ',' << r.performance_history[i] << ",\""
+      << (i < r.parameter_history.size() ? format_params(r.parameter_history[i], ";") : std::string()) << "\"\n";
+  }
 }
 
 // History file: one block per result,
@@ -178,6 +268,8 @@ void AutoTuner::Reset() {
   std::lock_guard<std::mutex> lk(mu_);
   config_ = TuningConfig{};
   history_.clear();
+  callbacks_.clear();
+  stop_.store(false);
 }
 
 }  // namespace cu_op_mem

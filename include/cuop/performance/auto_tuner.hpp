@@ -14,6 +14,7 @@
 // reference's StartTuning/StopTuning loop is not part of this library.
 #pragma once
 
+#include <atomic>
 #include <chrono>
 #include <cstddef>
 #include <functional>
@@ -88,6 +89,29 @@ class AutoTuner {
   // The result is appended to the history (and saved to
   // config.result_save_path when set).
   TuningResult Tune(const std::string& operator_name, BenchmarkFunction benchmark_func);
+  // Tune on a worker thread (the benchmark callbacks run there, with the
+  // caller's current CUDA device made current first).  The reference's
+  // signature returns the result, so this call waits for it; StopTuning()
+  // from another thread ends it after the evaluation in progress.
+  TuningResult TuneAsync(const std::string& operator_name, BenchmarkFunction benchmark_func);
+
+  // StopTuning() makes running Tune calls return after their current
+  // evaluation (result marked not converged); StartTuning() re-arms.
+  // IsTuning(): a Tune call is in progress.
+  void StartTuning() { stop_.store(false); }
+  void StopTuning() { stop_.store(true); }
+  bool IsTuning() const { return active_.load() > 0; }
+
+  // Human-readable report, and a CSV of every evaluation
+  // (iteration, performance, parameters as name=value;...).
+  std::string GenerateTuningReport(const TuningResult& result) const;
+  void ExportResults(const TuningResult& result, const std::string& filename) const;
+
+  // Callbacks get each finished result; with real-time monitoring on they
+  // also get the partial result during Tune, at most once per interval.
+  void RegisterCallback(std::function<void(const TuningResult&)> callback);
+  void EnableRealTimeMonitoring(bool enable) { monitoring_.store(enable); }
+  void SetMonitoringInterval(int interval_ms) { monitor_ms_.store(interval_ms < 0 ? 0 : interval_ms); }
 
   void SaveTuningHistory(const std::string& filename) const;
   void LoadTuningHistory(const std::string& filename);
@@ -98,9 +122,16 @@ class AutoTuner {
   bool better(double a, double b) const;  // is a better than b
   std::vector<ParameterSet> candidate_sets(const TuningConfig& cfg) const;
 
+  void notify(const TuningResult& r);
+
   mutable std::mutex mu_;
   TuningConfig config_;
   std::vector<TuningResult> history_;
+  std::vector<std::function<void(const TuningResult&)>> callbacks_;
+  std::atomic<bool> stop_{false};
+  std::atomic<int> active_{0};
+  std::atomic<bool> monitoring_{false};
+  std::atomic<int> monitor_ms_{1000};
 };
 
 }  // namespace cu_op_mem

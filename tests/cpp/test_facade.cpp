@@ -9,6 +9,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <fstream>
 #include <functional>
 #include <string>
 #include <vector>
@@ -325,6 +326,53 @@ TEST_GPU(ShapeMismatchIsReported) {
   Tensor<float> x({3}), y({4});
   v.SetWeight(x);
   EXPECT_TRUE(v.Forward(A, y) == StatusCode::SHAPE_MISMATCH);
+}
+
+TEST_HOST(AutoTunerAsyncStopCallbacksAndReports) {
+  AutoTuner t;
+  TuningConfig cfg;
+  cfg.optimization_target = "throughput";
+  t.SetTuningConfig(cfg);
+  t.AddParameter(ParameterDefinition{"a", ParameterType::INTEGER, "", {"1", "2", "3", "4"}, "1"});
+  std::vector<size_t> seen;
+  t.RegisterCallback([&](const TuningResult& r) { seen.push_back(r.iterations_used); });
+  auto score = [](const ParameterSet& p) { return std::stod(p.at("a")); };
+  EXPECT_TRUE(!t.IsTuning());
+  TuningResult r = t.TuneAsync("toy", score);  // runs on a worker thread, waits for it
+  EXPECT_TRUE(r.best_parameters.at("a") == "4" && r.iterations_used == 4 && r.converged);
+  EXPECT_TRUE(seen.size() == 1 && seen[0] == 4);
+  // monitoring with a zero interval: one partial report per evaluation, then the final one
+  t.EnableRealTimeMonitoring(true);
+  t.SetMonitoringInterval(0);
+  seen.clear();
+  t.Tune("toy", score);
+  EXPECT_EQ(seen.size(), size_t(5));
+  t.EnableRealTimeMonitoring(false);
+  // StopTuning from inside the benchmark: the evaluation in progress finishes, no more start
+  int calls = 0;
+  bool tuning_seen = false;
+  r = t.Tune("toy", [&](const ParameterSet& p) {
+    tuning_seen = t.IsTuning();
+    if (++calls == 2) t.StopTuning();
+    return score(p);
+  });
+  EXPECT_TRUE(tuning_seen && calls == 2 && r.iterations_used == 2 && !r.converged);
+  EXPECT_TRUE(!t.IsTuning());
+  t.StartTuning();
+  EXPECT_EQ(t.Tune("toy", score).iterations_used, size_t(4));
+  const std::string rep = t.GenerateTuningReport(r);
+  EXPECT_TRUE(rep.find("a=2") != std::string::npos && rep.find("stopped early") != std::string::npos);
+  const std::string path = "/tmp/cuop_autotuner_export.csv";
+  t.ExportResults(r, path);
+  std::ifstream f(path);
+  std::string line, all;
+  int lines = 0;
+  while (std::getline(f, line)) {
+    all += line + "\n";
+    ++lines;
+  }
+  EXPECT_EQ(lines, 3);
+  EXPECT_TRUE(all.rfind("iteration,performance,parameters\n0,1,\"a=1\"\n1,2,\"a=2\"", 0) == 0);
 }
 
 TEST_HOST(AutoTunerGridRandomEarlyStopAndHistory) {
