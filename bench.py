@@ -43,8 +43,8 @@ FP32_SIMT_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
 SPEC_HBM_GBS = 8000.0
 SPEC_DENSE_16BIT_TFLOPS = 2250.0
 
-# DRAM bytes per launch from the ncu capture summarised in
-# profiles/gemv_f32_8192_ncu.md (dram__bytes_read.sum + dram__bytes_write.sum).
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one
+# ncu capture of the two fp32 GEMV kernels at 8192 x 8192.
 NCU_TRAFFIC_BYTES = {"gemv_t_lsu": 272088832, "gemv_n_xreg": 272280576}
 
 
