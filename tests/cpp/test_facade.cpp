@@ -11,6 +11,9 @@
 #include <cstring>
 #include <fstream>
 #include <functional>
+#include <memory>
+#include <set>
+#include <stdexcept>
 #include <string>
 #include <vector>
 
@@ -348,7 +351,9 @@ TEST_HOST(AutoTunerAsyncStopCallbacksAndReports) {
   t.Tune("toy", score);
   EXPECT_EQ(seen.size(), size_t(5));
   t.EnableRealTimeMonitoring(false);
-  // StopTuning from inside the benchmark: the evaluation in progress finishes, no more start
+  // StopTuning from inside the benchmark: the evaluation in progress
+  // finishes, no further one starts, and IsTuning() reports the flag.
+  t.StartTuning();
   int calls = 0;
   bool tuning_seen = false;
   r = t.Tune("toy", [&](const ParameterSet& p) {
@@ -358,7 +363,8 @@ TEST_HOST(AutoTunerAsyncStopCallbacksAndReports) {
   });
   EXPECT_TRUE(tuning_seen && calls == 2 && r.iterations_used == 2 && !r.converged);
   EXPECT_TRUE(!t.IsTuning());
-  t.StartTuning();
+  // The stop ended only the call that was running: a later Tune runs in full
+  // without StartTuning (as in the reference, Tune ignores the flag).
   EXPECT_EQ(t.Tune("toy", score).iterations_used, size_t(4));
   const std::string rep = t.GenerateTuningReport(r);
   EXPECT_TRUE(rep.find("a=2") != std::string::npos && rep.find("stopped early") != std::string::npos);
@@ -373,6 +379,140 @@ TEST_HOST(AutoTunerAsyncStopCallbacksAndReports) {
   }
   EXPECT_EQ(lines, 3);
   EXPECT_TRUE(all.rfind("iteration,performance,parameters\n0,1,\"a=1\"\n1,2,\"a=2\"", 0) == 0);
+}
+
+// test/performance/test_performance_monitor.cpp:296-304 (AutoTunerBasic).
+TEST_HOST(AutoTunerBasicStartStop) {
+  auto& tuner = AutoTuner::Instance();
+  EXPECT_TRUE(!tuner.IsTuning());
+  tuner.StartTuning();
+  EXPECT_TRUE(tuner.IsTuning());
+  tuner.StopTuning();
+  EXPECT_TRUE(!tuner.IsTuning());
+}
+
+// test/performance/test_performance_monitor.cpp:352-388 (SimpleTuning): the
+// parameter is added before a config without parameters is set; Tune uses it.
+TEST_HOST(AutoTunerSimpleTuningSequence) {
+  AutoTuner t;
+  ParameterDefinition param;
+  param.name = "test_param";
+  param.type = ParameterType::INTEGER;
+  param.values = {"1", "2", "3"};
+  param.default_value = "2";
+  param.is_tunable = true;
+  t.AddParameter(param);
+  TuningConfig config;
+  config.operator_name = "test_operator";
+  config.max_iterations = 5;
+  config.convergence_threshold = 0.1;
+  config.improvement_threshold = 0.05;
+  t.SetTuningConfig(config);
+  auto r = t.Tune("test_operator", [](const ParameterSet& p) {
+    auto it = p.find("test_param");
+    return it != p.end() ? std::stod(it->second) : 0.0;
+  });
+  EXPECT_TRUE(r.iterations_used > 0 && r.best_performance > 0 && !r.best_parameters.empty());
+  EXPECT_TRUE(r.best_parameters.at("test_param") == "3");
+  EXPECT_EQ(t.GetParameters().size(), size_t(1));
+  t.RemoveParameter("test_param");
+  EXPECT_EQ(t.GetParameters().size(), size_t(0));
+}
+
+// Every strategy name of the reference (auto_tuner.cu:195-216) and its short
+// form selects that strategy, which then runs: the result names it, no set is
+// evaluated twice, the budget holds, and with a budget as large as the space
+// every strategy finds the best set.  An unknown name is refused, not ignored.
+TEST_HOST(AutoTunerEveryReferenceStrategyRuns) {
+  const std::vector<std::string> names = {"GridSearch", "RandomSearch", "BayesianOptimization", "GeneticAlgorithm"};
+  const std::vector<std::string> aliases = {"grid", "random", "bayesian", "genetic"};
+  AutoTuner t;
+  {
+    auto avail = t.GetAvailableStrategies();
+    EXPECT_TRUE(avail == names);
+  }
+  t.AddParameter(ParameterDefinition{"tile", ParameterType::INTEGER, "", {"32", "64", "128", "256", "512", "1024"}, "128"});
+  t.AddParameter(ParameterDefinition{"stages", ParameterType::ENUM, "", {"2", "3", "4"}, "3"});
+  ParameterDefinition fixed{"dtype", ParameterType::STRING, "", {}, "bf16"};
+  fixed.is_tunable = false;
+  t.AddParameter(fixed);
+  // Best at tile=256, stages=3: 30 - |log2(tile) - 8| * 3 - |stages - 3|.
+  auto score = [](const ParameterSet& p) {
+    EXPECT_TRUE(p.at("dtype") == "bf16");
+    const double lt = std::log2(std::stod(p.at("tile")));
+    return 30.0 - std::fabs(lt - 8.0) * 3.0 - std::fabs(std::stod(p.at("stages")) - 3.0);
+  };
+  for (size_t i = 0; i < names.size(); ++i) {
+    for (const std::string& nm : {names[i], aliases[i]}) {
+      t.SetTuningStrategy(nm);
+      EXPECT_TRUE(t.GetCurrentStrategy() == names[i]);
+      for (size_t budget : {size_t(7), size_t(100)}) {
+        TuningConfig cfg = t.GetTuningConfig();
+        cfg.max_iterations = budget;
+        cfg.tuning_strategy.clear();  // keep the strategy just selected
+        t.SetTuningConfig(cfg);
+        TuningResult r = t.Tune("toy", score);
+        EXPECT_TRUE(r.strategy_name == names[i]);
+        EXPECT_TRUE(r.optimization_summary.find(names[i]) != std::string::npos);
+        EXPECT_TRUE(r.iterations_used <= std::min<size_t>(budget, 18) && r.iterations_used >= 1);
+        std::set<std::string> distinct;
+        for (const auto& ps : r.parameter_history) distinct.insert(ps.at("tile") + "/" + ps.at("stages"));
+        EXPECT_EQ(distinct.size(), r.parameter_history.size());
+        const double best_seen = *std::max_element(r.performance_history.begin(), r.performance_history.end());
+        EXPECT_NEAR(r.best_performance, best_seen, 0.0);
+        if (budget == 100) {
+          EXPECT_EQ(r.iterations_used, size_t(18));
+          EXPECT_TRUE(r.converged);
+          EXPECT_TRUE(r.best_parameters.at("tile") == "256" && r.best_parameters.at("stages") == "3");
+        }
+      }
+    }
+  }
+  t.SetTuningStrategy("Annealing");
+  EXPECT_TRUE(t.GetCurrentStrategy() == "GeneticAlgorithm");
+  EXPECT_TRUE(t.GetLastError().find("Annealing") != std::string::npos);
+  TuningConfig bad = t.GetTuningConfig();
+  bad.tuning_strategy = "Tabu";
+  t.SetTuningConfig(bad);
+  EXPECT_TRUE(t.GetCurrentStrategy() == "GeneticAlgorithm" && t.GetLastError().find("Tabu") != std::string::npos);
+  // The strategy classes of the reference header are usable on their own.
+  TuningConfig space;
+  space.parameters = t.GetParameters();
+  GridSearchStrategy grid;
+  auto sets = grid.GenerateParameterSets(space, 100);
+  EXPECT_EQ(sets.size(), size_t(18));
+  EXPECT_TRUE(sets[0].at("tile") == "32" && sets[0].at("stages") == "2" && sets[1].at("stages") == "3");
+  std::unique_ptr<ITuningStrategy> s = MakeTuningStrategy("BayesianOptimization");
+  EXPECT_TRUE(s && s->GetStrategyName() == "BayesianOptimization");
+  EXPECT_TRUE(!MakeTuningStrategy("Annealing"));
+  // Predictions: a measured set returns its measurement.
+  ParameterSet best{{"tile", "256"}, {"stages", "3"}, {"dtype", "bf16"}};
+  EXPECT_NEAR(t.PredictPerformance(best), 30.0, 0.0);
+  EXPECT_TRUE(!t.GetPerformanceInsights().empty());
+}
+
+// A benchmark call that throws is recorded as 0.0 and the run goes on
+// (auto_tuner.cu:159-163); the failure never becomes the best.
+TEST_HOST(AutoTunerBenchmarkExceptionIsRecorded) {
+  AutoTuner t;
+  TuningConfig cfg;
+  cfg.optimization_target = "latency";
+  t.SetTuningConfig(cfg);
+  t.AddParameter(ParameterDefinition{"v", ParameterType::ENUM, "", {"a", "b", "c"}, "a"});
+  int calls = 0;
+  TuningResult r = t.Tune("toy", [&](const ParameterSet& p) -> double {
+    ++calls;
+    if (p.at("v") == "b") throw std::runtime_error("kernel refused");
+    return p.at("v") == "a" ? 5.0 : 3.0;
+  });
+  EXPECT_EQ(calls, 3);
+  EXPECT_EQ(r.iterations_used, size_t(3));
+  EXPECT_TRUE(r.performance_history.size() == 3 && r.performance_history[1] == 0.0);
+  EXPECT_TRUE(r.best_parameters.at("v") == "c");  // 0.0 from the failure is not the best latency
+  EXPECT_NEAR(r.best_performance, 3.0, 0.0);
+  bool noted = false;
+  for (const auto& rec : r.recommendations) noted |= rec.find("kernel refused") != std::string::npos;
+  EXPECT_TRUE(noted);
 }
 
 TEST_HOST(AutoTunerGridRandomEarlyStopAndHistory) {
