@@ -109,6 +109,7 @@ constexpr double kTcMinWork = 64.0 * 64.0 * 64.0;
 // (unless the FFMA mode is selected).
 constexpr double kTf32x3MinWork = 256.0 * 256.0 * 256.0;
 std::atomic<int> g_fp32_mode{CUOPX_FP32_AUTO};
+int fp32_mode() { return g_fp32_mode.load(std::memory_order_relaxed); }
 
 // Runs variant `v` when it can take `p`; -1 when it cannot (the caller then
 // makes the built-in choice).  In a non-default fp32 mode, variants of the
@@ -173,6 +174,24 @@ int validate_gemm(const GemmProblem& p) {
     if (overlaps(p.C, c_span, p.A, a_span) || overlaps(p.C, c_span, p.B, b_span)) return CUOPX_INVALID_ARGUMENT;
   }
   return -1;  // proceed
+}
+
+// Argument checks of every GEMV entry point: a status to return, or -1 to
+// proceed (M == 0 succeeds with nothing to do).
+int validate_gemv(int dtype, int trans, int64_t M, int64_t N, const void* A, int64_t lda, const void* x,
+                  const void* y) {
+  if (dtype_size(dtype) == 0) return CUOPX_UNSUPPORTED_TYPE;
+  if (M < 0 || N < 0) return CUOPX_INVALID_ARGUMENT;
+  if (M == 0) return CUOPX_SUCCESS;
+  if (y == nullptr) return CUOPX_INVALID_ARGUMENT;
+  if (N > 0) {
+    if (A == nullptr || x == nullptr) return CUOPX_INVALID_ARGUMENT;
+    if (lda < (trans ? M : N)) return CUOPX_INVALID_ARGUMENT;
+    const size_t es = dtype_size(dtype);
+    const size_t a_span = trans ? span_bytes(N, M, lda, es) : span_bytes(M, N, lda, es);
+    if (overlaps(y, M * es, A, a_span) || overlaps(y, M * es, x, N * es)) return CUOPX_INVALID_ARGUMENT;
+  }
+  return -1;
 }
 
 }  // namespace cuopx
@@ -259,17 +278,8 @@ size_t cuopx_gemv_workspace_size(int dtype, int trans, int64_t M, int64_t N) {
 int cuopx_gemv(int dtype, int trans, int64_t M, int64_t N, double alpha, const void* A, int64_t lda, const void* x,
                double beta, void* y, void* workspace, size_t workspace_bytes, void* stream) {
   ApiScope scope("cuopx_gemv", M, N, trans);
-  if (dtype_size(dtype) == 0) return scope.done(CUOPX_UNSUPPORTED_TYPE);
-  if (M < 0 || N < 0) return scope.done(CUOPX_INVALID_ARGUMENT);
-  if (M == 0) return scope.done(CUOPX_SUCCESS);
-  if (y == nullptr) return scope.done(CUOPX_INVALID_ARGUMENT);
-  if (N > 0) {
-    if (A == nullptr || x == nullptr) return scope.done(CUOPX_INVALID_ARGUMENT);
-    if (lda < (trans ? M : N)) return scope.done(CUOPX_INVALID_ARGUMENT);
-    const size_t es = dtype_size(dtype);
-    const size_t a_span = trans ? span_bytes(N, M, lda, es) : span_bytes(M, N, lda, es);
-    if (overlaps(y, M * es, A, a_span) || overlaps(y, M * es, x, N * es)) return scope.done(CUOPX_INVALID_ARGUMENT);
-  }
+  const int v = validate_gemv(dtype, trans, M, N, A, lda, x, y);
+  if (v >= 0) return scope.done(v);
   return scope.done(gemv_dispatch(dtype, trans, M, N, alpha, A, lda, x, beta, y, workspace, workspace_bytes,
                                   static_cast<cudaStream_t>(stream)));
 }

@@ -413,6 +413,21 @@ __device__ __forceinline__ __nv_bfloat16 from_acc<__nv_bfloat16>(float v) {
   return __float2bfloat16_rn(v);
 }
 
+// alpha*acc + beta*c exactly as the reference's kernels compute
+// `alpha * sum + beta * C` (src/cuda_op/detail/cuBlas/gemm.cu:41, gemv.cu:21):
+// beta*c rounded, then one fused multiply-add with alpha*acc.  (Measured on
+// B200 against the reference built from its sources: this form reproduces
+// every output bit; rounding alpha*acc separately does not when alpha != 1
+// and beta != 0.)  With beta == 0, C is not read: the rounded alpha*acc.
+__device__ __forceinline__ float epi_axpby(float alpha, float acc, float beta, float c) {
+  return __fmaf_rn(alpha, acc, __fmul_rn(beta, c));
+}
+__device__ __forceinline__ double epi_axpby(double alpha, double acc, double beta, double c) {
+  return __fma_rn(alpha, acc, __dmul_rn(beta, c));
+}
+__device__ __forceinline__ float epi_scale(float alpha, float acc) { return __fmul_rn(alpha, acc); }
+__device__ __forceinline__ double epi_scale(double alpha, double acc) { return __dmul_rn(alpha, acc); }
+
 // Fused GEMM epilogue, applied to alpha*acc (+ beta*C) before the one
 // rounding to the output type: + bias[col] (rounded add, never contracted
 // with the product), then ReLU(x) = x if x > 0 else +0 (NaN -> +0).

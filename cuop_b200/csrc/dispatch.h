@@ -20,8 +20,13 @@ void note_launch(const char* name);
 
 // cudaGetLastError -> CUOPX_SUCCESS / CUOPX_CUDA_ERROR.
 int check_launch();
+// Process-wide fp32 arithmetic mode (cuopx_set_fp32_gemm_mode).
+int fp32_mode();
 
 // ---- GEMV (gemv.cu) ----
+// Argument checks shared by the GEMV entry points (capi.cu): a status, or -1 to proceed.
+int validate_gemv(int dtype, int trans, int64_t M, int64_t N, const void* A, int64_t lda, const void* x,
+                  const void* y);
 size_t gemv_workspace_size(int dtype, int trans, int64_t M, int64_t N);
 int gemv_dispatch(int dtype, int trans, int64_t M, int64_t N, double alpha, const void* A, int64_t lda,
                   const void* x, double beta, void* y, void* ws, size_t ws_bytes, cudaStream_t stream);

@@ -10,11 +10,11 @@
 //   outputs per thread.
 //
 // Both accumulate every output as one fused-multiply-add chain over k in
-// ascending order, then apply C = alpha*acc (+ beta*C, unfused; then the
-// optional bias add and ReLU of cuopx_gemm_ex) — the
-// reference kernels' summation order (src/cuda_op/detail/cuBlas/gemm.cu:23-41,
-// gemm.cu:264-291) — so fp32 results are reproducible bit for bit by a CPU
-// loop doing the same fmaf chain.
+// ascending order, then apply C = fma(alpha, acc, beta*C) (alpha*acc when
+// beta == 0; then the optional bias add and ReLU of cuopx_gemm_ex) — the
+// reference kernels' summation order and epilogue (src/cuda_op/detail/cuBlas/
+// gemm.cu:23-41, gemm.cu:264-291) — so fp32 results reproduce the reference's
+// own kernels, and a CPU loop doing the same fmaf chain, bit for bit.
 #include "common.cuh"
 #include "dispatch.h"
 
@@ -27,15 +27,7 @@ __device__ __forceinline__ typename AccOf<T>::type epilogue_value(typename AccOf
                                                                   typename AccOf<T>::type alpha,
                                                                   typename AccOf<T>::type beta, const T* c) {
   using Acc = typename AccOf<T>::type;
-  Acc r;
-  if constexpr (sizeof(Acc) == 8) {
-    r = __dmul_rn(alpha, acc);
-    if (beta != Acc(0)) r = __dadd_rn(r, __dmul_rn(beta, to_acc<T>(*c)));
-  } else {
-    r = __fmul_rn(alpha, acc);
-    if (beta != Acc(0)) r = __fadd_rn(r, __fmul_rn(beta, to_acc<T>(*c)));
-  }
-  return r;
+  return beta != Acc(0) ? epi_axpby(alpha, acc, beta, to_acc<T>(*c)) : epi_scale(alpha, acc);
 }
 
 // ---------------------------------------------------------------------------

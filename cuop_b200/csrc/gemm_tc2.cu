@@ -540,15 +540,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
         float v[64];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          v[i] = p.alpha * __uint_as_float(r0[i]);
-          v[32 + i] = p.alpha * __uint_as_float(r1[i]);
+          v[i] = __uint_as_float(r0[i]);
+          v[32 + i] = __uint_as_float(r1[i]);
         }
         if (p.beta != 0.f && grow < p.M) {
           const int64_t gcol0 = static_cast<int64_t>(n0) + ch * P_CHUNK;
           const T* crow = Cin + static_cast<int64_t>(b) * p.strideC + grow * p.ldc;
 #pragma unroll
           for (int i = 0; i < 64; ++i)
-            if (gcol0 + i < p.N) v[i] = __fadd_rn(v[i], __fmul_rn(p.beta, to_acc<T>(crow[gcol0 + i])));
+            v[i] = gcol0 + i < p.N ? epi_axpby(p.alpha, v[i], p.beta, to_acc<T>(crow[gcol0 + i]))
+                                   : epi_scale(p.alpha, v[i]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) v[i] = epi_scale(p.alpha, v[i]);
         }
         if (p.epi) {
           const int64_t gcol0 = static_cast<int64_t>(n0) + ch * P_CHUNK;

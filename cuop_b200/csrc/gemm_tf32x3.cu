@@ -395,13 +395,16 @@ __global__ void __launch_bounds__(X3_THREADS, 1)
         }
         float v[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __fmul_rn(p.alpha, __uint_as_float(r[i]));
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
         if (p.beta != 0.f && grow < p.M) {
           const int64_t gcol0 = static_cast<int64_t>(n0) + ch * X3_CHUNK;
           const float* crow = p.C_in + static_cast<int64_t>(b) * p.strideC + grow * p.ldc;
 #pragma unroll
           for (int i = 0; i < 32; ++i)
-            if (gcol0 + i < p.N) v[i] = __fadd_rn(v[i], __fmul_rn(p.beta, crow[gcol0 + i]));
+            v[i] = gcol0 + i < p.N ? epi_axpby(p.alpha, v[i], p.beta, crow[gcol0 + i]) : epi_scale(p.alpha, v[i]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = epi_scale(p.alpha, v[i]);
         }
         if (p.epi) {
           const int64_t gcol0 = static_cast<int64_t>(n0) + ch * X3_CHUNK;

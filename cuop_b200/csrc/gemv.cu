@@ -48,9 +48,8 @@ __device__ __forceinline__ void unpack16(const uint4& v, typename AccOf<T>::type
 template <typename T>
 __device__ __forceinline__ void store_y(T* y, int64_t i, typename AccOf<T>::type acc, typename AccOf<T>::type alpha,
                                         typename AccOf<T>::type beta) {
-  typename AccOf<T>::type r = alpha * acc;
-  if (beta != typename AccOf<T>::type(0)) r += beta * to_acc<T>(y[i]);
-  y[i] = from_acc<T>(r);
+  using Acc = typename AccOf<T>::type;
+  y[i] = from_acc<T>(beta != Acc(0) ? epi_axpby(alpha, acc, beta, to_acc<T>(y[i])) : epi_scale(alpha, acc));
 }
 
 template <typename Acc>
@@ -113,6 +112,30 @@ __global__ void __launch_bounds__(256) gemv_n_rows(int64_t M, int64_t N, typenam
   if (row >= M) return;
   auto acc = warp_row_dot<T, VECTOR>(A + row * lda, x, 0, N, lane);
   if (lane == 0) store_y<T>(y, row, acc, alpha, beta);
+}
+
+// ---------------------------------------------------------------------------
+// Reference-order GEMV (fp32/fp64 in CUOPX_FP32_FFMA mode): one thread per
+// output, whose fma chain runs over j = 0..N-1 in ascending order, then the
+// reference's epilogue — the arithmetic of the reference's gemv_kernel
+// (src/cuda_op/detail/cuBlas/gemv.cu:10-23), so its results are reproduced
+// bit for bit.  Exactness, not bandwidth, is the point of this kernel.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256) gemv_ordered(int trans, int64_t M, int64_t N, typename AccOf<T>::type alpha,
+                                                    const T* __restrict__ A, int64_t lda, const T* __restrict__ x,
+                                                    typename AccOf<T>::type beta, T* __restrict__ y) {
+  using Acc = typename AccOf<T>::type;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= M) return;
+  Acc s = 0;
+  if (trans) {
+    for (int64_t j = 0; j < N; ++j) s = fma(to_acc<T>(A[j * lda + i]), to_acc<T>(x[j]), s);
+  } else {
+    const T* row = A + i * lda;
+    for (int64_t j = 0; j < N; ++j) s = fma(to_acc<T>(row[j]), to_acc<T>(x[j]), s);
+  }
+  store_y<T>(y, i, s, alpha, beta);
 }
 
 // ---------------------------------------------------------------------------
@@ -352,6 +375,14 @@ int launch_gemv(int trans, int64_t M, int64_t N, double alpha_d, const void* A_,
   const T* x = static_cast<const T*>(x_);
   T* y = static_cast<T*>(y_);
   const Acc alpha = static_cast<Acc>(alpha_d), beta = static_cast<Acc>(beta_d);
+  if constexpr (sizeof(Acc) == sizeof(T)) {  // fp32 / fp64 in FFMA mode: the reference's order
+    if (fp32_mode() == CUOPX_FP32_FFMA) {
+      gemv_ordered<T><<<static_cast<unsigned>((M + 255) / 256), 256, 0, stream>>>(trans, M, N, alpha, A, lda, x,
+                                                                                    beta, y);
+      note_launch("gemv_ordered");
+      return check_launch();
+    }
+  }
   // Streaming kernels (gemv_stream.cu) first; the kernels below cover the
   // shapes and alignments they do not take.
   const int rs = launch_gemv_stream<T>(trans, M, N, alpha_d, A_, lda, x_, beta_d, y_, ws, ws_bytes, kCounterBytes,

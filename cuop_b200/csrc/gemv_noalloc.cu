@@ -72,6 +72,8 @@ size_t scratch_for_call(int trans, int64_t M, int64_t N, int64_t lda, const void
 }
 
 size_t noalloc_need(int dtype, int trans, int64_t M, int64_t N, int64_t lda, const void* A, const void* x) {
+  // fp32/fp64 in FFMA mode run gemv_ordered, which needs no scratch.
+  if ((dtype == CUOPX_F32 || dtype == CUOPX_F64) && fp32_mode() == CUOPX_FP32_FFMA) return 0;
   switch (dtype) {
     case CUOPX_F32: return scratch_for_call<float>(trans, M, N, lda, A, x);
     case CUOPX_F64: return scratch_for_call<double>(trans, M, N, lda, A, x);
@@ -88,15 +90,16 @@ size_t noalloc_need(int dtype, int trans, int64_t M, int64_t N, int64_t lda, con
 extern "C" int cuopx_gemv_noalloc(int dtype, int trans, int64_t M, int64_t N, double alpha, const void* A,
                                   int64_t lda, const void* x, double beta, void* y, void* stream) {
   using namespace cuopx;
-  if (dtype_size(dtype) == 0) return CUOPX_UNSUPPORTED_TYPE;
-  if (M < 0 || N < 0) return CUOPX_INVALID_ARGUMENT;
-  if (M == 0) return CUOPX_SUCCESS;
+  ApiScope scope("cuopx_gemv_noalloc", M, N, trans);
+  // The same argument checks as cuopx_gemv, before the scratch is sized.
+  const int v = validate_gemv(dtype, trans, M, N, A, lda, x, y);
+  if (v >= 0) return scope.done(v);
   const size_t need = N > 0 ? noalloc_need(dtype, trans, M, N, lda, A, x) : 0;
-  if (need > kNoAllocScratchBytes) return CUOPX_RESOURCE_UNAVAILABLE;
+  if (need > kNoAllocScratchBytes) return scope.done(CUOPX_RESOURCE_UNAVAILABLE);
   void* scratch = nullptr;
   const int rc = noalloc_scratch(&scratch);
-  if (rc != CUOPX_SUCCESS) return rc;
+  if (rc != CUOPX_SUCCESS) return scope.done(rc);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (need > 0 && cudaMemsetAsync(scratch, 0, kCounterBytes, s) != cudaSuccess) return CUOPX_CUDA_ERROR;
-  return cuopx_gemv(dtype, trans, M, N, alpha, A, lda, x, beta, y, scratch, kNoAllocScratchBytes, stream);
+  if (need > 0 && cudaMemsetAsync(scratch, 0, kCounterBytes, s) != cudaSuccess) return scope.done(CUOPX_CUDA_ERROR);
+  return scope.done(gemv_dispatch(dtype, trans, M, N, alpha, A, lda, x, beta, y, scratch, kNoAllocScratchBytes, s));
 }

@@ -167,9 +167,7 @@ __global__ void __launch_bounds__(GS_THREADS, 2)
     Acc s = part[rr][0];
 #pragma unroll
     for (int w = 1; w < GS_WARPS; ++w) s += part[rr][w];
-    Acc res = alpha * s;
-    if (beta != Acc(0)) res += beta * to_acc<T>(y[r0 + rr]);
-    y[r0 + rr] = from_acc<T>(res);
+    y[r0 + rr] = from_acc<T>(beta != Acc(0) ? epi_axpby(alpha, s, beta, to_acc<T>(y[r0 + rr])) : epi_scale(alpha, s));
   }
 }
 
@@ -267,9 +265,8 @@ __global__ void __launch_bounds__(GS_THREADS, 2)
     if (ph == 0 && has) {
 #pragma unroll
       for (int i = 0; i < V; ++i) {
-        Acc res = alpha * acc[i];
-        if (beta != Acc(0)) res += beta * to_acc<T>(y[col + i]);
-        y[col + i] = from_acc<T>(res);
+        y[col + i] =
+            from_acc<T>(beta != Acc(0) ? epi_axpby(alpha, acc[i], beta, to_acc<T>(y[col + i])) : epi_scale(alpha, acc[i]));
       }
     }
     return;
@@ -338,9 +335,8 @@ __global__ void __launch_bounds__(GS_THREADS, 2)
       for (int i = 0; i < V; ++i) sum[i] += s_phase[q][cv * V + i];
 #pragma unroll
     for (int i = 0; i < V; ++i) {
-      Acc res = alpha * sum[i];
-      if (beta != Acc(0)) res += beta * to_acc<T>(y[col + i]);
-      y[col + i] = from_acc<T>(res);
+      y[col + i] =
+          from_acc<T>(beta != Acc(0) ? epi_axpby(alpha, sum[i], beta, to_acc<T>(y[col + i])) : epi_scale(alpha, sum[i]));
     }
   }
   if (tid == 0) counters[blockIdx.x] = 0u;

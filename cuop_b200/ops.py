@@ -141,6 +141,91 @@ def batched_gemm(A: torch.Tensor, B: torch.Tensor, C: Optional[torch.Tensor] = N
     return C
 
 
+class _HostStreamer:
+    """Device staging for batched_gemm_host on one device: `slots` chunk
+    buffers for A, B and C, a host-to-device and a device-to-host copy
+    stream, and one event per slot and stage.  Kept between calls (a call
+    after the first allocates nothing)."""
+
+    def __init__(self, device: torch.device, dtype: torch.dtype, chunk: int, shapes, slots: int):
+        (m, k), (k2, n) = shapes
+        self.key = (device, dtype, chunk, m, k, n, slots)
+        self.slots = slots
+        self.dA = [torch.empty((chunk, m, k), dtype=dtype, device=device) for _ in range(slots)]
+        self.dB = [torch.empty((chunk, k2, n), dtype=dtype, device=device) for _ in range(slots)]
+        self.dC = [torch.empty((chunk, m, n), dtype=dtype, device=device) for _ in range(slots)]
+        self.h2d = torch.cuda.Stream(device)
+        self.d2h = torch.cuda.Stream(device)
+        self.loaded = [torch.cuda.Event() for _ in range(slots)]
+        self.computed = [torch.cuda.Event() for _ in range(slots)]
+        self.stored = [torch.cuda.Event() for _ in range(slots)]
+
+
+_streamers: dict = {}
+
+
+def batched_gemm_host(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, *, alpha: float = 1.0, beta: float = 0.0,
+                      device: Optional[torch.device] = None, chunk: Optional[int] = None,
+                      slots: int = 3) -> torch.Tensor:
+    """C_b = alpha * A_b B_b + beta * C_b for PINNED HOST tensors [batch, ...]:
+    the batch streams through `device` (default: the current one) in chunks.
+    The host-to-device copy of chunk i+1, the batched GEMM of chunk i
+    (cuopx_gemm_strided_batched on the current stream) and the device-to-host
+    copy of chunk i-1 overlap, each copy direction on its own stream, so both
+    PCIe directions and the GPU are busy at once.  Returns after C holds the
+    result (the host has waited for the last copy).  The reference's
+    BatchMatMul<T>::Forward (src/cuda_op/detail/cuDNN/batchmatmul.cu:52-94)
+    takes device tensors; this is the same product for data that starts and
+    ends in host memory."""
+    for t, nm in ((A, "A"), (B, "B"), (C, "C")):
+        if t.is_cuda or not t.is_pinned() or not t.is_contiguous() or t.dim() != 3:
+            raise N.CuopError(N.INVALID_ARGUMENT, f"batched_gemm_host: {nm} must be a contiguous 3-D pinned host tensor")
+    if not (A.dtype == B.dtype == C.dtype):
+        raise N.CuopError(N.UNSUPPORTED_TYPE, "batched_gemm_host: A, B and C must share a dtype")
+    batch, M, K = A.shape
+    if B.size(0) != batch or B.size(1) != K or tuple(C.shape) != (batch, M, B.size(2)):
+        raise N.CuopError(N.SHAPE_MISMATCH, "batched_gemm_host: shape mismatch")
+    if batch == 0:
+        return C
+    dev = device or torch.device("cuda", torch.cuda.current_device())
+    per_batch = (M * K + K * B.size(2) + M * B.size(2)) * A.element_size()
+    if chunk is None:  # about 16 chunks, each moving at least 4 MiB
+        chunk = max(1, min(batch, max((4 << 20) // per_batch, -(-batch // 16))))
+    key = (dev, A.dtype, chunk, M, K, B.size(2), slots)
+    st = _streamers.get(key)
+    if st is None:
+        st = _HostStreamer(dev, A.dtype, chunk, ((M, K), (K, B.size(2))), slots)
+        _streamers[key] = st
+    comp = torch.cuda.current_stream(dev)
+    last = None
+    with torch.cuda.device(dev):
+        for c, b0 in enumerate(range(0, batch, chunk)):
+            b1 = min(batch, b0 + chunk)
+            n, s = b1 - b0, c % slots
+            with torch.cuda.stream(st.h2d):
+                if c >= slots:
+                    st.h2d.wait_event(st.computed[s])  # the GEMM of chunk c - slots has read this slot
+                st.dA[s][:n].copy_(A[b0:b1], non_blocking=True)
+                st.dB[s][:n].copy_(B[b0:b1], non_blocking=True)
+                if beta != 0.0:
+                    if c >= slots:
+                        st.h2d.wait_event(st.stored[s])  # and its C has left the slot
+                    st.dC[s][:n].copy_(C[b0:b1], non_blocking=True)
+                st.loaded[s].record(st.h2d)
+            comp.wait_event(st.loaded[s])
+            if c >= slots:
+                comp.wait_event(st.stored[s])
+            batched_gemm(st.dA[s][:n], st.dB[s][:n], st.dC[s][:n], alpha=alpha, beta=beta, stream=comp)
+            st.computed[s].record(comp)
+            with torch.cuda.stream(st.d2h):
+                st.d2h.wait_event(st.computed[s])
+                C[b0:b1].copy_(st.dC[s][:n], non_blocking=True)
+                st.stored[s].record(st.d2h)
+            last = st.stored[s]
+    last.synchronize()
+    return C
+
+
 def gemv(A: torch.Tensor, x: torch.Tensor, y: Optional[torch.Tensor] = None, *, trans: bool = False,
          alpha: float = 1.0, beta: float = 0.0, stream=None) -> torch.Tensor:
     """y = alpha * op(A) x + beta * y.

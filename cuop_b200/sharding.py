@@ -32,7 +32,17 @@ class CollectiveError(RuntimeError):
     """A collective of the column-sharded path did not complete: a rank died,
     left, or did not join within the process group's timeout.  `status` is
     cuOP's TIMEOUT StatusCode value.  The process group is unusable after
-    it: destroy it and build a new one before the next sharded call."""
+    it: destroy it and build a new one before the next sharded call.
+
+    This is raised where the backend reports the failure to the caller,
+    which is what a gloo process group does (tested with a rank that never
+    joins).  An NCCL process group normally does not: its watchdog thread
+    notices the timed-out collective and aborts the whole process (torch's
+    TORCH_NCCL_ASYNC_ERROR_HANDLING default), so no exception reaches this
+    code.  A caller that wants the error on NCCL instead has to turn that
+    handling off (TORCH_NCCL_ASYNC_ERROR_HANDLING=0, or 2 to only clean up)
+    and then finds hung ranks by their own timeout; this path is not tested
+    on NCCL."""
 
     status = _native.TIMEOUT
 

@@ -72,9 +72,13 @@ int cuopx_clear_device_error(void);
  *     rows run 3xTF32 on the tensor cores (hi*hi + hi*lo + lo*hi, fp32
  *     accumulate; meets ||C-R||_F/||R||_F <= 1e-5*sqrt(K), not bit-identical
  *     to an FFMA loop); the rest run FFMA.
- *   CUOPX_FP32_FFMA: always FFMA, one fma chain per output in ascending k —
- *     the summation order of the reference's kernels (gemm.cu:23-41), so
- *     results reproduce a CPU loop in that order bit for bit.
+ *   CUOPX_FP32_FFMA: always FFMA, one fma chain per output in ascending k,
+ *     then fma(alpha, sum, beta*C) — the summation order and epilogue of the
+ *     reference's kernels (gemm.cu:23-41, 264-291).  fp32 and fp64 GEMV then
+ *     also run one ascending fma chain per output (gemv.cu:10-23).  Results
+ *     reproduce the reference's own Gemm<float> (every kernel its selector
+ *     picks for untransposed operands) and its Gemv<float> for shapes its
+ *     gemv_kernel serves, bit for bit; the GPU tests run both side by side.
  *   CUOPX_FP32_TF32X3: 3xTF32 at every size it supports.
  * No reference counterpart (the reference has only FFMA kernels).
  */

@@ -17,9 +17,15 @@
  *              and src/jit/Blas/gemm_batched_jit_plugin.cu:324-330 (with
  *              alpha/beta, strides strideA/B/C).
  * Every output is one fused multiply-add chain over k in ascending order
- * (nvcc contracts `sum += a*b` into FFMA), then r = alpha*sum, and, only when
- * beta != 0, r = r + beta*c (unfused).  fp16/bf16 inputs are widened to fp32
- * exactly, accumulated in fp32, and the result rounded once to nearest-even.
+ * (nvcc contracts `sum += a*b` into FFMA), then the epilogue
+ * `alpha * sum + beta * C` (gemm.cu:41, gemv.cu:21) the way nvcc builds it:
+ * r = fma(alpha, sum, round(beta*c)) when beta != 0, else round(alpha*sum)
+ * (C is not read).  That form was pinned by running the reference's own
+ * kernels on a B200 with alpha = 0.7, beta = 1.3: it matched every output
+ * bit, while rounding alpha*sum separately, or fma(beta, c, alpha*sum), did
+ * not (tests/test_reference_bitexact_gpu.py keeps that check).  fp16/bf16
+ * inputs are widened to fp32 exactly, accumulated in fp32, and the result
+ * rounded once to nearest-even.
  *
  * Build: oracle/Makefile (gcc -O3 -march=x86-64-v3 -fopenmp -ffp-contract=off).
  */
@@ -32,6 +38,11 @@
 #endif
 
 #define ORACLE_API __attribute__((visibility("default")))
+
+/* The reference's epilogue alpha*sum + beta*c (see the header comment). */
+static inline float axpby_f32(float alpha, float sum, float beta, float c) {
+  return beta != 0.0f ? fmaf(alpha, sum, beta * c) : alpha * sum;
+}
 
 /* ------------------------------------------------------------------ RNG --
  * Counter-based splitmix64: element i of a tensor with seed s is
@@ -155,11 +166,7 @@ ORACLE_API void oracle_gemm_f32(int transA, int transB, int64_t M, int64_t N, in
         }
       }
       float* crow = C + i * ldc;
-      for (int64_t j = 0; j < N; ++j) {
-        float r = alpha * acc[j];
-        if (beta != 0.0f) r = r + beta * crow[j];
-        crow[j] = r;
-      }
+      for (int64_t j = 0; j < N; ++j) crow[j] = axpby_f32(alpha, acc[j], beta, crow[j]);
     }
     free(acc);
   }
@@ -180,11 +187,7 @@ ORACLE_API void oracle_gemm_f64(int transA, int transB, int64_t M, int64_t N, in
         for (int64_t j = 0; j < N; ++j) acc[j] = fma(a, transB ? B[j * ldb + k] : B[k * ldb + j], acc[j]);
       }
       double* crow = C + i * ldc;
-      for (int64_t j = 0; j < N; ++j) {
-        double r = alpha * acc[j];
-        if (beta != 0.0) r = r + beta * crow[j];
-        crow[j] = r;
-      }
+      for (int64_t j = 0; j < N; ++j) crow[j] = beta != 0.0 ? fma(alpha, acc[j], beta * crow[j]) : alpha * acc[j];
     }
     free(acc);
   }
@@ -245,8 +248,7 @@ ORACLE_API void oracle_gemm_lowp_ex(int dtype, int transA, int transB, int64_t M
         uint16_t* crow = C + (i0 + r) * ldc;
         const float* ar = acc + r * N;
         for (int64_t j = 0; j < N; ++j) {
-          float v = alpha * ar[j];
-          if (beta != 0.0f) v = v + beta * lowp_to_f32(dtype, crow[j]);
+          float v = beta != 0.0f ? axpby_f32(alpha, ar[j], beta, lowp_to_f32(dtype, crow[j])) : alpha * ar[j];
           if (epi & 1) v = v + lowp_to_f32(dtype, bias[j]);
           if (epi & 2) v = v > 0.0f ? v : 0.0f;
           crow[j] = f32_to_lowp(dtype, v);
@@ -319,9 +321,7 @@ ORACLE_API void oracle_gemv_f32(int trans, int64_t M, int64_t N, float alpha, co
       const float* arow = A + i * lda;
       float s = 0.0f;
       for (int64_t j = 0; j < N; ++j) s = fmaf(arow[j], x[j], s);
-      float r = alpha * s;
-      if (beta != 0.0f) r = r + beta * y[i];
-      y[i] = r;
+      y[i] = axpby_f32(alpha, s, beta, y[i]);
     }
   } else {
     /* Each thread owns a contiguous range of outputs and walks every row of A
@@ -342,11 +342,7 @@ ORACLE_API void oracle_gemv_f32(int trans, int64_t M, int64_t N, float alpha, co
         const float xj = x[j];
         for (int64_t i = i0; i < i1; ++i) acc[i] = fmaf(arow[i], xj, acc[i]);
       }
-      for (int64_t i = i0; i < i1; ++i) {
-        float r = alpha * acc[i];
-        if (beta != 0.0f) r = r + beta * y[i];
-        y[i] = r;
-      }
+      for (int64_t i = i0; i < i1; ++i) y[i] = axpby_f32(alpha, acc[i], beta, y[i]);
     }
     free(acc);
   }

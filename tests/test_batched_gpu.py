@@ -98,3 +98,31 @@ def test_shared_b_stride_zero(dev, fp32_ffma):
     assert rc == 0
     ref = O.gemm_batched_f32(A32, np.broadcast_to(B32, (batch, K, Nn)).copy())
     np.testing.assert_array_equal(C.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("beta", [0.0, 0.5])
+def test_batched_gemm_host_streams_pinned_buffers(dev, beta):
+    """The host-buffer form (chunks streamed through the GPU, copies in both
+    directions overlapped with the GEMMs) returns exactly the device call's
+    bits, for a batch that is not a multiple of the chunk, twice in a row
+    (the second call reuses the staging buffers)."""
+    batch, M, N, K = 1000, 128, 128, 64
+    for call in range(2):
+        g = torch.Generator().manual_seed(40 + call)
+        A = torch.randn(batch, M, K, generator=g).bfloat16().pin_memory()
+        B = torch.randn(batch, K, N, generator=g).bfloat16().pin_memory()
+        C0 = torch.randn(batch, M, N, generator=g).bfloat16()
+        C = C0.clone().pin_memory()
+        cx.batched_gemm_host(A, B, C, beta=beta, chunk=96)
+        Cd = C0.to(dev)
+        cx.batched_gemm(A.to(dev), B.to(dev), Cd, beta=beta)
+        torch.cuda.synchronize()
+        assert torch.equal(C, Cd.cpu()), call
+
+
+def test_batched_gemm_host_refuses_device_or_pageable_tensors(dev):
+    A = torch.zeros(2, 8, 8, dtype=torch.bfloat16)
+    with pytest.raises(cx.CuopError):
+        cx.batched_gemm_host(A, A.clone(), A.clone())  # pageable host memory
+    with pytest.raises(cx.CuopError):
+        cx.batched_gemm_host(A.to(dev), A.to(dev), A.to(dev))

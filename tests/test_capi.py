@@ -68,6 +68,14 @@ def test_argument_validation_without_gpu():
     # gemv: lda < N, y overlapping x
     assert L.cuopx_gemv(N.F32, 0, 4, 8, 1.0, 4096, 4, 8192, 0.0, 16384, None, 0, None) == N.INVALID_ARGUMENT
     assert L.cuopx_gemv(N.F32, 0, 4, 4, 1.0, 4096, 4, 8192, 0.0, 8192, None, 0, None) == N.INVALID_ARGUMENT
+    # the allocation-free GEMV runs the same checks before it sizes its scratch: the bf16
+    # transposed 8191 x 8192 shape (whose kernel would need more than its scratch) with
+    # lda < M is an invalid argument, not a resource shortage; and a null y as well
+    M, Nn = 8191, 8192
+    A, x, y = 1 << 32, 2 << 32, 3 << 32  # far apart, never dereferenced
+    assert L.cuopx_gemv_noalloc(N.BF16, 1, M, Nn, 1.0, A, M - 1, x, 0.0, y, None) == N.INVALID_ARGUMENT
+    assert L.cuopx_gemv_noalloc(N.BF16, 1, M, Nn, 1.0, A, M, x, 0.0, None, None) == N.INVALID_ARGUMENT
+    assert L.cuopx_gemv_noalloc(99, 1, M, Nn, 1.0, A, M, x, 0.0, y, None) == N.UNSUPPORTED_TYPE
     # vector ops
     assert L.cuopx_axpy(-1, 1.0, 16, 1, 32, 1, None) == N.INVALID_ARGUMENT
     assert L.cuopx_axpy(4, 1.0, 16, 0, 32, 1, None) == N.INVALID_ARGUMENT

@@ -44,12 +44,13 @@ def test_f32_bit_exact_vs_oracle(dev, fp32_ffma, M, N, K, tA, tB):
     A = O.uniform((K, M) if tA else (M, K), seed=M + 1)
     B = O.uniform((N, K) if tB else (K, N), seed=N + 2)
     C0 = O.uniform((M, N), seed=3)
-    ref = O.gemm_f32(A, B, C0, transA=tA, transB=tB, alpha=0.5, beta=2.0)
-    C = cx.gemm(to_dev_f32(A, dev), to_dev_f32(B, dev), to_dev_f32(C0, dev), transA=tA, transB=tB, alpha=0.5,
-                beta=2.0)
+    # alpha, beta not powers of two: any other epilogue rounding shows in the last bit
+    al, be = float(np.float32(0.7)), float(np.float32(1.3))
+    ref = O.gemm_f32(A, B, C0, transA=tA, transB=tB, alpha=al, beta=be)
+    C = cx.gemm(to_dev_f32(A, dev), to_dev_f32(B, dev), to_dev_f32(C0, dev), transA=tA, transB=tB, alpha=al, beta=be)
     got = C.cpu().numpy()
     np.testing.assert_array_equal(got, ref, err_msg=cx.last_kernel())
-    exact = 0.5 * ((A.T if tA else A).astype(np.float64) @ (B.T if tB else B).astype(np.float64)) + 2.0 * C0
+    exact = al * ((A.T if tA else A).astype(np.float64) @ (B.T if tB else B).astype(np.float64)) + be * C0
     assert O.rel_frobenius(got, exact) <= 1e-5 * np.sqrt(K)
 
 
