@@ -1,20 +1,30 @@
 #!/usr/bin/env python
 """Benchmark of the cuop_b200 dense BLAS hot path on B200.
 
-Headline workload (one JSON line, rank 0): fp32 GEMV, y = 1.0*A*x + 0.0*y with
-A 8192 x 8192 row-major, plus the transposed (A^T x) variant; A, x uniform
-[-1, 1).  One step = one plain + one transposed GEMV on a fresh input set
-(4 sets of 256 MiB rotated, so every A read comes from HBM, not the 126 MB
-L2).  Metric: HBM GB/s of algorithmic traffic (A once, x once, y written once
-per GEMV).  The GEMV path does not shard, so `--gpus N` runs N replicas.
+Headline (one JSON line, rank 0): bf16 strided-batched GEMM, 4096 batches of
+C[128x128] = A[128x64] B[64x128] (fp32 accumulate, bf16 out, inputs N(0,1)),
+sharded by batch over the N ranks with no collective: rank r runs batches
+[r*4096/N, (r+1)*4096/N).  The total work is fixed as N grows (strong
+scaling).  One step = one batched call per rank on a fresh input set (input
+sets rotated so that their total exceeds the 126 MB L2).  Metric: HBM GB/s of
+algorithmic traffic (A and B read once, C written once), whole job.
 
-The same line carries, under "configs", the other GEMM shapes of the path:
-fp32 GEMM 1024^3, fp16 GEMM 8192^3, bf16 batched 4096 x 128x128x64
-(batch-sharded, no collective), bf16 linear 4096 x 8192 x 28672.  At N>1 the
-two large GEMMs are column-sharded and the full output is assembled on every
-rank by the GEMM epilogue's own stores into the peers' outputs over NVLink
-(GEMM + NCCL all-gather + gather kernel is timed beside it).
-`--configs c3` (etc.) runs a subset of them.
+`e2e` is the same workload through the per-call public API with the data in
+pinned host memory: cuop_b200.batched_gemm_host streams each rank's shard
+host -> device -> host every step (both PCIe directions overlapped with the
+GEMMs) and returns when the host holds C.
+
+Under "configs" the same line carries the other shapes of the path, each with
+its clock record and a parity check:
+  c2  fp32 GEMV 8192^2, plain + transposed (replicas at N > 1), with its own
+      roofline, per-call e2e and CPU baseline;
+  c1  fp32 GEMM 1024^3 (replicas);
+  c3  fp16 GEMM 8192^3, column-sharded at N > 1 with the full output on
+      every rank (fused peer-store epilogue, and GEMM + NCCL all-gather);
+  c5  bf16 linear 4096 x 8192 x 28672, the same way.
+`--configs c3,c5` (etc.) runs a subset.  At N > 1 every sharded output is
+checked on every rank (complete sampled rows and columns against an fp32
+product, and a checksum all-gather showing every rank holds the same bytes).
 
 `--impl reference` times the reference path's CPU restatement (the
 reference has no CPU implementation of its own) on the host cores.
@@ -34,6 +44,10 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+# Headline workload (C4).
+BATCH, BM, BN, BK = 4096, 128, 128, 64
+C4_BYTES_PER_BATCH = (BM * BK + BK * BN + BM * BN) * 2
+C4_BYTES = BATCH * C4_BYTES_PER_BATCH  # 268,435,456
 GEMV_N = 8192
 GEMV_BYTES = (GEMV_N * GEMV_N + 2 * GEMV_N) * 4  # A + x + y (beta = 0: y not read)
 FALLBACK_HBM_GBS = 6650.0
@@ -42,10 +56,17 @@ FP32_SIMT_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
 # Nominal B200 figures, reported beside the measured-peak fractions.
 SPEC_HBM_GBS = 8000.0
 SPEC_DENSE_16BIT_TFLOPS = 2250.0
+LOWP_TOL = 1e-2
 
-# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one
-# ncu capture of the two fp32 GEMV kernels at 8192 x 8192.
-NCU_TRAFFIC_BYTES = {"gemv_t_lsu": 272088832, "gemv_n_xreg": 272280576}
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the
+# dominant kernels, from the ncu captures summarised in profiles/ (file
+# named beside each figure); per batch for the batched kernel.
+NCU_TRAFFIC = {
+    "gemm_tc_128x128_2cta": {"bytes_per_batch": None,  # filled from the capture of this kernel
+                        "source": "profiles/gemm_tc_bf16_batched_4096x128x128x64_ncu.md"},
+    "gemv_t_lsu": {"bytes": 272088832, "source": "profiles/gemv_f32_8192_ncu.md"},
+    "gemv_n_xreg": {"bytes": 272280576, "source": "profiles/gemv_f32_8192_ncu.md"},
+}
 
 
 # --------------------------------------------------------------------------- util
@@ -63,6 +84,16 @@ def load_peaks():
         except Exception:
             pass
     return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, None, "fallback"
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 class ClockSampler:
@@ -153,6 +184,19 @@ def max_over_ranks(v: float, world: int) -> float:
     return float(t.item())
 
 
+def all_gather_floats(vals, world: int):
+    """Every rank's list of floats, as a list per rank (collective)."""
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor(vals, dtype=torch.float64, device="cuda")
+    if world == 1:
+        return [t.tolist()]
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [o.tolist() for o in out]
+
+
 def capture_graph(fn, n):
     """CUDA graph of fn(0..n-1).  The launches inside are the library's own
     kernels through its public API; replaying the graph removes the host's
@@ -172,53 +216,332 @@ def capture_graph(fn, n):
     return g, cx.launch_count() - c0
 
 
-def time_graph(fn, steps, warmup, world, align=None):
+def time_graph(fn, steps, warmup, world, align=None, clock=None):
     """Device time (ms per call) of `steps` calls of fn replayed as one CUDA
     graph after `warmup` eager calls; max over ranks.  `align`, if given, is
     launched on the stream just before the timed replay (a cross-GPU barrier,
-    so that host-side skew between ranks stays out of the timed region)."""
+    so that host-side skew between ranks stays out of the timed region).
+    `clock` (a ClockSampler) samples the clocks during the timed replay."""
     import torch
+    from contextlib import nullcontext
 
     for i in range(warmup):
         fn(i)
-    g, _ = capture_graph(fn, steps)
+    g, launches = capture_graph(fn, steps)
     g.replay()  # first replay uploads the graph
     barrier(world)
     if align is not None:
         align()
     s = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(s)
-    g.replay()
-    e1.record(s)
-    torch.cuda.synchronize()
+    with (clock or nullcontext()):
+        e0.record(s)
+        g.replay()
+        e1.record(s)
+        torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
     barrier(world)
     del g
-    return max_over_ranks(ms, world)
+    return max_over_ranks(ms, world), launches
 
 
-def time_loop(fn, steps, warmup, world, stream=None):
+def time_loop(fn, steps, warmup, world, clock=None):
     """Eager device time (ms per call) of `steps` calls, max over ranks (used
     where a step holds NCCL collectives, which stay out of graphs)."""
     import torch
+    from contextlib import nullcontext
 
     for _ in range(warmup):
         fn(0)
     barrier(world)
-    s = stream or torch.cuda.current_stream()
+    s = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(s)
-    for i in range(steps):
-        fn(i)
-    e1.record(s)
-    torch.cuda.synchronize()
+    with (clock or nullcontext()):
+        e0.record(s)
+        for i in range(steps):
+            fn(i)
+        e1.record(s)
+        torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
     barrier(world)
     return max_over_ranks(ms, world)
 
 
-# --------------------------------------------------------------------------- GEMV (headline)
+def time_host_loop(fn, steps, warmup, world):
+    """Wall time (ms per call) of `steps` host-synchronous calls, max over
+    ranks: each call returns only when its results are in host memory."""
+    for i in range(warmup):
+        fn(i)
+    barrier(world)
+    t0 = time.perf_counter()
+    for i in range(steps):
+        fn(i)
+    ms = (time.perf_counter() - t0) * 1e3 / steps
+    barrier(world)
+    return max_over_ranks(ms, world)
+
+
+def fp32_product(a, b):
+    """Plain fp32 product (TF32 off) of widened operands on the GPU: the
+    reference for full-size checks, where the CPU oracle would take minutes."""
+    import torch
+
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        return a.float() @ b.float()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+def max_rel(got, ref) -> float:
+    """max|C - R| / max|R| (the fp16/bf16 bound is 1e-2)."""
+    den = float(ref.abs().max())
+    return float((got.float() - ref).abs().max()) / (den if den > 0 else 1.0)
+
+
+def checksum(t) -> list:
+    """Two position-weighted sums of a 2-D 16-bit tensor's bit patterns (row-
+    and column-weighted): equal on two ranks only if the bytes agree, with
+    overwhelming probability."""
+    import torch
+
+    v = t.contiguous().view(torch.int16).to(torch.int64)
+    rows = v.sum(dim=1)
+    cols = v.sum(dim=0)
+    wr = torch.arange(1, rows.numel() + 1, device=v.device, dtype=torch.int64)
+    wc = torch.arange(1, cols.numel() + 1, device=v.device, dtype=torch.int64)
+    return [float(int((rows * wr).sum()) % (1 << 52)), float(int((cols * wc).sum()) % (1 << 52))]
+
+
+# --------------------------------------------------------------------------- C4 (headline)
+def c4_inputs(dev, lb, seed):
+    import torch
+
+    per_set = lb * C4_BYTES_PER_BATCH
+    sets = max(2, math.ceil(400e6 / per_set))  # > 3x the 126 MB L2
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    As = [torch.randn(lb, BM, BK, device=dev, generator=g).bfloat16() for _ in range(sets)]
+    Bs = [torch.randn(lb, BK, BN, device=dev, generator=g).bfloat16() for _ in range(sets)]
+    Cs = [torch.empty(lb, BM, BN, device=dev, dtype=torch.bfloat16) for _ in range(sets)]
+    return As, Bs, Cs, sets
+
+
+def c4_parity(As, Bs, Cs, world):
+    """Each rank's shard against an fp32 product on 16 sampled batches of the
+    last rotation set computed; max over ranks."""
+    import torch
+
+    lb = As[0].size(0)
+    g = torch.Generator().manual_seed(5)
+    idx = sorted(set([0, lb - 1] + torch.randint(0, lb, (14,), generator=g).tolist()))
+    k = 0
+    err = 0.0
+    for b in idx:
+        ref = fp32_product(As[k][b], Bs[k][b])
+        err = max(err, max_rel(Cs[k][b], ref))
+    return {"max_rel": max_over_ranks(err, world), "tol": LOWP_TOL, "batches_checked_per_rank": len(idx),
+            "reference": "fp32 product (TF32 off) of the same bf16 inputs"}
+
+
+def run_c4(args, rank, world, local_rank):
+    import torch
+    import cuop_b200 as cx
+    from cuop_b200 import sharding
+
+    dev = torch.device("cuda", local_rank)
+    b0, b1 = sharding.shard_range(BATCH, rank, world)
+    lb = b1 - b0
+    As, Bs, Cs, sets = c4_inputs(dev, lb, seed=1000 + rank)
+
+    def step(i):
+        cx.batched_gemm(As[i % sets], Bs[i % sets], Cs[i % sets])
+
+    for i in range(args.warmup):
+        step(i)
+    barrier(world)
+    K = args.steps
+    g_step, launches = capture_graph(step, K)
+    kname = cx.last_kernel()
+    g_step.replay()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stream = torch.cuda.current_stream()
+    with ClockSampler(local_rank) as clk:
+        e0.record(stream)
+        g_step.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms_local = e0.elapsed_time(e1) / K
+    del g_step
+    barrier(world)
+    ms = max_over_ranks(ms_local, world)
+    for k in range(sets):  # outputs of every set, for the parity check below
+        cx.batched_gemm(As[k], Bs[k], Cs[k])
+    parity = c4_parity(As, Bs, Cs, world)
+
+    hbm, _, _, peak_src = load_peaks()
+    value = C4_BYTES / (ms * 1e-3) / 1e9
+    local_bytes = lb * C4_BYTES_PER_BATCH
+    achieved = local_bytes / (ms_local * 1e-3) / 1e9  # one launch per step on this rank
+    tr = NCU_TRAFFIC.get(kname, {})
+    traffic = tr["bytes_per_batch"] * lb if tr.get("bytes_per_batch") else None
+    line = {
+        "metric": "bf16 batched GEMM 4096 x (128x128x64), batch-sharded: HBM GB/s", "value": round(value, 2),
+        "unit": "GB/s", "n_gpus": world, "steps": K, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "bf16 strided-batched GEMM C[b] = A[b] B[b], batch 4096, M=N=128, K=64, "
+                               "A,B ~ N(0,1), fp32 accumulate, bf16 out", "global_batch": BATCH,
+                   "per_gpu_batch": lb, "parallelism": f"batch-sharded x{world}, no collective",
+                   "l2": f"inputs larger than L2: {sets} rotated input sets of {local_bytes / 1e6:.1f} MB per rank",
+                   "bytes_per_step": C4_BYTES},
+        "roofline": {"bound": "hbm", "kernel": kname, "achieved": round(achieved, 1), "peak": hbm,
+                     "peak_source": f"{peak_src} hbm_gbs (burst copy)", "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "frac_spec": round(achieved / SPEC_HBM_GBS, 4),
+                     "spec_peak": SPEC_HBM_GBS, "traffic": traffic, "traffic_source": tr.get("source"),
+                     "algorithmic_bytes": local_bytes, "per": "one launch on one GPU"},
+        "gpu_launches": launches,
+        "timing": "timed region = one CUDA graph replay of K steps (one batched launch per rank each)",
+        "clocks": clk.summary(),
+        "parity": parity,
+    }
+    line["e2e"] = c4_e2e(args, rank, world, local_rank, lb)
+    del As, Bs, Cs
+    torch.cuda.empty_cache()
+    return line
+
+
+def c4_e2e(args, rank, world, local_rank, lb):
+    """The same workload through the per-call public API with the data in
+    pinned host memory: every step, cuop_b200.batched_gemm_host copies this
+    rank's A and B shard in, runs the batched GEMM and copies C out (copies of
+    both directions overlapped with the GEMMs), returning when the host holds
+    C.  Two host input sets alternate.  Checked bit for bit against the device
+    call on the same inputs."""
+    import torch
+    import cuop_b200 as cx
+
+    dev = torch.device("cuda", local_rank)
+    g = torch.Generator().manual_seed(77 + rank)
+    hA = [torch.randn(lb, BM, BK, generator=g).bfloat16().pin_memory() for _ in range(2)]
+    hB = [torch.randn(lb, BK, BN, generator=g).bfloat16().pin_memory() for _ in range(2)]
+    hC = torch.empty(lb, BM, BN, dtype=torch.bfloat16).pin_memory()
+
+    cx.batched_gemm_host(hA[0], hB[0], hC)
+    dC = cx.batched_gemm(hA[0].to(dev), hB[0].to(dev))
+    torch.cuda.synchronize()
+    if not torch.equal(hC, dC.cpu()):
+        raise RuntimeError("batched_gemm_host result differs from the device call")
+    del dC
+
+    steps = max(5, min(args.steps, 50))
+    ms = time_host_loop(lambda i: cx.batched_gemm_host(hA[i % 2], hB[i % 2], hC), steps, 3, world)
+    return {"value": round(C4_BYTES / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": world * lb * (BM * BK + BK * BN) * 2,
+            "d2h_bytes_per_step": world * lb * BM * BN * 2, "per_rank_h2d_bytes": lb * (BM * BK + BK * BN) * 2,
+            "ms_per_step": round(ms, 4), "steps": steps,
+            "path": "cuop_b200.batched_gemm_host per step (one call per rank): pinned host A,B shard -> device in "
+                    "chunks, cuopx_gemm_strided_batched per chunk, C -> pinned host, host waits; wall clock, "
+                    "max over ranks"}
+
+
+# --------------------------------------------------------------------------- CPU baselines (oracle)
+def _timed(fn, budget_s, max_reps=20):
+    fn()  # page-in
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        fn()
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or reps >= max_reps:
+            return el / reps
+
+
+def cpu_c4_baseline(budget_s: float = 3.0):
+    """The oracle's batched bf16 GEMM (CPU restatement of the reference's
+    batched kernel arithmetic) on the C4 workload: all host threads on the
+    full 4096 batches, and one thread on a 256-batch slab."""
+    import oracle as O
+
+    nt = O.threads()
+    A = O.to_lowp(O.normal((BATCH, BM, BK), seed=4), O.BF16)
+    B = O.to_lowp(O.normal((BATCH, BK, BN), seed=5), O.BF16)
+    t = _timed(lambda: O.gemm_batched_lowp(O.BF16, A, B, nthreads=nt), budget_s)
+    slab = 256
+    t1 = _timed(lambda: O.gemm_batched_lowp(O.BF16, A[:slab], B[:slab], nthreads=1), budget_s)
+    return {"value": round(C4_BYTES / t / 1e9, 3), "unit": "GB/s", "cores": nt, "kind": "port",
+            "sample": f"full workload, 4096 x 128x128x64 bf16 batched GEMM in {t * 1e3:.0f} ms, oracle/cpu_ref.c, "
+                      f"OpenMP {nt} threads",
+            "single_thread": {"value": round(slab * C4_BYTES_PER_BATCH / t1 / 1e9, 3), "unit": "GB/s", "cores": 1,
+                              "sample": f"{slab}-batch slab in {t1 * 1e3:.0f} ms"},
+            "cpu_model": cpu_model()}
+
+
+def cpu_gemv_baseline(budget_s: float = 3.0):
+    """The CPU restatement of the reference GEMV on all host threads (full
+    8192^2 plain + transposed) and on one thread (a 512-row slab)."""
+    import oracle as O
+
+    nt = O.threads()
+    A = O.uniform((GEMV_N, GEMV_N), seed=0)
+    x = O.uniform(GEMV_N, seed=1)
+    t = _timed(lambda: (O.gemv_f32(A, x, nthreads=nt), O.gemv_f32(A, x, trans=True, nthreads=nt)), budget_s, 50)
+    rows = 512
+    As, xs = A[:rows], x[:rows]
+    t1 = _timed(lambda: (O.gemv_f32(As, x, nthreads=1), O.gemv_f32(As, xs, trans=True, nthreads=1)), budget_s, 50)
+    slab_bytes = 2 * (rows * GEMV_N + GEMV_N + rows) * 4
+    return {"value": round(2 * GEMV_BYTES / t / 1e9, 2), "unit": "GB/s", "cores": nt, "kind": "port",
+            "sample": f"full workload, plain + transposed fp32 GEMV 8192^2 in {t * 1e3:.0f} ms, oracle/cpu_ref.c, "
+                      f"OpenMP {nt} threads",
+            "single_thread": {"value": round(slab_bytes / t1 / 1e9, 3), "unit": "GB/s", "cores": 1,
+                              "sample": f"{rows}-row slab, plain + transposed, {t1 * 1e3:.0f} ms"},
+            "cpu_model": cpu_model()}
+
+
+def cpu_config_baselines(budget_s: float = 1.5) -> dict:
+    """The oracle on the GEMM configs, all host threads and one thread: C1 in
+    full (one thread: a 128-row slab), C3 and C5 on a 64-row slab of A (one
+    thread: 8 rows), full-problem times extrapolated by rows."""
+    import oracle as O
+
+    nt = O.threads()
+    out = {}
+    n = 1024
+    A, B = O.uniform((n, n), seed=0), O.uniform((n, n), seed=1)
+    t = _timed(lambda: O.gemm_f32(A, B, nthreads=nt), budget_s)
+    t1 = _timed(lambda: O.gemm_f32(A[:128], B, nthreads=1), budget_s)
+    out["c1_fp32_gemm_1024"] = {
+        "value": round(2 * n ** 3 / t / 1e12, 4), "unit": "TFLOP/s", "cores": nt, "kind": "port",
+        "sample": f"full 1024^3 fp32 GEMM, {t * 1e3:.1f} ms",
+        "single_thread": {"value": round(2 * 128 * n * n / t1 / 1e12, 4), "unit": "TFLOP/s",
+                          "sample": f"128-row slab, {t1 * 1e3:.1f} ms"}}
+    n, rows, rows1 = 8192, 64, 8
+    A = O.to_lowp(O.normal((rows, n), seed=2) / math.sqrt(n), O.F16)
+    B = O.to_lowp(O.normal((n, n), seed=3) / math.sqrt(n), O.F16)
+    t = _timed(lambda: O.gemm_lowp(O.F16, A, B, nthreads=nt), budget_s)
+    t1 = _timed(lambda: O.gemm_lowp(O.F16, A[:rows1], B, nthreads=1), budget_s, 3)
+    out["c3_fp16_gemm_8192"] = {
+        "value": round(2 * rows * n * n / t / 1e12, 4), "unit": "TFLOP/s", "cores": nt, "kind": "port",
+        "sample": f"64-row slab of the 8192^3 fp16 GEMM, {t * 1e3:.0f} ms; extrapolated full problem "
+                  f"{t * n / rows:.1f} s",
+        "single_thread": {"value": round(2 * rows1 * n * n / t1 / 1e12, 5), "unit": "TFLOP/s",
+                          "sample": f"{rows1}-row slab, {t1 * 1e3:.0f} ms; extrapolated {t1 * n / rows1:.0f} s"}}
+    M, K, N_ = 4096, 8192, 28672
+    X = O.to_lowp(O.normal((rows, K), seed=6), O.BF16)
+    W = O.to_lowp(O.normal((K, N_), seed=7) * 0.02, O.BF16)
+    t = _timed(lambda: O.gemm_lowp(O.BF16, X, W, nthreads=nt), budget_s)
+    t1 = _timed(lambda: O.gemm_lowp(O.BF16, X[:rows1], W, nthreads=1), budget_s, 3)
+    out["c5_bf16_linear_4096x8192x28672"] = {
+        "value": round(2 * rows * K * N_ / t / 1e12, 4), "unit": "TFLOP/s", "cores": nt, "kind": "port",
+        "sample": f"64-row slab of the 4096 x 8192 x 28672 bf16 GEMM, {t * 1e3:.0f} ms; extrapolated full problem "
+                  f"{t * M / rows:.1f} s",
+        "single_thread": {"value": round(2 * rows1 * K * N_ / t1 / 1e12, 5), "unit": "TFLOP/s",
+                          "sample": f"{rows1}-row slab, {t1 * 1e3:.0f} ms; extrapolated {t1 * M / rows1:.0f} s"}}
+    return out
+
+
+# --------------------------------------------------------------------------- C2 GEMV
 def gemv_inputs(dev, sets: int, seed: int = 0):
     import torch
 
@@ -231,94 +554,72 @@ def gemv_inputs(dev, sets: int, seed: int = 0):
 
 
 def run_gemv(args, rank, world, local_rank):
+    """C2: plain + transposed fp32 GEMV 8192^2 per step (replicas at N > 1)."""
     import torch
     import cuop_b200 as cx
 
     dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
     sets = 2
     An, At, x = gemv_inputs(dev, sets, seed=1234 + rank)
     yn = torch.empty(GEMV_N, device=dev)
     yt = torch.empty(GEMV_N, device=dev)
-    stream = torch.cuda.current_stream()
 
     def step(i):
         cx.gemv(An[i % sets], x, yn)
         cx.gemv(At[i % sets], x, yt, trans=True)
 
-    for i in range(args.warmup):
-        step(i)
-    barrier(world)
-
-    K = args.steps
-    # The timed region replays one CUDA graph of K steps (2K kernels).
-    g_step, launches = capture_graph(step, K)
-    kn = kt = None
+    K = max(20, min(args.steps, 2000))
+    clk = ClockSampler(local_rank)
+    ms, launches = time_graph(step, K, max(3, args.warmup), world, clock=clk)
     cx.gemv(An[0], x, yn)
     kn = cx.last_kernel()
     cx.gemv(At[0], x, yt, trans=True)
     kt = cx.last_kernel()
-    g_step.replay()
-    barrier(world)
-    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local_rank) as clk:
-        e_start.record(stream)
-        g_step.replay()
-        e_end.record(stream)
-        torch.cuda.synchronize()
-    ms_local = e_start.elapsed_time(e_end) / K
-    del g_step
-    barrier(world)
-    ms = max_over_ranks(ms_local, world)
     # Per-kernel device time: each kernel alone, back to back, same rotation.
-    t_n = time_graph(lambda i: cx.gemv(An[i % sets], x, yn), K, 2, world)
-    t_t = time_graph(lambda i: cx.gemv(At[i % sets], x, yt, trans=True), K, 2, world)
+    t_n, _ = time_graph(lambda i: cx.gemv(An[i % sets], x, yn), K, 2, world)
+    t_t, _ = time_graph(lambda i: cx.gemv(At[i % sets], x, yt, trans=True), K, 2, world)
+    # Parity: both results against an fp64-accumulated product on the GPU.
+    ref_n = (An[0].double() @ x.double())
+    ref_t = (At[0].double().t() @ x.double())
+    cx.gemv(An[0], x, yn)
+    cx.gemv(At[0], x, yt, trans=True)
+    rel = max(float((yn.double() - ref_n).norm() / ref_n.norm()), float((yt.double() - ref_t).norm() / ref_t.norm()))
 
-    hbm, bf16, bf16_sus, peak_src = load_peaks()
-    value = world * 2 * GEMV_BYTES / (ms * 1e-3) / 1e9
+    hbm, _, _, peak_src = load_peaks()
     dom_name, dom_ms = (kt, t_t) if t_t >= t_n else (kn, t_n)
     achieved = GEMV_BYTES / (dom_ms * 1e-3) / 1e9
-    kernels = {
-        kn: {"ms": round(t_n, 5), "gbs": round(GEMV_BYTES / (t_n * 1e-3) / 1e9, 1),
-             "frac": round(GEMV_BYTES / (t_n * 1e-3) / 1e9 / hbm, 4)},
-        kt: {"ms": round(t_t, 5), "gbs": round(GEMV_BYTES / (t_t * 1e-3) / 1e9, 1),
-             "frac": round(GEMV_BYTES / (t_t * 1e-3) / 1e9 / hbm, 4)},
-    }
-
-    e2e = gemv_e2e_plugin(args, rank, world, local_rank, An, At)
-    e2e_operator = gemv_e2e(args, rank, world, local_rank, An[0], At[0], x)
-    line = {
-        "metric": "GEMV fp32 8192x8192 (plain + transposed) HBM GB/s", "value": round(value, 2), "unit": "GB/s",
-        "n_gpus": world, "steps": K, "warmup": args.warmup, "ms_per_step": round(ms, 5),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "fp32 GEMV y=1.0*A*x+0.0*y, M=N=8192 row-major, plain + transposed (A^T x), "
-                               "A,x ~ U[-1,1)", "parallelism": f"replicas x{world} (GEMV does not shard)",
-                   "l2": "inputs larger than L2: 4 x 256 MiB matrices rotated per step",
-                   "bytes_per_step": 2 * GEMV_BYTES},
+    kernels = {k: {"ms": round(t, 5), "gbs": round(GEMV_BYTES / (t * 1e-3) / 1e9, 1),
+                   "frac": round(GEMV_BYTES / (t * 1e-3) / 1e9 / hbm, 4)} for k, t in ((kn, t_n), (kt, t_t))}
+    tr = NCU_TRAFFIC.get(dom_name, {})
+    out = {
+        "gbs_total": round(world * 2 * GEMV_BYTES / (ms * 1e-3) / 1e9, 1), "ms": round(ms, 5),
+        "workload": "fp32 GEMV y=1.0*A*x+0.0*y, M=N=8192, plain + transposed, A,x ~ U[-1,1); 2 matrix sets "
+                    "per kind rotated (1 GiB > L2)",
+        "parallelism": f"replicas x{world} (GEMV does not shard)",
         "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": round(achieved, 1), "peak": hbm,
                      "peak_source": f"{peak_src} hbm_gbs (burst copy)", "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "frac_spec": round(achieved / SPEC_HBM_GBS, 4),
-                     "spec_peak": SPEC_HBM_GBS, "traffic": NCU_TRAFFIC_BYTES.get(dom_name),
+                     "traffic": tr.get("bytes"), "traffic_source": tr.get("source"),
                      "algorithmic_bytes": GEMV_BYTES},
-        "kernels": kernels,
-        "gpu_launches": launches,
-        "timing": "timed region = one CUDA graph replay of K steps; per-kernel times from graphs of K launches",
-        "clocks": clk.summary(),
-        "e2e": e2e,
-        "e2e_operator_path": e2e_operator,
+        "kernels": kernels, "gpu_launches": launches, "clocks": clk.summary(),
+        "parity": {"rel_frobenius_max": max_over_ranks(rel, world), "tol": 1e-5 * math.sqrt(GEMV_N),
+                   "reference": "fp64 product on the GPU"},
     }
-    return line
+    out["e2e"], out["e2e_graph_replay"] = gemv_e2e(args, rank, world, local_rank, An, At)
+    del An, At
+    torch.cuda.empty_cache()
+    return out
 
 
-def gemv_e2e_plugin(args, rank, world, local_rank, An, At):
-    """Same metric through the public API in the plugin's usage model
-    (GemvJITPlugin: the matrix is the plugin's weight, set once and resident;
-    each Execute takes x and returns y): every step brings a fresh x from
-    pinned host memory to the device, runs both GEMVs on the step's resident
-    matrices, puts both results in pinned host memory and waits for them on
-    the host.  x is staged by the library's copy kernel reading the pinned
-    buffer (cuopx_copy) and the GEMVs write y straight into pinned host
-    memory, so the step is three kernels with no copy-engine transfer."""
+def gemv_e2e(args, rank, world, local_rank, An, At):
+    """The GEMV through the public API in the plugin's usage model
+    (GemvJITPlugin holds the matrix as its weight, set once and resident;
+    each Execute takes x and returns y).  Per step: cuop_b200.copy brings a
+    fresh x from pinned host memory (the copy kernel reads the pinned
+    buffer), both cuop_b200.gemv calls write y straight into pinned host
+    memory, and the host waits.  Timed as three ordinary calls per step
+    (`e2e`) and, for comparison, with the three launches replayed as one CUDA
+    graph (`e2e_graph_replay`)."""
     import torch
     import cuop_b200 as cx
 
@@ -335,8 +636,24 @@ def gemv_e2e_plugin(args, rank, world, local_rank, An, At):
         cx.gemv(An[k], dx, hy[0])
         cx.gemv(At[k], dx, hy[1], trans=True)
 
-    # One CUDA graph per rotation slot holds the step's three launches (host
-    # launch cost of one replay instead of three API calls).
+    # The host copy of the results is the device's answer.
+    yn = torch.empty(GEMV_N, device=dev)
+    yt = torch.empty(GEMV_N, device=dev)
+    body(0)
+    stream.synchronize()
+    cx.gemv(An[0], dx, yn)
+    cx.gemv(At[0], dx, yt, trans=True)
+    torch.cuda.synchronize()
+    if not (torch.equal(hy[0], yn.cpu()) and torch.equal(hy[1], yt.cpu())):
+        raise RuntimeError("GEMV results in pinned host memory differ from the device results")
+
+    def step(i):
+        body(i % sets)
+        stream.synchronize()  # the host has the step's results
+
+    steps = max(5, min(args.steps, 500))
+    ms = time_host_loop(step, steps, 5, world)
+
     graphs = []
     for k in range(sets):
         body(k)
@@ -346,140 +663,21 @@ def gemv_e2e_plugin(args, rank, world, local_rank, An, At):
             body(k)
         graphs.append(gk)
 
-    # The host copy of the results is the device's answer.
-    yn = torch.empty(GEMV_N, device=dev)
-    yt = torch.empty(GEMV_N, device=dev)
-    graphs[0].replay()
-    stream.synchronize()
-    cx.gemv(An[0], dx, yn)
-    cx.gemv(At[0], dx, yt, trans=True)
-    torch.cuda.synchronize()
-    if not (torch.equal(hy[0], yn.cpu()) and torch.equal(hy[1], yt.cpu())):
-        raise RuntimeError("GEMV results in pinned host memory differ from the device results")
-
-    def step(i):
+    def gstep(i):
         graphs[i % sets].replay()
-        stream.synchronize()  # the host has the step's results
+        stream.synchronize()
 
-    steps = max(5, min(args.steps, 200))
-    ms = time_loop(step, steps, 3, world)
+    ms_g = time_host_loop(gstep, steps, 5, world)
     del graphs
-    return {"value": round(world * 2 * GEMV_BYTES / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-            "h2d_bytes_per_step": GEMV_N * 4, "d2h_bytes_per_step": 2 * GEMV_N * 4,
-            "ms_per_step": round(ms, 4), "steps": steps,
-            "path": "cuop_b200.copy + cuop_b200.gemv (C ABI) with the matrices resident as plugin weights; per "
-                    "step x read from pinned host memory by the copy kernel, both GEMVs writing y into pinned host "
-                    "memory, replayed as one CUDA graph, then host synchronisation"}
-
-
-def gemv_e2e(args, rank, world, local_rank, An, At, x):
-    """Same metric through the public API with pinned host buffers: H2D of
-    both matrices and x, both GEMVs, D2H of both results, every step."""
-    import torch
-    import cuop_b200 as cx
-
-    dev = torch.device("cuda", local_rank)
-    hA = An.cpu().pin_memory()
-    hAt = At.cpu().pin_memory()
-    hx = x.cpu().pin_memory()
-    hyn = torch.empty(GEMV_N, pin_memory=True)
-    hyt = torch.empty(GEMV_N, pin_memory=True)
-    dA = torch.empty_like(An)
-    dAt = torch.empty_like(At)
-    dx = torch.empty_like(x)
-    yn = torch.empty(GEMV_N, device=dev)
-    yt = torch.empty(GEMV_N, device=dev)
-
-    def step(_):  # the operator API's model: the matrix itself is the per-call input
-        dA.copy_(hA, non_blocking=True)
-        dAt.copy_(hAt, non_blocking=True)
-        dx.copy_(hx, non_blocking=True)
-        cx.gemv(dA, dx, yn)
-        cx.gemv(dAt, dx, yt, trans=True)
-        hyn.copy_(yn, non_blocking=True)
-        hyt.copy_(yt, non_blocking=True)
-
-    steps = max(3, min(args.steps, 10))
-    ms = time_loop(step, steps, 2, world)
-    return {"value": round(world * 2 * GEMV_BYTES / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-            "h2d_bytes_per_step": 2 * GEMV_N * GEMV_N * 4 + GEMV_N * 4, "d2h_bytes_per_step": 2 * GEMV_N * 4,
-            "ms_per_step": round(ms, 4), "steps": steps,
-            "path": "Gemv<T>::Forward model: both 256 MiB matrices H2D every step (PCIe-bound)"}
-
-
-# --------------------------------------------------------------------------- CPU baseline (oracle)
-def cpu_gemv_baseline(budget_s: float = 4.0):
-    """The CPU restatement of the reference GEMV on all host threads, full
-    8192^2 plain + transposed, repeated for about `budget_s` seconds."""
-    import numpy as np
-    import oracle as O
-
-    nt = O.threads()
-    A = O.uniform((GEMV_N, GEMV_N), seed=0)
-    x = O.uniform(GEMV_N, seed=1)
-    O.gemv_f32(A, x, nthreads=nt)  # warm-up (page-in)
-    reps, t0 = 0, time.perf_counter()
-    while True:
-        O.gemv_f32(A, x, nthreads=nt)
-        O.gemv_f32(A, x, trans=True, nthreads=nt)
-        reps += 1
-        el = time.perf_counter() - t0
-        if el >= budget_s or reps >= 50:
-            break
-    gbs = reps * 2 * GEMV_BYTES / el / 1e9
-    return {"value": round(gbs, 2), "unit": "GB/s", "cores": nt, "kind": "port",
-            "sample": f"full workload: {reps} x (plain + transposed) fp32 GEMV 8192^2 in {el:.2f} s, "
-                      f"oracle/cpu_ref.c, OpenMP {nt} threads"}
-
-
-def cpu_config_baselines(budget_s: float = 1.5) -> dict:
-    """The oracle (CPU restatement of the reference kernels' arithmetic) on
-    the GEMM configs, all host threads: C1 and C4 in full, C3 and C5 on a
-    64-row slab of A with the full-problem time extrapolated by rows."""
-    import numpy as np
-    import oracle as O
-
-    nt = O.threads()
-
-    def timed(fn):
-        fn()  # page-in
-        reps, t0 = 0, time.perf_counter()
-        while True:
-            fn()
-            reps += 1
-            el = time.perf_counter() - t0
-            if el >= budget_s or reps >= 20:
-                return el / reps
-
-    out = {}
-    n = 1024
-    A, B = O.uniform((n, n), seed=0), O.uniform((n, n), seed=1)
-    t = timed(lambda: O.gemm_f32(A, B, nthreads=nt))
-    out["c1_fp32_gemm_1024"] = {"value": round(2 * n ** 3 / t / 1e12, 4), "unit": "TFLOP/s", "cores": nt,
-                                "kind": "port", "sample": f"full 1024^3 fp32 GEMM, {t * 1e3:.1f} ms"}
-    n, rows = 8192, 64
-    A = O.to_lowp(O.normal((rows, n), seed=2) / math.sqrt(n), O.F16)
-    B = O.to_lowp(O.normal((n, n), seed=3) / math.sqrt(n), O.F16)
-    t = timed(lambda: O.gemm_lowp(O.F16, A, B, nthreads=nt))
-    out["c3_fp16_gemm_8192"] = {"value": round(2 * rows * n * n / t / 1e12, 4), "unit": "TFLOP/s", "cores": nt,
-                                "kind": "port", "sample": f"64-row slab of the 8192^3 fp16 GEMM, {t * 1e3:.0f} ms; "
-                                                          f"extrapolated full problem {t * n / rows:.1f} s"}
-    bt, M, N_, K = 4096, 128, 128, 64
-    A = O.to_lowp(O.normal((bt, M, K), seed=4), O.BF16)
-    B = O.to_lowp(O.normal((bt, K, N_), seed=5), O.BF16)
-    t = timed(lambda: O.gemm_batched_lowp(O.BF16, A, B, nthreads=nt))
-    out["c4_bf16_batched_4096x128x128x64"] = {
-        "value": round(bt * (M * K + K * N_ + M * N_) * 2 / t / 1e9, 3), "unit": "GB/s", "cores": nt, "kind": "port",
-        "sample": f"full 4096 x 128x128x64 bf16 batched GEMM, {t * 1e3:.0f} ms"}
-    M, K, N_ = 4096, 8192, 28672
-    X = O.to_lowp(O.normal((rows, K), seed=6), O.BF16)
-    W = O.to_lowp(O.normal((K, N_), seed=7) * 0.02, O.BF16)
-    t = timed(lambda: O.gemm_lowp(O.BF16, X, W, nthreads=nt))
-    out["c5_bf16_linear_4096x8192x28672"] = {
-        "value": round(2 * rows * K * N_ / t / 1e12, 4), "unit": "TFLOP/s", "cores": nt, "kind": "port",
-        "sample": f"64-row slab of the 4096 x 8192 x 28672 bf16 GEMM, {t * 1e3:.0f} ms; "
-                  f"extrapolated full problem {t * M / rows:.1f} s"}
-    return out
+    common = {"unit": "GB/s", "h2d_bytes_per_step": world * GEMV_N * 4, "d2h_bytes_per_step": world * 2 * GEMV_N * 4,
+              "steps": steps}
+    e2e = {"value": round(world * 2 * GEMV_BYTES / (ms * 1e-3) / 1e9, 2), "ms_per_step": round(ms, 4), **common,
+           "path": "per step: cuop_b200.copy (x from pinned host) + 2 x cuop_b200.gemv (y into pinned host), "
+                   "three ordinary calls, then host synchronisation; wall clock, max over ranks"}
+    e2e_g = {"value": round(world * 2 * GEMV_BYTES / (ms_g * 1e-3) / 1e9, 2), "ms_per_step": round(ms_g, 4),
+             **common, "path": "the same three launches replayed as one CUDA graph per step, then host "
+                               "synchronisation"}
+    return e2e, e2e_g
 
 
 # --------------------------------------------------------------------------- other configs
@@ -496,194 +694,194 @@ def run_configs(args, rank, world, local_rank):
     g.manual_seed(99 + rank)
 
     want = {c.strip().lower() for c in args.configs.split(",") if c.strip()}
-    # The memory-bound batched config runs before the tensor-bound GEMMs:
-    # right after the 8192^3 GEMM at the power cap it read up to ~10 % lower
-    # than the same kernel measured alone on the same part.
+    if "c2" in want:
+        out["c2_fp32_gemv_8192"] = run_gemv(args, rank, world, local_rank)
     if "c1" in want:
-        out.update(_config_c1(cx, dev, g, steps, world))
-    if "c4" in want:
-        out.update(_config_c4(cx, sharding, dev, g, steps, rank, world, hbm))
+        out.update(_config_c1(cx, dev, g, steps, world, local_rank))
     if "c3" in want:
-        out.update(_config_c3(cx, sharding, dev, g, steps, rank, world, bf16_peak, peak_src))
+        out.update(_config_c3(cx, sharding, dev, steps, rank, world, local_rank, bf16_peak, peak_src))
     if "c5" in want:
-        out.update(_config_c5(cx, sharding, dev, g, steps, rank, world, bf16_peak))
+        out.update(_config_c5(cx, sharding, dev, steps, rank, world, local_rank, bf16_peak))
     return out
 
 
-def _config_c1(cx, dev, g, steps, world):
-    """fp32 GEMM 1024^3 (replicas)."""
+def _config_c1(cx, dev, g, steps, world, local_rank):
+    """fp32 GEMM 1024^3 (replicas), default mode (3xTF32 on the tensor cores)."""
     import torch
 
     n = 1024
     A = torch.rand(n, n, device=dev, generator=g) * 2 - 1
     B = torch.rand(n, n, device=dev, generator=g) * 2 - 1
     C = torch.empty(n, n, device=dev)
-    ms = time_graph(lambda i: cx.gemm(A, B, C), steps * 4, 5, world)
+    clk = ClockSampler(local_rank)
+    ms, launches = time_graph(lambda i: cx.gemm(A, B, C), steps * 20, 5, world, clock=clk)
+    kname = cx.last_kernel()
+    ref = (A.double() @ B.double())
+    cx.gemm(A, B, C)
+    rel = float((C.double() - ref).norm() / ref.norm())
     tf = 2 * n ** 3 / (ms * 1e-3) / 1e12
-    return {"c1_fp32_gemm_1024": {"tflops_total": round(world * tf, 3), "ms": round(ms, 5),
-                                  "kernel": cx.last_kernel(),
+    return {"c1_fp32_gemm_1024": {"tflops_total": round(world * tf, 3), "ms": round(ms, 5), "kernel": kname,
                                   "frac_fp32_simt_nominal": round(tf / FP32_SIMT_NOMINAL_TFLOPS, 4),
-                                  "parallelism": f"replicas x{world}"}}
+                                  "parallelism": f"replicas x{world}", "gpu_launches": launches,
+                                  "clocks": clk.summary(),
+                                  "parity": {"rel_frobenius_max": max_over_ranks(rel, world),
+                                             "tol": 1e-5 * math.sqrt(n), "reference": "fp64 product on the GPU"}}}
 
 
-def _sharded_gemm(cx, sharding, X, Wl, rank, world, steps, n_total):
+def _sharded_parity(Y, X, W_full, world, seed=11):
+    """Full output Y [M, N] on this rank against an fp32 product: 64 complete
+    rows and 64 complete columns (seeded, the same on every rank); then a
+    checksum of all of Y gathered from every rank.  Collective."""
+    import torch
+
+    M, Nt = Y.shape
+    g = torch.Generator().manual_seed(seed)
+    rows = torch.randperm(M, generator=g)[:64].to(Y.device)
+    cols = torch.randperm(Nt, generator=g)[:64].to(Y.device)
+    r_rows = fp32_product(X[rows], W_full)
+    r_cols = fp32_product(X, W_full[:, cols])
+    err = max(max_rel(Y[rows], r_rows), max_rel(Y[:, cols], r_cols))
+    sums = all_gather_floats(checksum(Y), world)
+    return {"max_rel": max_over_ranks(err, world), "tol": LOWP_TOL,
+            "ranks_identical": all(s == sums[0] for s in sums),
+            "checked": "64 complete rows + 64 complete columns per rank vs fp32 product (TF32 off); "
+                       "checksum of the full output all-gathered"}
+
+
+def _sharded_gemm(cx, sharding, X, Wl, W_full, rank, world, steps, n_total, local_rank):
     """Column-sharded Y = X @ W with the full Y on every rank: the fused
     peer-store GEMM (graph-replayed, cross-GPU barriers inside) and, for
-    comparison, GEMM + NCCL all-gather + gather kernel.  Returns
-    (ms fused, ms nccl, kernel name)."""
+    comparison, GEMM + NCCL all-gather + gather kernel; each output checked
+    on every rank after its timed region.  Returns (ms fused, ms nccl, kernel
+    name, clocks, parity fused, parity nccl)."""
     import torch
     from cuop_b200 import peer
 
     M = X.size(0)
     pg = peer.PeerShardedGemm(Wl, rank, world, max_rows=M)
+    clk = ClockSampler(local_rank)
     try:
-        ms_peer = time_graph(lambda i: pg.forward(X), steps, 3, world, align=lambda: peer.peer_barrier(pg.signals))
-        pg.forward(X)
+        ms_peer, _ = time_graph(lambda i: pg.forward(X), steps, 3, world, align=lambda: peer.peer_barrier(pg.signals),
+                                clock=clk)
+        Y = pg.forward(X)
         kname = pg.last_kernel
+        torch.cuda.synchronize()
+        par_peer = _sharded_parity(Y, X, W_full, world)
+        del Y
     finally:
         torch.cuda.synchronize()
         pg.close()
     sg = sharding.ColumnShardedGemm(Wl, world)
     Y = torch.empty(M, n_total, device=X.device, dtype=X.dtype)
     ms_nccl = time_loop(lambda i: sg.forward(X, out=Y), steps, 3, world)
+    par_nccl = _sharded_parity(Y, X, W_full, world)
     del Y
-    return ms_peer, ms_nccl, kname
+    return ms_peer, ms_nccl, kname, clk.summary(), par_peer, par_nccl
 
 
-def _config_c3(cx, sharding, dev, g, steps, rank, world, bf16_peak, peak_src):
-    """fp16 GEMM 8192^3; N-sharded with an all-gather of C when world > 1."""
+def _config_gemm_lowp(cx, sharding, dev, steps, rank, world, local_rank, M, K, N_, dtype, x_scale, w_scale,
+                      bf16_peak, seed):
+    """One 16-bit GEMM config: single GPU, or column-sharded over the ranks
+    with the full output on every rank.  X and W are generated from the same
+    seed on every rank (each rank keeps its column block of W)."""
     import torch
 
-    n = 8192
-    A = (torch.randn(n, n, device=dev, generator=g) / math.sqrt(n)).half()
-    Wfull_cols = n // world
-    Wl = (torch.randn(n, Wfull_cols, device=dev, generator=g) / math.sqrt(n)).half()
-    Cl = torch.empty(n, Wfull_cols, device=dev, dtype=torch.half)
-    ms_local = time_graph(lambda i: cx.gemm(A, Wl, Cl), steps, 3, world)
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    X = (torch.randn(M, K, device=dev, generator=g) * x_scale).to(dtype)
+    W_full = (torch.randn(K, N_, device=dev, generator=g) * w_scale).to(dtype)
+    nl = N_ // world
+    Wl = W_full[:, rank * nl:(rank + 1) * nl].contiguous()
+    Yl = torch.empty(M, nl, device=dev, dtype=dtype)
+    clk_local = ClockSampler(local_rank)
+    ms_local, launches = time_graph(lambda i: cx.gemm(X, Wl, Yl), steps, 3, world, clock=clk_local)
     kname = cx.last_kernel()
-    del Cl
     res = {}
     if world == 1:
         ms = ms_local
+        clocks = clk_local.summary()
+        parity = _sharded_parity(Yl, X, W_full, 1)
     else:
-        ms, ms_nccl, kname = _sharded_gemm(cx, sharding, A, Wl, rank, world, steps, n)
+        ms, ms_nccl, kname, clocks, parity, par_nccl = _sharded_gemm(cx, sharding, X, Wl, W_full, rank, world, steps,
+                                                                     N_, local_rank)
         res["nccl_allgather_path"] = {"ms": round(ms_nccl, 4),
-                                      "tflops_total": round(2 * n ** 3 / (ms_nccl * 1e-3) / 1e12, 1)}
-    tf_local = 2 * n * n * Wfull_cols / (ms_local * 1e-3) / 1e12
-    res = {
-        "tflops_total": round(2 * n ** 3 / (ms * 1e-3) / 1e12, 1), "ms": round(ms, 4), "kernel": kname,
-        "gemm_only_tflops_per_gpu": round(tf_local, 1), "frac_gemm_only": round(tf_local / bf16_peak, 4),
-        "frac_spec_gemm_only": round(tf_local / SPEC_DENSE_16BIT_TFLOPS, 4), "peak_tflops": bf16_peak, "peak_source": f"{peak_src} bf16_tflops (burst)",
-        "parallelism": "single GPU" if world == 1 else
-        f"N-sharded x{world}; GEMM epilogue stores every tile into all ranks' outputs over NVLink", **res}
-    del A, Wl
-    torch.cuda.empty_cache()
-    return {"c3_fp16_gemm_8192": res}
-
-
-def _config_c4(cx, sharding, dev, g, steps, rank, world, hbm):
-    """bf16 batched 4096 x (128x128x64), batch-sharded, no collective."""
-    import torch
-
-    batch, M, N_, K = 4096, 128, 128, 64
-    b0, b1 = sharding.shard_range(batch, rank, world)
-    lb = b1 - b0
-    per_set = lb * (M * K + K * N_ + M * N_) * 2
-    sets = max(2, math.ceil(400e6 / per_set))
-    As = [torch.randn(lb, M, K, device=dev, generator=g).bfloat16() for _ in range(sets)]
-    Bs = [torch.randn(lb, K, N_, device=dev, generator=g).bfloat16() for _ in range(sets)]
-    Cs = [torch.empty(lb, M, N_, device=dev, dtype=torch.bfloat16) for _ in range(sets)]
-    ms = time_graph(lambda i: cx.batched_gemm(As[i % sets], Bs[i % sets], Cs[i % sets]), steps * 4, 5, world)
-    bytes_total = batch * (M * K + K * N_ + M * N_) * 2
-    gbs_local = lb * (M * K + K * N_ + M * N_) * 2 / (ms * 1e-3) / 1e9
-    res = {
-        "gbs_total": round(bytes_total / (ms * 1e-3) / 1e9, 1), "ms": round(ms, 5), "kernel": cx.last_kernel(),
-        "tflops_total": round(2 * batch * M * N_ * K / (ms * 1e-3) / 1e12, 2),
-        "frac_hbm_per_gpu": round(gbs_local / hbm, 4), "frac_spec_hbm_per_gpu": round(gbs_local / SPEC_HBM_GBS, 4),
-        "l2": f"{sets} rotated input sets > L2",
-        "parallelism": f"batch-sharded x{world}, no collective"}
-    del As, Bs, Cs
-    torch.cuda.empty_cache()
-    return {"c4_bf16_batched_4096x128x128x64": res}
-
-
-def _config_c5(cx, sharding, dev, g, steps, rank, world, bf16_peak):
-    """bf16 linear 4096 x 8192 x 28672, W column-sharded, all-gather of Y."""
-    import torch
-
-    M, K, N_ = 4096, 8192, 28672
-    X = torch.randn(M, K, device=dev, generator=g).bfloat16()
-    nl = N_ // world
-    Wl = (torch.randn(K, nl, device=dev, generator=g) * 0.02).bfloat16()
-    Yl = torch.empty(M, nl, device=dev, dtype=torch.bfloat16)
-    ms_local = time_graph(lambda i: cx.gemm(X, Wl, Yl), steps, 3, world)
-    kname = cx.last_kernel()
+                                      "tflops_total": round(2 * M * K * N_ / (ms_nccl * 1e-3) / 1e12, 1),
+                                      "parity": par_nccl}
     del Yl
-    res = {}
-    if world > 1:
-        ms, ms_nccl, kname = _sharded_gemm(cx, sharding, X, Wl, rank, world, steps, N_)
-        res["nccl_allgather_path"] = {"ms": round(ms_nccl, 4),
-                                      "tflops_total": round(2 * M * K * N_ / (ms_nccl * 1e-3) / 1e12, 1)}
-    else:
-        ms = ms_local
     tf_local = 2 * M * K * nl / (ms_local * 1e-3) / 1e12
-    res = {
+    out = {
         "tflops_total": round(2 * M * K * N_ / (ms * 1e-3) / 1e12, 1), "ms": round(ms, 4), "kernel": kname,
         "gemm_only_tflops_per_gpu": round(tf_local, 1), "frac_gemm_only": round(tf_local / bf16_peak, 4),
         "frac_spec_gemm_only": round(tf_local / SPEC_DENSE_16BIT_TFLOPS, 4),
         "parallelism": "single GPU" if world == 1 else
-        f"W column-sharded x{world}; GEMM epilogue stores every tile of Y into all ranks' outputs over NVLink",
+        f"W column-sharded x{world}; GEMM epilogue stores every tile into all ranks' outputs over NVLink",
+        "clocks": clocks, "clocks_gemm_only": clk_local.summary(), "parity": parity, "gpu_launches_gemm_only": launches,
         **res}
-    del X, Wl
+    del X, W_full, Wl
     torch.cuda.empty_cache()
-    return {"c5_bf16_linear_4096x8192x28672": res}
+    return out
+
+
+def _config_c3(cx, sharding, dev, steps, rank, world, local_rank, bf16_peak, peak_src):
+    """fp16 GEMM 8192^3, A,B ~ N(0,1)/sqrt(K); N-sharded with the full C on every rank when world > 1."""
+    n = 8192
+    import torch
+
+    out = _config_gemm_lowp(cx, sharding, dev, steps, rank, world, local_rank, n, n, n, torch.float16,
+                            1 / math.sqrt(n), 1 / math.sqrt(n), bf16_peak, seed=301)
+    out["peak_tflops"] = bf16_peak
+    out["peak_source"] = f"{peak_src} bf16_tflops (burst)"
+    return {"c3_fp16_gemm_8192": out}
+
+
+def _config_c5(cx, sharding, dev, steps, rank, world, local_rank, bf16_peak):
+    """bf16 linear 4096 x 8192 x 28672, X ~ N(0,1), W ~ N(0, 0.02); W column-sharded, full Y on every rank."""
+    import torch
+
+    out = _config_gemm_lowp(cx, sharding, dev, steps, rank, world, local_rank, 4096, 8192, 28672, torch.bfloat16,
+                            1.0, 0.02, bf16_peak, seed=501)
+    return {"c5_bf16_linear_4096x8192x28672": out}
 
 
 # --------------------------------------------------------------------------- reference arm
 def run_reference(args, rank, world):
-    """CPU restatement of the reference GEMV path (the reference has no CPU
-    implementation) on all host threads; each step is a bounded row sample of
-    the 8192^2 plain + transposed workload."""
+    """CPU restatement of the reference's batched GEMM arithmetic (the
+    reference has no CPU implementation) on all host threads; each step is a
+    bounded batch sample of the C4 workload, sized so that the run ends in
+    about a minute."""
     if rank != 0:
         return None
-    import numpy as np
     import oracle as O
 
     nt = O.threads()
-    A = O.uniform((GEMV_N, GEMV_N), seed=0)
-    x = O.uniform(GEMV_N, seed=1)
+    A = O.to_lowp(O.normal((BATCH, BM, BK), seed=4), O.BF16)
+    B = O.to_lowp(O.normal((BATCH, BK, BN), seed=5), O.BF16)
     t0 = time.perf_counter()
-    O.gemv_f32(A, x, nthreads=nt)
-    O.gemv_f32(A, x, trans=True, nthreads=nt)
+    O.gemm_batched_lowp(O.BF16, A, B, nthreads=nt)
     t_full = time.perf_counter() - t0
-    budget = 90.0
+    budget = 60.0
     frac = min(1.0, budget / max(1e-9, (args.steps + args.warmup) * t_full))
-    rows = max(64, int(GEMV_N * frac) // 64 * 64)
-    As = np.ascontiguousarray(A[:rows])
-    xs_t = np.ascontiguousarray(x[:rows])
-    sample_bytes = (rows * GEMV_N + GEMV_N + rows) * 4 + (rows * GEMV_N + rows + GEMV_N) * 4
-
-    def step():
-        O.gemv_f32(As, x, nthreads=nt)          # rows x 8192 plain
-        O.gemv_f32(As, xs_t, trans=True, nthreads=nt)  # sum over `rows` rows, 8192 outputs
-
+    nb = max(64, int(BATCH * frac) // 64 * 64)
+    As, Bs = A[:nb], B[:nb]
     for _ in range(args.warmup):
-        step()
+        O.gemm_batched_lowp(O.BF16, As, Bs, nthreads=nt)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        step()
+        O.gemm_batched_lowp(O.BF16, As, Bs, nthreads=nt)
     el = time.perf_counter() - t0
-    gbs = args.steps * sample_bytes / el / 1e9
-    sample = (f"each step: plain GEMV on a {rows}x8192 row slab + transposed GEMV over the same {rows} rows "
-              f"(8192 outputs) of the seeded 8192^2 fp32 workload; oracle/cpu_ref.c, OpenMP {nt} threads")
+    gbs = args.steps * nb * C4_BYTES_PER_BATCH / el / 1e9
+    sample = (f"each step: {nb} of the 4096 batches (128x128x64 bf16, fp32 accumulate) of the seeded workload; "
+              f"oracle/cpu_ref.c, OpenMP {nt} threads")
     return {
-        "impl": "reference", "metric": "GEMV fp32 8192x8192 (plain + transposed) HBM GB/s", "value": round(gbs, 3),
-        "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(el / args.steps * 1e3, 4), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "fp32 GEMV y=1.0*A*x+0.0*y, M=N=8192 row-major, plain + transposed (A^T x), "
-                               "A,x ~ U[-1,1)", "parallelism": "host CPU"},
-        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": nt, "kind": "port", "sample": sample},
+        "impl": "reference", "metric": "bf16 batched GEMM 4096 x (128x128x64), batch-sharded: HBM GB/s",
+        "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(el / args.steps * 1e3, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "bf16 strided-batched GEMM C[b] = A[b] B[b], batch 4096, M=N=128, K=64, "
+                               "A,B ~ N(0,1), fp32 accumulate, bf16 out", "global_batch": BATCH,
+                   "parallelism": "host CPU (rank 0)"},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": nt, "kind": "port", "sample": sample,
+                         "cpu_model": cpu_model()},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -695,9 +893,9 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--no-configs", action="store_true", help="skip the other GEMM configs")
-    ap.add_argument("--configs", default="c1,c3,c4,c5",
-                    help="comma-separated subset of the other configs to run (c1, c3, c4, c5)")
+    ap.add_argument("--no-configs", action="store_true", help="skip the other configs")
+    ap.add_argument("--configs", default="c2,c1,c3,c5",
+                    help="comma-separated subset of the other configs to run (c2, c1, c3, c5)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
@@ -713,13 +911,16 @@ def main():
 
     torch.cuda.set_device(local_rank)
     dist_init(world)
-    line = run_gemv(args, rank, world, local_rank)
+    line = run_c4(args, rank, world, local_rank)
     if not args.no_configs:
         line["configs"] = run_configs(args, rank, world, local_rank)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_gemv_baseline()
+        line["cpu_baseline"] = cpu_c4_baseline()
         if "configs" in line:
-            for key, cb in cpu_config_baselines().items():
+            cbs = cpu_config_baselines()
+            if "c2_fp32_gemv_8192" in line["configs"]:
+                cbs["c2_fp32_gemv_8192"] = cpu_gemv_baseline()
+            for key, cb in cbs.items():
                 if key in line["configs"]:
                     line["configs"][key]["cpu_baseline"] = cb
     elif rank == 0:

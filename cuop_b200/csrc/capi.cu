@@ -124,6 +124,8 @@ int run_variant(int v, const GemmProblem& p, cudaStream_t stream) {
     case kVariantTc2x512: return tc_ok ? gemm_tc2(p, stream, 512) : -1;
     case kVariantTc128x256: return tc_ok ? gemm_tc(p, stream, 256) : -1;
     case kVariantTc128x128: return tc_ok ? gemm_tc(p, stream, 128) : -1;
+    case kVariantTc128x128x2: return tc_ok ? gemm_tc(p, stream, kTc128x128TwoPerSm) : -1;
+    case kVariantTc128x64x2: return tc_ok ? gemm_tc(p, stream, kTc128x64TwoPerSm) : -1;
     case kVariantTf32x3_64: return x3_ok ? gemm_tf32x3(p, stream, 64) : -1;
     case kVariantTf32x3_128: return x3_ok ? gemm_tf32x3(p, stream, 128) : -1;
     case kVariantFfma: return ffma_ok ? gemm_simt_f32(p, stream) : -1;

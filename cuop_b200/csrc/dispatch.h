@@ -60,6 +60,10 @@ int gemm_simt_f32(const GemmProblem& p, cudaStream_t stream);
 // bn = 0: choose (2-SM kernel for large problems, else BN 256 or 128);
 // bn = 128 / 256: the 1-SM kernel with that tile width.
 bool gemm_tc_supported(const GemmProblem& p);
+// bn = kTc128x128TwoPerSm: 128 x 128 tiles with two CTAs resident per SM.
+constexpr int kTc128x128TwoPerSm = -128;
+// bn = kTc128x64TwoPerSm: 128 x 64 tiles with two CTAs resident per SM.
+constexpr int kTc128x64TwoPerSm = -64;
 int gemm_tc(const GemmProblem& p, cudaStream_t stream, int bn = 0);
 // The 1-SM kernel (bn 128 or 256) with every output chunk also stored to
 // peers[0..npeers) (peer mappings of identically laid out outputs).
@@ -90,7 +94,9 @@ enum GemmVariant : int {
   kVariantFfma = 6,        // register-blocked fp32 FFMA
   kVariantGeneric = 7,     // any dtype / layout
   kVariantTc2x512 = 8,     // 2-SM tcgen05, 256 x 512 pair tiles
-  kVariantCount = 9,
+  kVariantTc128x128x2 = 9, // 1-SM tcgen05, 128 x 128 tiles, two CTAs per SM
+  kVariantTc128x64x2 = 10, // 1-SM tcgen05, 128 x 64 tiles, two CTAs per SM
+  kVariantCount = 11,
 };
 const char* gemm_variant_name(int v);
 // The override (set by cuopx_set_gemm_variant) if any, else the first

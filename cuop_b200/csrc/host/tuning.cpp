@@ -34,7 +34,8 @@ namespace {
 
 const char* const kVariantNames[kVariantCount] = {"auto",          "tc2",           "tc_128x256",
                                                   "tc_128x128",    "tf32x3_128x64", "tf32x3_128x128",
-                                                  "ffma",          "generic",       "tc2_256x512"};
+                                                  "ffma",          "generic",       "tc2_256x512",
+                                                  "tc_128x128_2cta", "tc_128x64_2cta"};
 
 struct Range {
   int64_t lo = 0, hi = INT64_MAX;

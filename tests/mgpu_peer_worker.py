@@ -6,7 +6,13 @@ W's column block, and runs PeerShardedGemm (fused GEMM + all-gather over
 NVLink peer stores) and ColumnShardedGemm (GEMM + NCCL all-gather + gather
 kernel).  Checks: the full output on every rank is within the fp16/bf16
 tolerance (max|C-R|/max|R| <= 1e-2) of an fp32 product, every rank holds the
-same bits, and a second forward with new inputs replaces the first."""
+same bits, and a second forward with new inputs replaces the first.
+
+Then the two benchmark shapes at the world size of the run: fp16 8192^3
+(A, B ~ N(0,1)/sqrt(K)) and the bf16 linear layer 4096 x 8192 x 28672
+(X ~ N(0,1), W ~ N(0, 0.02)), generated on every device from one seed, each
+full output checked on every rank against the full fp32 product, for both
+the fused and the NCCL path, and compared bit for bit across ranks."""
 import datetime
 import os
 import sys
@@ -33,6 +39,45 @@ def ref_product(X, W):
         return X.float() @ W.float()
     finally:
         torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+def checksum(Y):
+    v = Y.contiguous().view(torch.int16).to(torch.int64)
+    rw = torch.arange(1, v.size(0) + 1, device=v.device, dtype=torch.int64)
+    cw = torch.arange(1, v.size(1) + 1, device=v.device, dtype=torch.int64)
+    return torch.stack([(v.sum(dim=1) * rw).sum(), (v.sum(dim=0) * cw).sum()])
+
+
+def same_on_every_rank(Y, world):
+    h = checksum(Y)
+    hs = [torch.zeros_like(h) for _ in range(world)]
+    dist.all_gather(hs, h)
+    return all(torch.equal(x, hs[0]) for x in hs)
+
+
+def check_benchmark_shape(name, dtype, M, K, N, x_scale, w_scale, rank, world, dev):
+    """Full output of the fused and the NCCL path on every rank vs the full fp32 product."""
+    g = torch.Generator(device=dev).manual_seed(1234)
+    X = (torch.randn(M, K, device=dev, generator=g) * x_scale).to(dtype)
+    W = (torch.randn(K, N, device=dev, generator=g) * w_scale).to(dtype)
+    Wl = sharding.split_columns(W, rank, world)
+    ref = ref_product(X, W)
+    sg = peer.PeerShardedGemm(Wl, rank, world, max_rows=M)
+    Y = sg.forward(X)
+    torch.cuda.synchronize()
+    err = max_rel(Y, ref)
+    same = same_on_every_rank(Y, world)
+    del Y
+    sg.close()
+    Yn = sharding.ColumnShardedGemm(Wl, world).forward(X)
+    torch.cuda.synchronize()
+    errn = max_rel(Yn, ref)
+    same_n = same_on_every_rank(Yn, world)
+    print(f"rank {rank} {name}: fused err {err:.2e} identical {same}, nccl err {errn:.2e} identical {same_n}",
+          flush=True)
+    del Yn, ref, X, W, Wl
+    torch.cuda.empty_cache()
+    return err <= TOL and errn <= TOL and same and same_n
 
 
 def main():
@@ -73,6 +118,10 @@ def main():
         print(f"rank {rank} {dtype} M={M} K={K} nb={nb}: peer err {err:.2e}, second {err2:.2e}, nccl {errn:.2e}",
               flush=True)
         sg.close()
+    ok &= check_benchmark_shape("fp16 8192^3", torch.float16, 8192, 8192, 8192, 8192 ** -0.5, 8192 ** -0.5, rank,
+                                world, dev)
+    ok &= check_benchmark_shape("bf16 4096x8192x28672", torch.bfloat16, 4096, 8192, 28672, 1.0, 0.02, rank, world,
+                                dev)
     code = cx.device_error()
     ok &= code == 0
     flag = torch.tensor([1 if ok else 0], device=dev)

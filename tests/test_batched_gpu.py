@@ -71,7 +71,7 @@ def test_c4_bf16_batched_full(dev):
     B16 = O.to_lowp(O.normal((batch, K, N), seed=1), dt)
     A, B = to_dev_lowp(A16, dt, dev), to_dev_lowp(B16, dt, dev)
     C = cx.batched_gemm(A, B)
-    assert cx.last_kernel() == "gemm_tc_128x128"
+    assert cx.last_kernel() == "gemm_tc_128x128_2cta"
     prev = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = False
     full = torch.bmm(A.float(), B.float())

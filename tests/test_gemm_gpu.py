@@ -302,3 +302,34 @@ def test_deterministic_lowp(dev):
     A = to_dev_lowp(O.to_lowp(O.normal((1024, 2048), seed=1), dt), dt, dev)
     B = to_dev_lowp(O.to_lowp(O.normal((2048, 1536), seed=2), dt), dt, dev)
     assert torch.equal(cx.gemm(A, B), cx.gemm(A, B))
+
+
+TWO_PER_SM_CASES = [  # (batch, M, N, K, transA, transB)
+    (1, 300, 504, 200, False, False), (3, 256, 384, 192, True, False), (3, 256, 384, 192, False, True),
+    (2, 384, 136, 320, True, True), (512, 128, 128, 64, False, False), (37, 200, 136, 72, False, False),
+]
+
+
+@pytest.mark.parametrize("dt", [O.F16, O.BF16])
+@pytest.mark.parametrize("batch,M,N,K,tA,tB", TWO_PER_SM_CASES)
+def test_lowp_two_ctas_per_sm_variant(dev, dt, batch, M, N, K, tA, tB):
+    """The 1-SM kernel with two CTAs per SM (128 x 128 tiles, two stages, or
+    128 x 64 tiles, three stages; 256 TMEM columns per CTA) runs, for every
+    output, the same MMAs over K in the same order as the one-CTA kernel:
+    bit-identical results, and within tolerance of the oracle."""
+    A = O.to_lowp(O.normal((batch, K, M) if tA else (batch, M, K), seed=M + batch) / np.sqrt(K), dt)
+    B = O.to_lowp(O.normal((batch, N, K) if tB else (batch, K, N), seed=N + 3), dt)
+    C0 = O.to_lowp(O.normal((batch, M, N), seed=K), dt)
+    outs = []
+    for variant, kernel in (("tc_128x128_2cta", "gemm_tc_128x128_2cta"), ("tc_128x128", "gemm_tc_128x128"),
+                            ("tc_128x64_2cta", "gemm_tc_128x64_2cta")):
+        Cd = to_dev_lowp(C0, dt, dev)
+        with forced_variant(variant):
+            cx.batched_gemm(to_dev_lowp(A, dt, dev), to_dev_lowp(B, dt, dev), Cd, transA=tA, transB=tB,
+                            alpha=0.75, beta=-0.5)
+        assert cx.last_kernel() == kernel, cx.last_kernel()
+        outs.append(Cd)
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+    for b in sorted({0, batch - 1}):
+        ref = O.gemm_lowp(dt, A[b], B[b], C0[b], transA=tA, transB=tB, alpha=0.75, beta=-0.5)
+        assert O.max_relative(O.from_lowp(lowp_bits(outs[0][b]), dt), O.from_lowp(ref, dt)) <= LOWP_TOL
