@@ -189,8 +189,22 @@ def batched_gemm_host(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, *, alph
         return C
     dev = device or torch.device("cuda", torch.cuda.current_device())
     per_batch = (M * K + K * B.size(2) + M * B.size(2)) * A.element_size()
-    if chunk is None:  # about 16 chunks, each moving at least 4 MiB
-        chunk = max(1, min(batch, max((4 << 20) // per_batch, -(-batch // 16))))
+    if chunk is None:  # about 8 chunks, each moving at least 4 MiB
+        chunk = max(1, min(batch, max((4 << 20) // per_batch, -(-batch // 8))))
+    # Chunk boundaries: the first and the last chunk are half size, so that
+    # the copy-in before the first GEMM and the copy-out after the last one,
+    # which nothing overlaps, are short.
+    bounds = []
+    b0 = 0
+    first = max(1, chunk // 2)
+    while b0 < batch:
+        rest = batch - b0
+        n = first if b0 == 0 else chunk
+        if b0 > 0 and rest <= chunk + chunk // 2:  # tail: split what is left into two, the last half size
+            n = rest - chunk // 2 if rest > chunk // 2 and chunk // 2 > 0 else rest
+        n = min(n, rest)
+        bounds.append((b0, b0 + n))
+        b0 += n
     key = (dev, A.dtype, chunk, M, K, B.size(2), slots)
     st = _streamers.get(key)
     if st is None:
@@ -199,8 +213,7 @@ def batched_gemm_host(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, *, alph
     comp = torch.cuda.current_stream(dev)
     last = None
     with torch.cuda.device(dev):
-        for c, b0 in enumerate(range(0, batch, chunk)):
-            b1 = min(batch, b0 + chunk)
+        for c, (b0, b1) in enumerate(bounds):
             n, s = b1 - b0, c % slots
             with torch.cuda.stream(st.h2d):
                 if c >= slots:
