@@ -9,12 +9,12 @@
 // reference's FFMA chain (gemm.cu:14-42), so results match within that
 // tolerance, not bit for bit (the FFMA kernels in gemm_simt.cu are exact).
 //
-// One persistent CTA per SM, 14 warps:
+// One persistent CTA per SM, 6 + 4 * CG warps (CG = 2 converter groups):
 //   warp 0      TMA producer: fp32 A (128 x 32) and B (BN x 32) tiles into the
 //               "hi" buffers of a STAGES-deep ring: 128-byte swizzle for
 //               K-major operands, 128-byte swizzle with 32-byte atoms for
 //               MN-major ones (the only MN-major layout tf32 MMAs accept).
-//   warps 6..13 converters, two groups of 4 taking alternate K blocks: wait
+//   warps 6..   converters, CG groups of 4 taking K blocks in turn: wait
 //               for a landed stage; split K-major A straight into TMEM
 //               (tcgen05.st, one tile row per thread, the MMAs read A from
 //               TMEM), split B (and an MN-major A) in place in shared memory
@@ -33,15 +33,17 @@ namespace {
 
 constexpr int X3_BM = 128;
 constexpr int X3_BK = 32;  // 32 fp32 = 128 bytes = one swizzle row
-constexpr int X3_THREADS = 448;
 constexpr int X3_EPI_WARPS = 4;
-constexpr int X3_CONV_WARPS = 8;
-// Converter groups: group g splits the K blocks whose sequence number is g
-// modulo the group count, so consecutive stages are split concurrently (the
-// split of one stage ends in a TMEM-store wait, which one group alone would
-// serialise).
-constexpr int X3_CONV_GROUPS = 2;
-constexpr int X3_CONV_PER_GROUP = X3_CONV_WARPS / X3_CONV_GROUPS;
+// Converter groups (template parameter CG): group g splits the K blocks
+// whose sequence number is g modulo CG, so consecutive stages are split
+// concurrently (the split of one stage ends in a TMEM-store wait, which one
+// group alone would serialise).  A group is four warps, one per TMEM lane
+// quarter, because a warp can only store to its own quarter.  Measured on
+// B200: two groups are enough (four gave the same time at 512^3 to 4096^3,
+// ~0.7 us per K block at 1024^3 either way).
+constexpr int X3_CONV_PER_GROUP = 4;
+// Threads per CTA: producer, MMA issuer, 4 epilogue warps, CG converter groups.
+__host__ __device__ constexpr int x3_threads(int cg) { return (6 + X3_CONV_PER_GROUP * cg) * 32; }
 constexpr int X3_CHUNK = 32;  // epilogue columns per TMA store (32 fp32 = 128 bytes)
 
 struct X3Params {
@@ -123,8 +125,8 @@ __device__ __forceinline__ void split_tf32(unsigned char* hi, unsigned char* lo,
   }
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(X3_THREADS, 1)
+template <int BN, int STAGES, bool A_MN, bool B_MN, int CG>
+__global__ void __launch_bounds__(x3_threads(CG), 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ CUtensorMap tmC, const X3Params p) {
   using L = X3Smem<BN, STAGES, A_MN>;
@@ -252,7 +254,7 @@ __global__ void __launch_bounds__(X3_THREADS, 1)
     bool ok = true;
     for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
       for (int kb = 0; kb < p.k_blocks; ++kb, ++seq) {
-        if (seq % X3_CONV_GROUPS == grp) {
+        if (seq % CG == grp) {
           if (!mbar_wait_bounded(&full[stage], phase, kDevErrWaitTimeoutFull, abort_flag)) {
             ok = false;
             break;
@@ -441,7 +443,7 @@ __global__ void __launch_bounds__(X3_THREADS, 1)
   }
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN>
+template <int BN, int STAGES, bool A_MN, bool B_MN, int CG>
 int launch_x3(const GemmProblem& p, cudaStream_t stream, const char* name) {
   using L = X3Smem<BN, STAGES, A_MN>;
   const auto dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
@@ -470,7 +472,7 @@ int launch_x3(const GemmProblem& p, cudaStream_t stream, const char* name) {
   prm.strideC = p.strideC;
   prm.bias = p.bias;
   prm.epi = p.epi;
-  auto kern = gemm_tf32x3_kernel<BN, STAGES, A_MN, B_MN>;
+  auto kern = gemm_tf32x3_kernel<BN, STAGES, A_MN, B_MN, CG>;
   static std::atomic<bool> attr_set[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return CUOPX_CUDA_ERROR;
@@ -480,7 +482,7 @@ int launch_x3(const GemmProblem& p, cudaStream_t stream, const char* name) {
     attr_set[dev].store(true, std::memory_order_relaxed);
   }
   const int grid = std::min(prm.num_tiles, device_sm_count());
-  if (launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(X3_THREADS), L::ALLOC, stream, mA, mB, mC, prm) !=
+  if (launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(x3_threads(CG)), L::ALLOC, stream, mA, mB, mC, prm) !=
       cudaSuccess) {
     cudaGetLastError();
     return CUOPX_CUDA_ERROR;
@@ -491,13 +493,13 @@ int launch_x3(const GemmProblem& p, cudaStream_t stream, const char* name) {
 
 // Stage counts: K-major A (A split in TMEM, smaller stages) runs deeper
 // rings — 6 x 64 or 4 x 64 TMEM columns of A next to the accumulators.
-template <int BN, int STAGES_TMEM_A, int STAGES_SMEM_A>
+template <int BN, int STAGES_TMEM_A, int STAGES_SMEM_A, int CG = 2>
 int launch_x3_layout(const GemmProblem& p, cudaStream_t stream, const char* name) {
   const bool a_mn = p.transA, b_mn = !p.transB;
-  if (!a_mn && b_mn) return launch_x3<BN, STAGES_TMEM_A, false, true>(p, stream, name);
-  if (!a_mn && !b_mn) return launch_x3<BN, STAGES_TMEM_A, false, false>(p, stream, name);
-  if (a_mn && b_mn) return launch_x3<BN, STAGES_SMEM_A, true, true>(p, stream, name);
-  return launch_x3<BN, STAGES_SMEM_A, true, false>(p, stream, name);
+  if (!a_mn && b_mn) return launch_x3<BN, STAGES_TMEM_A, false, true, CG>(p, stream, name);
+  if (!a_mn && !b_mn) return launch_x3<BN, STAGES_TMEM_A, false, false, CG>(p, stream, name);
+  if (a_mn && b_mn) return launch_x3<BN, STAGES_SMEM_A, true, true, CG>(p, stream, name);
+  return launch_x3<BN, STAGES_SMEM_A, true, false, CG>(p, stream, name);
 }
 
 }  // namespace

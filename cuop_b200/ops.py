@@ -189,8 +189,8 @@ def batched_gemm_host(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, *, alph
         return C
     dev = device or torch.device("cuda", torch.cuda.current_device())
     per_batch = (M * K + K * B.size(2) + M * B.size(2)) * A.element_size()
-    if chunk is None:  # about 8 chunks, each moving at least 4 MiB
-        chunk = max(1, min(batch, max((4 << 20) // per_batch, -(-batch // 8))))
+    if chunk is None:  # about 8 chunks, each moving at least 8 MiB (measured best on B200 over PCIe 5)
+        chunk = max(1, min(batch, max((8 << 20) // per_batch, -(-batch // 8))))
     # Chunk boundaries: the first and the last chunk are half size, so that
     # the copy-in before the first GEMM and the copy-out after the last one,
     # which nothing overlaps, are short.
