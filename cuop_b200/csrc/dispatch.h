@@ -81,6 +81,8 @@ int gemm_tc2_peers(const GemmProblem& p, void* const* peers, int npeers, cudaStr
 // 3xTF32 tcgen05 back-end (gemm_tf32x3.cu) for fp32.
 bool gemm_tf32x3_supported(const GemmProblem& p);
 int gemm_tf32x3(const GemmProblem& p, cudaStream_t stream, int bn = 0);  // bn: 0 = choose, 64, 128
+// bn = kTf32x3SplitK2: 128 x 128 tiles, K split over a pair of CTAs (cluster).
+constexpr int kTf32x3SplitK2 = -2;
 
 // ---- variant selection (host/tuning.cpp) ----
 // GEMM variants a tuning table or an override may name.
@@ -96,7 +98,8 @@ enum GemmVariant : int {
   kVariantTc2x512 = 8,     // 2-SM tcgen05, 256 x 512 pair tiles
   kVariantTc128x128x2 = 9, // 1-SM tcgen05, 128 x 128 tiles, two CTAs per SM
   kVariantTc128x64x2 = 10, // 1-SM tcgen05, 128 x 64 tiles, two CTAs per SM
-  kVariantCount = 11,
+  kVariantTf32x3_128k2 = 11, // 3xTF32, 128 x 128 tiles, K split over a CTA pair
+  kVariantCount = 12,
 };
 const char* gemm_variant_name(int v);
 // The override (set by cuopx_set_gemm_variant) if any, else the first

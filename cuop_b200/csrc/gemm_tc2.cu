@@ -102,28 +102,6 @@ struct PairParams {
   int epi;           // CUOPX_EPI_* flags
 };
 
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-__device__ __forceinline__ uint32_t cluster_id_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
-  return r;
-}
-
-// shared::cluster address of the same shared variable in CTA `rank`.
-__device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
-  uint32_t out;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
-  return out;
-}
-
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
 
 // Bounded wait with cluster-scope acquire (data written by the partner CTA
 // before its release-arrive is visible afterwards).
@@ -152,11 +130,6 @@ __device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t* bar, uint32_
   }
 }
 
-__device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, uint4 v) {
-  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "r"(v.x), "r"(v.y), "r"(v.z),
-               "r"(v.w)
-               : "memory");
-}
 
 // Next pair tile from a completed launch-control response (the cancelled
 // cluster's first CTA index / 2); false when none was left.

@@ -58,14 +58,18 @@ struct X3Params {
 
 // A_LO: the stage also holds A's lo part in shared memory (MN-major A);
 // K-major A is split into TMEM instead, and its stages are 16 KB smaller.
-template <int BN, int STAGES, bool A_LO = true>
+// KSPLIT > 1: a receive area for the other ranks' partial sums of this
+// CTA's output columns (split-K over a cluster, see the epilogue).
+template <int BN, int STAGES, bool A_LO = true, int KSPLIT = 1>
 struct X3Smem {
   static constexpr int A_BYTES = X3_BM * X3_BK * 4;  // 16 KB
   static constexpr int B_BYTES = BN * X3_BK * 4;
   static constexpr int STAGE = (A_LO ? 2 : 1) * A_BYTES + 2 * B_BYTES;  // A_hi[, A_lo], B_hi, B_lo
   static constexpr int C_STAGE = 32 * X3_CHUNK * 4;                      // 4 KB
   static constexpr int OFF_C = STAGES * STAGE;
-  static constexpr int OFF_BAR = OFF_C + X3_EPI_WARPS * 2 * C_STAGE;
+  static constexpr int OFF_RECV = OFF_C + X3_EPI_WARPS * 2 * C_STAGE;
+  static constexpr int RECV_SLOT = X3_BM * (BN / KSPLIT) * 4;  // one sender's partial sums
+  static constexpr int OFF_BAR = OFF_RECV + (KSPLIT - 1) * RECV_SLOT;
   // full[S], conv[S], empty[S], acc_full[2], acc_empty[2], drain
   static constexpr int NUM_BARS = 3 * STAGES + 5;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
@@ -125,11 +129,12 @@ __device__ __forceinline__ void split_tf32(unsigned char* hi, unsigned char* lo,
   }
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, int CG>
+template <int BN, int STAGES, bool A_MN, bool B_MN, int CG, int KSPLIT>
 __global__ void __launch_bounds__(x3_threads(CG), 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ CUtensorMap tmC, const X3Params p) {
-  using L = X3Smem<BN, STAGES, A_MN>;
+  using L = X3Smem<BN, STAGES, A_MN, KSPLIT>;
+  static_assert(KSPLIT == 1 || (BN % (KSPLIT * X3_CHUNK) == 0), "split-K owners take whole store chunks");
   constexpr uint32_t STAGE_TX = static_cast<uint32_t>(L::A_BYTES + L::B_BYTES);
   constexpr uint32_t IDESC = make_idesc(2u /*tf32*/, A_MN, B_MN, X3_BM, BN);
   constexpr uint32_t CHUNK_BYTES = 32 * X3_BK * 4;  // one 32 x 32 fp32 box = 4 KB
@@ -155,6 +160,12 @@ __global__ void __launch_bounds__(x3_threads(CG), 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // Work units: tiles, walked persistently (KSPLIT == 1); with KSPLIT > 1
+  // one tile per cluster, rank krank of which sums K blocks [kb0, kb1).
+  const int krank = KSPLIT > 1 ? static_cast<int>(cluster_ctarank()) : 0;
+  const int unit0 = static_cast<int>(blockIdx.x) / KSPLIT;
+  const int ustep = static_cast<int>(gridDim.x) / KSPLIT;
+  const int kb0 = krank * p.k_blocks / KSPLIT, kb1 = (krank + 1) * p.k_blocks / KSPLIT;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -194,11 +205,11 @@ __global__ void __launch_bounds__(x3_threads(CG), 1)
       // parity of the last phase loaded.
       uint32_t issued_mask = 0, phase_mask = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      for (int t = unit0; t < p.num_tiles && ok; t += ustep) {
         int b, mt, nt;
         x3_tile_coords(t, p, b, mt, nt);
         const int m0 = mt * X3_BM, n0 = nt * BN;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, kDevErrWaitTimeoutEmpty, abort_flag)) {
             ok = false;
             break;
@@ -252,8 +263,8 @@ __global__ void __launch_bounds__(x3_threads(CG), 1)
     uint32_t phase = 0;
     int seq = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
-      for (int kb = 0; kb < p.k_blocks; ++kb, ++seq) {
+    for (int t = unit0; t < p.num_tiles && ok; t += ustep) {
+      for (int kb = kb0; kb < kb1; ++kb, ++seq) {
         if (seq % CG == grp) {
           if (!mbar_wait_bounded(&full[stage], phase, kDevErrWaitTimeoutFull, abort_flag)) {
             ok = false;
@@ -308,14 +319,14 @@ __global__ void __launch_bounds__(x3_threads(CG), 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true, issued = false;
-      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      for (int t = unit0; t < p.num_tiles && ok; t += ustep) {
         if (!mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1u, kDevErrWaitTimeoutAccEmpty, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(&conv[stage], phase, kDevErrWaitTimeoutFull, abort_flag)) {
             ok = false;
             break;
@@ -340,11 +351,11 @@ __global__ void __launch_bounds__(x3_threads(CG), 1)
                                       : make_smem_desc_sw128(bl + bo, 16, 1024);
             if constexpr (A_TMEM) {
               const uint32_t ta = tmem_base + A_COL0 + static_cast<uint32_t>(stage * 2 * X3_BK + kk * 8);
-              umma_tf32_a_tmem(d_tmem, ta + X3_BK, dbh, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);  // lo*hi first
+              umma_tf32_a_tmem(d_tmem, ta + X3_BK, dbh, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);  // lo*hi first
               umma_tf32_a_tmem(d_tmem, ta, dbl, IDESC, 1u);
               umma_tf32_a_tmem(d_tmem, ta, dbh, IDESC, 1u);
             } else {
-              umma_tf32(d_tmem, dal, dbh, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);  // small terms first
+              umma_tf32(d_tmem, dal, dbh, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);  // small terms first
               umma_tf32(d_tmem, dah, dbl, IDESC, 1u);
               umma_tf32(d_tmem, dah, dbh, IDESC, 1u);
             }
@@ -374,65 +385,142 @@ __global__ void __launch_bounds__(x3_threads(CG), 1)
     const int q = warp & 3;
     const int row_in_tile = 32 * q + lane;
     unsigned char* const stage_base = smem + L::OFF_C + (warp - 2) * 2 * L::C_STAGE;  // two buffers
-    int acc = 0;
-    uint32_t acc_phase = 0;
     int sbuf = 0;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
-      int b, mt, nt;
-      x3_tile_coords(t, p, b, mt, nt);
-      const int m0 = mt * X3_BM, n0 = nt * BN;
-      if (!mbar_wait_bounded(&acc_full[acc], acc_phase, kDevErrWaitTimeoutAccFull, abort_flag)) break;
-      tc_fence_after_sync();
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(acc * BN);
+    // alpha/beta, bias, ReLU on the fp32 sums of output chunk `ch` of a tile
+    // (this thread's row), swizzled staging, TMA store.
+    auto finish_chunk = [&](float (&v)[32], int b, int m0, int n0, int ch) {
       const int64_t grow = static_cast<int64_t>(m0) + row_in_tile;
-#pragma unroll 1
-      for (int ch = 0; ch < BN / X3_CHUNK; ++ch) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + ch * X3_CHUNK, r);
-        tmem_wait_ld();
-        if (ch == BN / X3_CHUNK - 1) {
-          tc_fence_before_sync();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&acc_empty[acc]);
-        }
-        float v[32];
+      const int64_t gcol0 = static_cast<int64_t>(n0) + ch * X3_CHUNK;
+      if (p.beta != 0.f && grow < p.M) {
+        const float* crow = p.C_in + static_cast<int64_t>(b) * p.strideC + grow * p.ldc;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-        if (p.beta != 0.f && grow < p.M) {
-          const int64_t gcol0 = static_cast<int64_t>(n0) + ch * X3_CHUNK;
-          const float* crow = p.C_in + static_cast<int64_t>(b) * p.strideC + grow * p.ldc;
+        for (int i = 0; i < 32; ++i)
+          v[i] = gcol0 + i < p.N ? epi_axpby(p.alpha, v[i], p.beta, crow[gcol0 + i]) : epi_scale(p.alpha, v[i]);
+      } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            v[i] = gcol0 + i < p.N ? epi_axpby(p.alpha, v[i], p.beta, crow[gcol0 + i]) : epi_scale(p.alpha, v[i]);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = epi_scale(p.alpha, v[i]);
-        }
-        if (p.epi) {
-          const int64_t gcol0 = static_cast<int64_t>(n0) + ch * X3_CHUNK;
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (gcol0 + i < p.N) v[i] = apply_epilogue<float>(v[i], p.bias, gcol0 + i, p.epi);
-        }
-        if (lane == 0) bulk_wait_group_read<1>();
-        __syncwarp();
-        unsigned char* sbase = stage_base + sbuf * L::C_STAGE;
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          *reinterpret_cast<float4*>(sbase + lane * 128 + ((j ^ (lane & 7)) << 4)) =
-              make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-        fence_proxy_async_shared();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_3d(&tmC, sbase, n0 + ch * X3_CHUNK, m0 + 32 * q, b);
-          bulk_commit_group();
-        }
-        sbuf ^= 1;
+        for (int i = 0; i < 32; ++i) v[i] = epi_scale(p.alpha, v[i]);
       }
-      if (++acc == 2) acc = 0, acc_phase ^= 1u;
+      if (p.epi) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (gcol0 + i < p.N) v[i] = apply_epilogue<float>(v[i], p.bias, gcol0 + i, p.epi);
+      }
+      if (lane == 0) bulk_wait_group_read<1>();
+      __syncwarp();
+      unsigned char* sbase = stage_base + sbuf * L::C_STAGE;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        *reinterpret_cast<float4*>(sbase + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+            make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      fence_proxy_async_shared();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_3d(&tmC, sbase, n0 + ch * X3_CHUNK, m0 + 32 * q, b);
+        bulk_commit_group();
+      }
+      sbuf ^= 1;
+    };
+    if constexpr (KSPLIT == 1) {
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int t = unit0; t < p.num_tiles; t += ustep) {
+        int b, mt, nt;
+        x3_tile_coords(t, p, b, mt, nt);
+        if (!mbar_wait_bounded(&acc_full[acc], acc_phase, kDevErrWaitTimeoutAccFull, abort_flag)) break;
+        tc_fence_after_sync();
+        const uint32_t t_row = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+        for (int ch = 0; ch < BN / X3_CHUNK; ++ch) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + ch * X3_CHUNK, r);
+          tmem_wait_ld();
+          if (ch == BN / X3_CHUNK - 1) {
+            tc_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[acc]);
+          }
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+          finish_chunk(v, b, mt * X3_BM, nt * BN, ch);
+        }
+        if (++acc == 2) acc = 0, acc_phase ^= 1u;
+      }
+    } else {
+      // Split K: rank r of the cluster owns output columns [r*OWN, (r+1)*OWN)
+      // of the tile.  Each rank first writes the raw fp32 partial sums of
+      // the other ranks' columns into their receive areas (distributed
+      // shared memory), then, after a cluster barrier, adds the partial sums
+      // of its own columns in rank order 0, 1, ... — a fixed order, so the
+      // result does not depend on timing — and finishes them.
+      static_assert(KSPLIT == 2, "the in-place sum below is the fixed order only for two ranks");
+      constexpr int OWN = BN / KSPLIT;
+      constexpr int CPO = OWN / X3_CHUNK;  // store chunks per owner
+      int b = 0, mt = 0, nt = 0;
+      x3_tile_coords(unit0, p, b, mt, nt);
+      const bool got = unit0 < p.num_tiles &&
+                       mbar_wait_bounded(&acc_full[0], 0, kDevErrWaitTimeoutAccFull, abort_flag);
+      if (got) tc_fence_after_sync();
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(32 * q) << 16);
+      // Receive rows are OWN fp32 (OWN / 4 16-byte granules); granule g of
+      // row r lives at g ^ (r & 15), so a warp's 32 rows spread over banks.
+      const uint32_t rsw = static_cast<uint32_t>(row_in_tile & 15);
+      for (int dst = 0; dst < KSPLIT; ++dst) {
+        if (dst == krank) continue;
+        const int slot = krank < dst ? krank : krank - 1;  // this rank's slot in dst's receive area
+        const uint32_t rrow =
+            map_to_rank(smem + L::OFF_RECV + slot * L::RECV_SLOT + row_in_tile * OWN * 4, static_cast<uint32_t>(dst));
+#pragma unroll 1
+        for (int c = 0; c < CPO; ++c) {
+          uint32_t r[32];
+          if (got) {
+            tmem_ld_32x32b_x32(t_row + (dst * CPO + c) * X3_CHUNK, r);
+            tmem_wait_ld();
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = 0u;
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t g = static_cast<uint32_t>(c * 8 + j) ^ rsw;
+            st_cluster_v4(rrow + (g << 4), make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]));
+          }
+        }
+      }
+      cluster_sync_all();  // every rank's partial sums of this rank's columns have landed
+      if (got) {
+        const unsigned char* rrow = smem + L::OFF_RECV + row_in_tile * OWN * 4;
+#pragma unroll 1
+        for (int c = 0; c < CPO; ++c) {
+          const int ch = krank * CPO + c;
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + ch * X3_CHUNK, r);
+          tmem_wait_ld();
+          // Two ranks: the fixed-order sum p0 + p1 is one IEEE addition,
+          // which is commutative, so each rank adds the partner's part to
+          // its own in place.
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 f = *reinterpret_cast<const float4*>(rrow + ((static_cast<uint32_t>(c * 8 + j) ^ rsw) << 4));
+            v[4 * j] = __fadd_rn(v[4 * j], f.x);
+            v[4 * j + 1] = __fadd_rn(v[4 * j + 1], f.y);
+            v[4 * j + 2] = __fadd_rn(v[4 * j + 2], f.z);
+            v[4 * j + 3] = __fadd_rn(v[4 * j + 3], f.w);
+          }
+          finish_chunk(v, b, mt * X3_BM, nt * BN, ch);
+        }
+      }
     }
     if (lane == 0) bulk_wait_group<0>();
     __syncwarp();
+  }
+  // Split K: the other roles take part in the one cluster barrier too (the
+  // epilogue warps passed it above), before the CTA-wide barrier below.
+  if constexpr (KSPLIT > 1) {
+    if (warp < 2 || warp >= 6) cluster_sync_all();
   }
 
   tc_fence_before_sync();
@@ -443,9 +531,9 @@ __global__ void __launch_bounds__(x3_threads(CG), 1)
   }
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, int CG>
+template <int BN, int STAGES, bool A_MN, bool B_MN, int CG, int KSPLIT>
 int launch_x3(const GemmProblem& p, cudaStream_t stream, const char* name) {
-  using L = X3Smem<BN, STAGES, A_MN>;
+  using L = X3Smem<BN, STAGES, A_MN, KSPLIT>;
   const auto dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   CUtensorMap mA, mB, mC;
   bool ok = true;
@@ -472,7 +560,7 @@ int launch_x3(const GemmProblem& p, cudaStream_t stream, const char* name) {
   prm.strideC = p.strideC;
   prm.bias = p.bias;
   prm.epi = p.epi;
-  auto kern = gemm_tf32x3_kernel<BN, STAGES, A_MN, B_MN, CG>;
+  auto kern = gemm_tf32x3_kernel<BN, STAGES, A_MN, B_MN, CG, KSPLIT>;
   static std::atomic<bool> attr_set[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return CUOPX_CUDA_ERROR;
@@ -481,9 +569,15 @@ int launch_x3(const GemmProblem& p, cudaStream_t stream, const char* name) {
       return CUOPX_CUDA_ERROR;
     attr_set[dev].store(true, std::memory_order_relaxed);
   }
-  const int grid = std::min(prm.num_tiles, device_sm_count());
-  if (launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(x3_threads(CG)), L::ALLOC, stream, mA, mB, mC, prm) !=
-      cudaSuccess) {
+  cudaError_t err;
+  if constexpr (KSPLIT > 1) {  // one cluster of KSPLIT CTAs per tile
+    err = launch_pdl_cluster(kern, dim3(static_cast<unsigned>(prm.num_tiles * KSPLIT)), dim3(x3_threads(CG)), L::ALLOC,
+                             stream, KSPLIT, mA, mB, mC, prm);
+  } else {  // persistent: at most one CTA per SM
+    const int grid = std::min(prm.num_tiles, device_sm_count());
+    err = launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(x3_threads(CG)), L::ALLOC, stream, mA, mB, mC, prm);
+  }
+  if (err != cudaSuccess) {
     cudaGetLastError();
     return CUOPX_CUDA_ERROR;
   }
@@ -493,13 +587,13 @@ int launch_x3(const GemmProblem& p, cudaStream_t stream, const char* name) {
 
 // Stage counts: K-major A (A split in TMEM, smaller stages) runs deeper
 // rings — 6 x 64 or 4 x 64 TMEM columns of A next to the accumulators.
-template <int BN, int STAGES_TMEM_A, int STAGES_SMEM_A, int CG = 2>
+template <int BN, int STAGES_TMEM_A, int STAGES_SMEM_A, int CG = 2, int KSPLIT = 1>
 int launch_x3_layout(const GemmProblem& p, cudaStream_t stream, const char* name) {
   const bool a_mn = p.transA, b_mn = !p.transB;
-  if (!a_mn && b_mn) return launch_x3<BN, STAGES_TMEM_A, false, true, CG>(p, stream, name);
-  if (!a_mn && !b_mn) return launch_x3<BN, STAGES_TMEM_A, false, false, CG>(p, stream, name);
-  if (a_mn && b_mn) return launch_x3<BN, STAGES_SMEM_A, true, true, CG>(p, stream, name);
-  return launch_x3<BN, STAGES_SMEM_A, true, false, CG>(p, stream, name);
+  if (!a_mn && b_mn) return launch_x3<BN, STAGES_TMEM_A, false, true, CG, KSPLIT>(p, stream, name);
+  if (!a_mn && !b_mn) return launch_x3<BN, STAGES_TMEM_A, false, false, CG, KSPLIT>(p, stream, name);
+  if (a_mn && b_mn) return launch_x3<BN, STAGES_SMEM_A, true, true, CG, KSPLIT>(p, stream, name);
+  return launch_x3<BN, STAGES_SMEM_A, true, false, CG, KSPLIT>(p, stream, name);
 }
 
 }  // namespace
@@ -521,10 +615,17 @@ int gemm_tf32x3(const GemmProblem& p, cudaStream_t stream, int bn) {
   if (bn == 0) {
     const int sms = device_sm_count();
     const int64_t tiles128 = ((p.M + X3_BM - 1) / X3_BM) * ((p.N + 127) / 128) * p.batch;
+    const int64_t k_blocks = (p.K + X3_BK - 1) / X3_BK;
+    // Too few 128 x 128 tiles to fill the part but a long K loop: split K
+    // over CTA pairs (twice the CTAs, half the K loop each).
+    if (p.N > 64 && tiles128 * 2 <= sms && k_blocks >= 8) bn = kTf32x3SplitK2;
     // 128 x 128 tiles halve B traffic per FLOP; measured on B200 they win
     // from about two thirds of an SM wave of them.
     bn = (p.N > 64 && tiles128 * 3 >= sms * 2) ? 128 : 64;
   }
+  // Each rank of the pair needs at least one K block of its own.
+  if (bn == kTf32x3SplitK2 && (p.K + X3_BK - 1) / X3_BK < 2) bn = 128;
+  if (bn == kTf32x3SplitK2) return launch_x3_layout<128, 3, 2, 2, 2>(p, stream, "gemm_tf32x3_128x128_k2");
   if (bn == 128) return launch_x3_layout<128, 4, 3>(p, stream, "gemm_tf32x3_128x128");
   return launch_x3_layout<64, 6, 4>(p, stream, "gemm_tf32x3_128x64");
 }

@@ -333,3 +333,48 @@ def test_lowp_two_ctas_per_sm_variant(dev, dt, batch, M, N, K, tA, tB):
     for b in sorted({0, batch - 1}):
         ref = O.gemm_lowp(dt, A[b], B[b], C0[b], transA=tA, transB=tB, alpha=0.75, beta=-0.5)
         assert O.max_relative(O.from_lowp(lowp_bits(outs[0][b]), dt), O.from_lowp(ref, dt)) <= LOWP_TOL
+
+
+SPLITK_CASES = [  # (batch, M, N, K, transA, transB)
+    (1, 1024, 1024, 1024, False, False), (1, 512, 512, 512, False, False), (1, 384, 320, 1000, False, False),
+    (1, 256, 192, 416, True, False), (1, 256, 264, 96, False, True), (3, 256, 128, 384, True, True),
+]
+
+
+@pytest.mark.parametrize("batch,M,N,K,tA,tB", SPLITK_CASES)
+def test_f32_tf32x3_split_k_pair(dev, batch, M, N, K, tA, tB):
+    """3xTF32 with K split over a CTA pair (partial sums exchanged through
+    distributed shared memory, added in a fixed order): within a tenth of the
+    fp32 bound of an fp64 product, with alpha/beta and a fused bias + ReLU,
+    and the same bits on every run."""
+    A32 = O.uniform((batch, K, M) if tA else (batch, M, K), seed=M + K)
+    B32 = O.uniform((batch, N, K) if tB else (batch, K, N), seed=N + 1)
+    C32 = O.uniform((batch, M, N), seed=7)
+    A, B = to_dev_f32(A32, dev), to_dev_f32(B32, dev)
+    outs = []
+    for _ in range(2):
+        Cd = to_dev_f32(C32, dev)
+        with forced_variant("tf32x3_128x128_k2"):
+            cx.batched_gemm(A, B, Cd, transA=tA, transB=tB, alpha=0.75, beta=-0.5)
+        assert cx.last_kernel() == "gemm_tf32x3_128x128_k2", cx.last_kernel()
+        outs.append(Cd)
+    assert torch.equal(outs[0], outs[1])
+    opA = np.swapaxes(A32, 1, 2) if tA else A32
+    opB = np.swapaxes(B32, 1, 2) if tB else B32
+    exact = 0.75 * np.einsum("bmk,bkn->bmn", opA.astype(np.float64), opB.astype(np.float64)) - 0.5 * C32
+    assert O.rel_frobenius(outs[0].cpu().numpy(), exact) <= 0.1 * 1e-5 * np.sqrt(K)
+    if batch == 1 and not tA and not tB:
+        bias = to_dev_f32(O.uniform(N, seed=9), dev)
+        with forced_variant("tf32x3_128x128_k2"):
+            Cr = cx.gemm(A[0], B[0], bias=bias, relu=True)
+        ref = np.maximum(A32[0].astype(np.float64) @ B32[0].astype(np.float64) + bias.double().cpu().numpy(), 0.0)
+        assert O.rel_frobenius(Cr.cpu().numpy(), ref) <= 0.1 * 1e-5 * np.sqrt(K)
+
+
+def test_f32_1024_default_takes_split_k(dev):
+    """C1 (1024^3, 64 tiles of 128 x 128) fills the part with K split over
+    CTA pairs."""
+    A = to_dev_f32(O.uniform((1024, 1024), seed=0), dev)
+    B = to_dev_f32(O.uniform((1024, 1024), seed=1), dev)
+    cx.gemm(A, B)
+    assert cx.last_kernel() == "gemm_tf32x3_128x128_k2"
