@@ -618,10 +618,13 @@ int gemm_tf32x3(const GemmProblem& p, cudaStream_t stream, int bn) {
     const int64_t k_blocks = (p.K + X3_BK - 1) / X3_BK;
     // Too few 128 x 128 tiles to fill the part but a long K loop: split K
     // over CTA pairs (twice the CTAs, half the K loop each).
-    if (p.N > 64 && tiles128 * 2 <= sms && k_blocks >= 8) bn = kTf32x3SplitK2;
-    // 128 x 128 tiles halve B traffic per FLOP; measured on B200 they win
-    // from about two thirds of an SM wave of them.
-    bn = (p.N > 64 && tiles128 * 3 >= sms * 2) ? 128 : 64;
+    if (p.N > 64 && tiles128 * 2 <= sms && k_blocks >= 8) {
+      bn = kTf32x3SplitK2;
+    } else {
+      // 128 x 128 tiles halve B traffic per FLOP; measured on B200 they win
+      // from about two thirds of an SM wave of them.
+      bn = (p.N > 64 && tiles128 * 3 >= sms * 2) ? 128 : 64;
+    }
   }
   // Each rank of the pair needs at least one K block of its own.
   if (bn == kTf32x3SplitK2 && (p.K + X3_BK - 1) / X3_BK < 2) bn = 128;
