@@ -122,6 +122,7 @@ int run_variant(int v, const GemmProblem& p, cudaStream_t stream) {
   switch (v) {
     case kVariantTc2: return tc_ok ? gemm_tc2(p, stream, 256) : -1;
     case kVariantTc2x512: return tc_ok ? gemm_tc2(p, stream, 512) : -1;
+    case kVariantTc2x128: return tc_ok ? gemm_tc2(p, stream, 128) : -1;
     case kVariantTc128x256: return tc_ok ? gemm_tc(p, stream, 256) : -1;
     case kVariantTc128x128: return tc_ok ? gemm_tc(p, stream, 128) : -1;
     case kVariantTc128x128x2: return tc_ok ? gemm_tc(p, stream, kTc128x128TwoPerSm) : -1;

@@ -71,7 +71,7 @@ int gemm_tc_peers(const GemmProblem& p, void* const* peers, int npeers, cudaStre
 
 // Two-SM (cta_group::2) tcgen05 back-end (gemm_tc2.cu) for large fp16/bf16.
 bool gemm_tc2_wanted(const GemmProblem& p);
-// pbn: pair tile width, 256 or 512; 0 = choose (gemm_tc2_pick_width).
+// pbn: pair tile width, 128, 256 or 512; 0 = choose (gemm_tc2_pick_width).
 int gemm_tc2_pick_width(const GemmProblem& p, bool peers);
 int gemm_tc2(const GemmProblem& p, cudaStream_t stream, int pbn = 0);
 // Same kernel; every output chunk is also stored to peers[0..npeers) (peer
@@ -99,7 +99,8 @@ enum GemmVariant : int {
   kVariantTc128x128x2 = 9, // 1-SM tcgen05, 128 x 128 tiles, two CTAs per SM
   kVariantTc128x64x2 = 10, // 1-SM tcgen05, 128 x 64 tiles, two CTAs per SM
   kVariantTf32x3_128k2 = 11, // 3xTF32, 128 x 128 tiles, K split over a CTA pair
-  kVariantCount = 12,
+  kVariantTc2x128 = 12,    // 2-SM tcgen05, 256 x 128 pair tiles
+  kVariantCount = 13,
 };
 const char* gemm_variant_name(int v);
 // The override (set by cuopx_set_gemm_variant) if any, else the first

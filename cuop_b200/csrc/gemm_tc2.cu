@@ -1,13 +1,18 @@
 // Two-SM tcgen05 GEMM (cta_group::2) for large fp16/bf16 problems.
 //
-// A cluster of two CTAs on two SMs owns a 256 x PBN output tile (PBN = 256 or
-// 512).  CTA r of the pair loads rows [128r, 128r+128) of the A tile and, for
-// each 256-column slot h of the tile, columns [256h + 128r, 256h + 128r + 128)
+// A cluster of two CTAs on two SMs owns a 256 x PBN output tile (PBN = 128,
+// 256 or 512).  A slot is SLOT = min(PBN, 256) accumulator columns, the N of
+// one MMA.  CTA r of the pair loads rows [128r, 128r+128) of the A tile and,
+// for each slot h of the tile, columns [SLOT h + SLOT/2 r, SLOT h + SLOT/2 (r+1))
 // of the B tile into its own shared memory; one tcgen05.mma.cta_group::2
-// (M=256, N=256, K=16) per slot, issued by the even CTA, reads both CTAs'
+// (M=256, N=SLOT, K=16) per slot, issued by the even CTA, reads both CTAs'
 // halves and writes each CTA's 128 accumulator rows of that slot into the
-// CTA's TMEM (slot h = columns [256h, 256h+256) of the 512).  Per SM this
-// halves the shared-memory operand traffic of the 1-SM 128 x 256 kernel.
+// CTA's TMEM (512 / SLOT slots).  Per SM this halves the shared-memory
+// operand traffic of the 1-SM kernel of the same tile width.
+//   PBN = 128: 7-stage ring of 24 KB, four TMEM slots rotating between
+//              tiles; a tile's outputs are ready after half the MMA time of
+//              a 256 x 256 tile, which the peer-store path can use to start
+//              its NVLink traffic earlier.
 //   PBN = 256: 6-stage ring of 32 KB; the two TMEM slots alternate between
 //              tiles, so the epilogue of a tile overlaps the next one.
 //   PBN = 512: 4-stage ring of 48 KB; a tile fills both slots, so each K
@@ -48,8 +53,7 @@ constexpr int P_THREADS = 192;
 constexpr int P_EPI_WARPS = 4;
 constexpr int P_CHUNK = 64;
 constexpr uint32_t P_TMEM_COLS = 512;
-constexpr int P_SLOT_COLS = 256;  // accumulator columns of one MMA (N = 256)
-constexpr int P_SLOTS = 2;        // TMEM holds two slots
+constexpr int P_MAX_SLOTS = 4;    // TMEM slots at the narrowest tile (128 columns each)
 constexpr int P_GROUP_M = 8;      // pair-row tiles per raster group
 // Scheduler ring depth (> the producers' lead over the epilogue, in tiles).
 constexpr int P_CLC_SLOTS = 16;
@@ -59,24 +63,26 @@ constexpr int P_CLC_READERS = (2 + P_EPI_WARPS) + (1 + P_EPI_WARPS);
 
 template <int PBN>
 struct PairCfg {
-  static_assert(PBN == 256 || PBN == 512, "pair tile width");
-  static constexpr int SPT = PBN / P_SLOT_COLS;  // TMEM slots per tile
-  static constexpr int STAGES = SPT == 1 ? 6 : 4;
+  static_assert(PBN == 128 || PBN == 256 || PBN == 512, "pair tile width");
+  static constexpr int SLOT = PBN < 256 ? PBN : 256;               // accumulator columns of one MMA (its N)
+  static constexpr int SLOTS = static_cast<int>(P_TMEM_COLS) / SLOT;  // TMEM slots
+  static constexpr int SPT = PBN / SLOT;                           // TMEM slots per tile
+  static constexpr int STAGES = PBN == 128 ? 7 : (SPT == 1 ? 6 : 4);
 };
 
 template <int PBN>
 struct PairSmem {
   static constexpr int STAGES = PairCfg<PBN>::STAGES;
   static constexpr int A_STAGE = P_BM * P_BK * 2;               // 16 KB
-  static constexpr int B_PIECE = (P_SLOT_COLS / 2) * P_BK * 2;  // 16 KB: this CTA's half of one slot
+  static constexpr int B_PIECE = (PairCfg<PBN>::SLOT / 2) * P_BK * 2;  // this CTA's half of one slot
   static constexpr int B_STAGE = PairCfg<PBN>::SPT * B_PIECE;
   static constexpr int C_STAGE = 32 * P_CHUNK * 2;              // 4 KB
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = STAGES * A_STAGE;
   static constexpr int OFF_C = OFF_B + STAGES * B_STAGE;
   static constexpr int OFF_BAR = OFF_C + P_EPI_WARPS * 2 * C_STAGE;
-  // full[S], empty[S], acc_full[2], acc_empty[2], drain
-  static constexpr int NUM_BARS = 2 * STAGES + 2 * P_SLOTS + 1;
+  // full[S], empty[S], acc_full[SLOTS], acc_empty[SLOTS], drain
+  static constexpr int NUM_BARS = 2 * STAGES + 2 * PairCfg<PBN>::SLOTS + 1;
   // Tile-scheduler ring: P_CLC_SLOTS 16-byte launch-control responses, then
   // clc_full[P_CLC_SLOTS] and clc_empty[P_CLC_SLOTS] mbarriers.
   static constexpr int OFF_CLC = (OFF_BAR + NUM_BARS * 8 + 15) / 16 * 16;
@@ -212,6 +218,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
   using L = PairSmem<PBN>;
   constexpr int SPT = PairCfg<PBN>::SPT;
   constexpr int P_STAGES = PairCfg<PBN>::STAGES;
+  constexpr int P_SLOT_COLS = PairCfg<PBN>::SLOT;
+  constexpr int P_SLOTS = PairCfg<PBN>::SLOTS;
   constexpr int CHUNKS_PER_SLOT = P_SLOT_COLS / P_CHUNK;
   constexpr uint32_t PAIR_TX = 2u * static_cast<uint32_t>(L::A_STAGE + L::B_STAGE);
   constexpr uint32_t AB_FMT = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
@@ -402,7 +410,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     if (leader && lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      int acc = 0;              // first TMEM slot of the tile (alternates when SPT == 1)
+      int acc = 0;              // first TMEM slot of the tile (rotates when SPT == 1)
       uint32_t empty_bits = 0;  // bit s: parity of slot s's next acc_empty phase
       bool ok = true, issued = false;
       for (int seq = 0; ok; ++seq) {
@@ -454,7 +462,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
         umma_commit_pair(&acc_full[s0]);
 #pragma unroll
         for (int h = 0; h < SPT; ++h) empty_bits ^= 1u << (s0 + h);
-        if (SPT == 1) acc ^= 1;
+        if (SPT == 1) acc = acc + 1 == P_SLOTS ? 0 : acc + 1;
         const int cs = seq % P_CLC_SLOTS;
         if (!mbar_wait_bounded(&clc_full[cs], static_cast<uint32_t>(seq / P_CLC_SLOTS) & 1u, kDevErrWaitTimeoutFull,
                                abort_flag))
@@ -481,7 +489,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     const int q = warp & 3;
     const int row_in_tile = 32 * q + lane;
     unsigned char* const stage_base = smem + L::OFF_C + (warp - 2) * 2 * L::C_STAGE;  // two buffers
-    int acc = 0;             // first TMEM slot of the tile (alternates when SPT == 1)
+    int acc = 0;             // first TMEM slot of the tile (rotates when SPT == 1)
     uint32_t full_bits = 0;  // bit s: parity of slot s's next acc_full phase
     int sbuf = 0;
     const T* Cin = static_cast<const T*>(p.C_in);
@@ -574,7 +582,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
         sbuf ^= 1;
       }
       full_bits ^= 1u << s0;
-      if (SPT == 1) acc ^= 1;
+      if (SPT == 1) acc = acc + 1 == P_SLOTS ? 0 : acc + 1;
       const int cs = seq % P_CLC_SLOTS;
       const uint32_t cpar = static_cast<uint32_t>(seq / P_CLC_SLOTS) & 1u;
       const bool got = leader ? mbar_wait_bounded(&clc_full[cs], cpar, kDevErrWaitTimeoutAccFull, abort_flag)
@@ -608,6 +616,7 @@ template <typename T, bool A_MN, bool B_MN, int PBN>
 int launch_tc2(const GemmProblem& p, cudaStream_t stream, const char* name, void* const* peers = nullptr,
                int npeers = 0) {
   using L = PairSmem<PBN>;
+  constexpr int P_SLOT_COLS = PairCfg<PBN>::SLOT;
   const CUtensorMapDataType dt =
       std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap mA, mB, mC;
@@ -682,8 +691,9 @@ namespace {
 template <int PBN>
 int launch_tc2_layout(const GemmProblem& p, void* const* peers, int npeers, cudaStream_t stream) {
   const bool a_mn = p.transA, b_mn = !p.transB;
-  const char* name = PBN == 512 ? (npeers > 0 ? "gemm_tc2_256x512_peer" : "gemm_tc2_256x512")
-                                : (npeers > 0 ? "gemm_tc2_256x256_peer" : "gemm_tc2_256x256");
+  const char* name = PBN == 512   ? (npeers > 0 ? "gemm_tc2_256x512_peer" : "gemm_tc2_256x512")
+                     : PBN == 256 ? (npeers > 0 ? "gemm_tc2_256x256_peer" : "gemm_tc2_256x256")
+                                  : (npeers > 0 ? "gemm_tc2_256x128_peer" : "gemm_tc2_256x128");
   if (p.dtype == CUOPX_BF16) {
     if (!a_mn && b_mn) return launch_tc2<__nv_bfloat16, false, true, PBN>(p, stream, name, peers, npeers);
     if (!a_mn && !b_mn) return launch_tc2<__nv_bfloat16, false, false, PBN>(p, stream, name, peers, npeers);
@@ -719,6 +729,7 @@ int gemm_tc2_pick_width(const GemmProblem& p, bool peers) {
 
 int gemm_tc2_peers(const GemmProblem& p, void* const* peers, int npeers, cudaStream_t stream, int pbn) {
   if (pbn == 0) pbn = gemm_tc2_pick_width(p, npeers > 0);
+  if (pbn == 128) return launch_tc2_layout<128>(p, peers, npeers, stream);
   return pbn == 512 ? launch_tc2_layout<512>(p, peers, npeers, stream)
                     : launch_tc2_layout<256>(p, peers, npeers, stream);
 }

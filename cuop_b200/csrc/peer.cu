@@ -185,6 +185,7 @@ int cuopx_gemm_allgather(int dtype, int transA, int transB, int64_t M, int64_t N
   if (v == kVariantTc128x128) return gemm_tc_peers(p, peers, np, s, 128);
   if (v == kVariantTc2) return gemm_tc2_peers(p, peers, np, s, 256);
   if (v == kVariantTc2x512) return gemm_tc2_peers(p, peers, np, s, 512);
+  if (v == kVariantTc2x128) return gemm_tc2_peers(p, peers, np, s, 128);
   return gemm_tc2_peers(p, peers, np, s);
 }
 

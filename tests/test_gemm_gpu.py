@@ -171,7 +171,8 @@ PAIR_CASES = [  # the two-SM (cta_group::2) kernel, forced (ragged and transpose
 ]
 
 
-@pytest.mark.parametrize("variant,kernel", [("tc2", "gemm_tc2_256x256"), ("tc2_256x512", "gemm_tc2_256x512")])
+@pytest.mark.parametrize("variant,kernel", [("tc2", "gemm_tc2_256x256"), ("tc2_256x512", "gemm_tc2_256x512"),
+                                            ("tc2_256x128", "gemm_tc2_256x128")])
 @pytest.mark.parametrize("dt", [O.F16, O.BF16])
 @pytest.mark.parametrize("M,N,K,tA,tB", PAIR_CASES)
 def test_lowp_pair_kernel_vs_oracle(dev, dt, M, N, K, tA, tB, variant, kernel):

@@ -44,7 +44,7 @@ CASES = [  # (world, M, nb, K, tA, tB)
 
 
 PATHS = [("tc2", "gemm_tc2_256x256"), ("tc2_256x512", "gemm_tc2_256x512"), ("tc_128x128", "gemm_tc_128x128"),
-         ("tc_128x256", "gemm_tc_128x256")]
+         ("tc_128x256", "gemm_tc_128x256"), ("tc2_256x128", "gemm_tc2_256x128")]
 
 
 @pytest.mark.parametrize("variant,kernel", PATHS)
