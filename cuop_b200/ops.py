@@ -14,6 +14,8 @@ and argument meaning follow cuOP's operators:
 from __future__ import annotations
 
 import ctypes as C
+import threading
+from collections import OrderedDict
 from typing import Optional
 
 import torch
@@ -145,12 +147,14 @@ class _HostStreamer:
     """Device staging for batched_gemm_host on one device: `slots` chunk
     buffers for A, B and C, a host-to-device and a device-to-host copy
     stream, and one event per slot and stage.  Kept between calls (a call
-    after the first allocates nothing)."""
+    after the first allocates nothing); `lock` serialises calls that share
+    it (several host threads with the same shape)."""
 
     def __init__(self, device: torch.device, dtype: torch.dtype, chunk: int, shapes, slots: int):
         (m, k), (k2, n) = shapes
         self.key = (device, dtype, chunk, m, k, n, slots)
         self.slots = slots
+        self.lock = threading.Lock()
         self.dA = [torch.empty((chunk, m, k), dtype=dtype, device=device) for _ in range(slots)]
         self.dB = [torch.empty((chunk, k2, n), dtype=dtype, device=device) for _ in range(slots)]
         self.dC = [torch.empty((chunk, m, n), dtype=dtype, device=device) for _ in range(slots)]
@@ -161,7 +165,11 @@ class _HostStreamer:
         self.stored = [torch.cuda.Event() for _ in range(slots)]
 
 
-_streamers: dict = {}
+# Staging sets by (device, dtype, chunk, shape, slots), least recently used
+# first; at most _MAX_STREAMERS are kept.
+_streamers: "OrderedDict" = OrderedDict()
+_streamers_lock = threading.Lock()
+_MAX_STREAMERS = 4
 
 
 def batched_gemm_host(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, *, alpha: float = 1.0, beta: float = 0.0,
@@ -206,10 +214,23 @@ def batched_gemm_host(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, *, alph
         bounds.append((b0, b0 + n))
         b0 += n
     key = (dev, A.dtype, chunk, M, K, B.size(2), slots)
-    st = _streamers.get(key)
-    if st is None:
-        st = _HostStreamer(dev, A.dtype, chunk, ((M, K), (K, B.size(2))), slots)
-        _streamers[key] = st
+    with _streamers_lock:
+        st = _streamers.get(key)
+        if st is None:
+            st = _HostStreamer(dev, A.dtype, chunk, ((M, K), (K, B.size(2))), slots)
+            _streamers[key] = st
+            while len(_streamers) > _MAX_STREAMERS:  # drop the least recently used (idle: calls end synchronised)
+                old_key, old_st = next(iter(_streamers.items()))
+                if old_st.lock.locked():
+                    break
+                del _streamers[old_key]
+        _streamers.move_to_end(key)
+    with st.lock:
+        return _stream_batches(st, A, B, C, alpha, beta, bounds, dev)
+
+
+def _stream_batches(st: "_HostStreamer", A, B, C, alpha, beta, bounds, dev):
+    slots = st.slots
     comp = torch.cuda.current_stream(dev)
     last = None
     with torch.cuda.device(dev):
