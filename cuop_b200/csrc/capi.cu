@@ -130,6 +130,7 @@ int run_variant(int v, const GemmProblem& p, cudaStream_t stream) {
     case kVariantTf32x3_64: return x3_ok ? gemm_tf32x3(p, stream, 64) : -1;
     case kVariantTf32x3_128: return x3_ok ? gemm_tf32x3(p, stream, 128) : -1;
     case kVariantTf32x3_128k2: return x3_ok ? gemm_tf32x3(p, stream, kTf32x3SplitK2) : -1;
+    case kVariantTf32x3Pair: return x3_ok ? gemm_tf32x3(p, stream, kTf32x3PairSplitK2) : -1;
     case kVariantFfma: return ffma_ok ? gemm_simt_f32(p, stream) : -1;
     case kVariantGeneric:
       return (p.dtype == CUOPX_F32 && mode == CUOPX_FP32_TF32X3 && gemm_tf32x3_supported(p)) ? -1

@@ -153,6 +153,22 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// The two halves of cluster_sync_all, for a barrier whose arrival comes
+// early and whose wait comes much later (each thread does both, in order).
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+
+// Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned)
+// from this CTA's shared memory to `dst` in another CTA of the cluster (a
+// shared::cluster address from map_to_rank); the copy completes `bytes` of
+// transaction count on the mbarrier `bar` of the destination CTA (also a
+// shared::cluster address).  No multicast.
+__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "r"(smem_u32(src)), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
 __device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, uint4 v) {
   asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "r"(v.x), "r"(v.y), "r"(v.z),
                "r"(v.w)
@@ -223,6 +239,38 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
   return ok != 0;
 }
 
+// Non-blocking test (cluster-scope acquire) of whether the phase with the
+// given parity has completed.  An MMA-issuing thread tests the next stage's
+// barrier while the current stage's last MMAs are still being issued, so
+// the test's latency is not a gap in the tensor pipe (a blocking wait
+// between stages costs ~120 cycles of idle pipe per stage, measured on
+// B200 with back-to-back tf32 MMAs).
+__device__ __forceinline__ bool mbar_test_wait_cluster(uint32_t bar_addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P1;\n\t"
+      "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 P1, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, P1;\n\t}"
+      : "=r"(ok)
+      : "r"(bar_addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// The same test with CTA-scope acquire (the barrier's arrivals come from
+// this CTA).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar_addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P1;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 P1, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, P1;\n\t}"
+      : "=r"(ok)
+      : "r"(bar_addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait for the phase with the given parity to complete.  Returns
 // false (and records `err`) after kWaitLimitNs, or immediately once another
 // role has raised *abort.
@@ -242,6 +290,50 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
       }
     }
   }
+}
+
+// Bounded wait with cluster-scope acquire (data written by the partner CTA
+// before its release-arrive is visible afterwards).
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t* bar, uint32_t parity, int err,
+                                                          volatile int* abort) {
+  const uint32_t addr = smem_u32(bar);
+  const unsigned long long t0 = global_timer_ns();
+  for (uint32_t it = 0;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred P1;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P1, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, P1;\n\t}"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((it & 255u) == 255u) {
+      if (*abort) return false;
+      if (global_timer_ns() - t0 > kWaitLimitNs) {
+        record_device_error(err);
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// Arrive (release, cluster scope) on an mbarrier of any CTA of the cluster.
+// The cluster-scope release orders all of this thread's prior memory
+// operations and costs ~1-2k cycles; use it where the arrival publishes
+// data that another CTA's threads read.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// Arrive on an mbarrier of any CTA of the cluster with the default
+// (CTA-scope) release: the hand-off from a CTA's converter warps to the pair
+// MMA that reads their shared memory and TMEM, after the writer's
+// fence.proxy.async and tcgen05.fence::before_thread_sync.  Measured on
+// B200: ~100 cycles against ~1-2k for the cluster-scope release.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -348,6 +440,30 @@ __device__ __forceinline__ void umma_tf32_a_tmem(uint32_t d_tmem, uint32_t a_tme
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Pair MMA (cta_group::2, issued by the even CTA of the pair), kind::tf32:
+// each CTA's TMEM holds its 128 rows of A at a_tmem and its half of B's
+// columns at the same shared-memory offset; D gets each CTA's 128 rows.
+__device__ __forceinline__ void umma_tf32_pair_a_tmem(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                                      uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` (same offset) in every CTA of the cluster named by `mask`
+// (bit i = CTA rank i) once all prior tcgen05 ops of this thread complete;
+// issued for a pair MMA (cta_group::2).
+__device__ __forceinline__ void umma_commit_pair_mask(uint64_t* bar, uint16_t mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(mask)
       : "memory");
 }
 

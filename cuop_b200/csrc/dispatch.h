@@ -83,6 +83,9 @@ bool gemm_tf32x3_supported(const GemmProblem& p);
 int gemm_tf32x3(const GemmProblem& p, cudaStream_t stream, int bn = 0);  // bn: 0 = choose, 64, 128
 // bn = kTf32x3SplitK2: 128 x 128 tiles, K split over a pair of CTAs (cluster).
 constexpr int kTf32x3SplitK2 = -2;
+// bn = kTf32x3PairSplitK2: 256 x 128 tiles on CTA pairs (cta_group::2), K
+// split over two pairs (a cluster of four); K-major A only.
+constexpr int kTf32x3PairSplitK2 = -3;
 
 // ---- variant selection (host/tuning.cpp) ----
 // GEMM variants a tuning table or an override may name.
@@ -100,7 +103,8 @@ enum GemmVariant : int {
   kVariantTc128x64x2 = 10, // 1-SM tcgen05, 128 x 64 tiles, two CTAs per SM
   kVariantTf32x3_128k2 = 11, // 3xTF32, 128 x 128 tiles, K split over a CTA pair
   kVariantTc2x128 = 12,    // 2-SM tcgen05, 256 x 128 pair tiles
-  kVariantCount = 13,
+  kVariantTf32x3Pair = 13, // 3xTF32, 256 x 128 tiles on CTA pairs, K split over two pairs
+  kVariantCount = 14,
 };
 const char* gemm_variant_name(int v);
 // The override (set by cuopx_set_gemm_variant) if any, else the first

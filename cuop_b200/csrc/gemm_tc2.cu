@@ -109,34 +109,6 @@ struct PairParams {
 };
 
 
-// Bounded wait with cluster-scope acquire (data written by the partner CTA
-// before its release-arrive is visible afterwards).
-__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t* bar, uint32_t parity, int err,
-                                                          volatile int* abort) {
-  const uint32_t addr = smem_u32(bar);
-  const unsigned long long t0 = global_timer_ns();
-  for (uint32_t it = 0;; ++it) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred P1;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P1, [%1], %2;\n\t"
-        "selp.b32 %0, 1, 0, P1;\n\t}"
-        : "=r"(ok)
-        : "r"(addr), "r"(parity)
-        : "memory");
-    if (ok) return true;
-    if ((it & 255u) == 255u) {
-      if (*abort) return false;
-      if (global_timer_ns() - t0 > kWaitLimitNs) {
-        record_device_error(err);
-        *abort = 1;
-        return false;
-      }
-    }
-  }
-}
-
-
 // Next pair tile from a completed launch-control response (the cancelled
 // cluster's first CTA index / 2); false when none was left.
 __device__ __forceinline__ bool clc_next_pair_tile(const void* resp, int num_tiles, int& next) {
@@ -150,9 +122,6 @@ __device__ __forceinline__ bool clc_next_pair_tile(const void* resp, int num_til
   return true;
 }
 
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
 
 // TMA load into this CTA's smem, completing bytes on the mbarrier at a
 // shared::cluster address (the leader's), no multicast.

@@ -36,7 +36,7 @@ const char* const kVariantNames[kVariantCount] = {"auto",          "tc2",       
                                                   "tc_128x128",    "tf32x3_128x64", "tf32x3_128x128",
                                                   "ffma",          "generic",       "tc2_256x512",
                                                   "tc_128x128_2cta", "tc_128x64_2cta", "tf32x3_128x128_k2",
-                                                  "tc2_256x128"};
+                                                  "tc2_256x128",   "tf32x3_256x128_pair"};
 
 struct Range {
   int64_t lo = 0, hi = INT64_MAX;

@@ -372,10 +372,60 @@ def test_f32_tf32x3_split_k_pair(dev, batch, M, N, K, tA, tB):
         assert O.rel_frobenius(Cr.cpu().numpy(), ref) <= 0.1 * 1e-5 * np.sqrt(K)
 
 
-def test_f32_1024_default_takes_split_k(dev):
-    """C1 (1024^3, 64 tiles of 128 x 128) fills the part with K split over
-    CTA pairs."""
+PAIR_CASES = [  # (batch, M, N, K, transB); A is K-major (the pair kernel splits A into TMEM)
+    (1, 1024, 1024, 1024, False), (1, 512, 512, 512, False), (1, 300, 200, 500, False),
+    (1, 384, 320, 1000, True), (2, 256, 264, 96, True), (3, 200, 136, 384, False), (1, 128, 128, 64, False),
+]
+
+
+@pytest.mark.parametrize("batch,M,N,K,tB", PAIR_CASES)
+def test_f32_tf32x3_pair_split_k(dev, batch, M, N, K, tB):
+    """3xTF32 on CTA pairs (tcgen05 cta_group::2, 256 x 128 tiles, each CTA
+    splitting its A rows into its own TMEM and holding half of B) with K
+    split over two pairs: within a tenth of the fp32 bound of an fp64
+    product, with alpha/beta, ragged M/N/K and a fused bias + ReLU, and the
+    same bits on every run."""
+    A32 = O.uniform((batch, M, K), seed=M + K)
+    B32 = O.uniform((batch, N, K) if tB else (batch, K, N), seed=N + 1)
+    C32 = O.uniform((batch, M, N), seed=7)
+    A, B = to_dev_f32(A32, dev), to_dev_f32(B32, dev)
+    outs = []
+    for _ in range(2):
+        Cd = to_dev_f32(C32, dev)
+        with forced_variant("tf32x3_256x128_pair"):
+            cx.batched_gemm(A, B, Cd, transB=tB, alpha=0.75, beta=-0.5)
+        assert cx.last_kernel() == "gemm_tf32x3_256x128_pair_k2", cx.last_kernel()
+        outs.append(Cd)
+    assert cx.device_error() == 0
+    assert torch.equal(outs[0], outs[1])
+    opB = np.swapaxes(B32, 1, 2) if tB else B32
+    exact = 0.75 * np.einsum("bmk,bkn->bmn", A32.astype(np.float64), opB.astype(np.float64)) - 0.5 * C32
+    assert O.rel_frobenius(outs[0].cpu().numpy(), exact) <= 0.1 * 1e-5 * np.sqrt(K)
+    if batch == 1 and not tB:
+        bias = to_dev_f32(O.uniform(N, seed=9), dev)
+        with forced_variant("tf32x3_256x128_pair"):
+            Cr = cx.gemm(A[0], B[0], bias=bias, relu=True)
+        assert cx.last_kernel() == "gemm_tf32x3_256x128_pair_k2", cx.last_kernel()
+        ref = np.maximum(A32[0].astype(np.float64) @ B32[0].astype(np.float64) + bias.double().cpu().numpy(), 0.0)
+        assert O.rel_frobenius(Cr.cpu().numpy(), ref) <= 0.1 * 1e-5 * np.sqrt(K)
+
+
+def test_f32_tf32x3_pair_falls_back_for_mn_major_a(dev):
+    """The pair kernel takes K-major A only: a transposed A forced onto it
+    runs the one-CTA split instead, with the same accuracy."""
+    A32 = O.uniform((512, 256), seed=3)  # A^T stored: (K, M)
+    B32 = O.uniform((512, 384), seed=4)
+    with forced_variant("tf32x3_256x128_pair"):
+        C = cx.gemm(to_dev_f32(A32, dev), to_dev_f32(B32, dev), transA=True)
+    assert cx.last_kernel() == "gemm_tf32x3_128x128_k2", cx.last_kernel()
+    exact = A32.T.astype(np.float64) @ B32.astype(np.float64)
+    assert O.rel_frobenius(C.cpu().numpy(), exact) <= 0.1 * 1e-5 * np.sqrt(512)
+
+
+def test_f32_1024_default_takes_pair_split_k(dev):
+    """C1 (1024^3: 32 tiles of 256 x 128) fills the part with CTA pairs and K
+    split over two pairs (128 CTAs)."""
     A = to_dev_f32(O.uniform((1024, 1024), seed=0), dev)
     B = to_dev_f32(O.uniform((1024, 1024), seed=1), dev)
     cx.gemm(A, B)
-    assert cx.last_kernel() == "gemm_tf32x3_128x128_k2"
+    assert cx.last_kernel() == "gemm_tf32x3_256x128_pair_k2"
