@@ -47,6 +47,7 @@ SIGNATURES = [
     ("cuopx_set_fp32_gemm_mode", _int, [_int]),
     ("cuopx_get_fp32_gemm_mode", _int, []),
     ("cuopx_last_kernel", C.c_char_p, []),
+    ("cuopx_last_cuda_error", C.c_char_p, []),
     ("cuopx_launch_count", _i64, []),
     ("cuopx_get_device_error", _int, [C.POINTER(_int)]),
     ("cuopx_clear_device_error", _int, []),
@@ -117,4 +118,6 @@ def lib() -> C.CDLL:
 
 def check(code: int, what: str) -> None:
     if code != SUCCESS:
+        if code == CUDA_ERROR:
+            what = f"{what} [{lib().cuopx_last_cuda_error().decode()}]"
         raise CuopError(code, what)

@@ -14,6 +14,9 @@ namespace cuopx {
 
 namespace {
 thread_local const char* t_last_kernel = "none";
+// Why the last CUOPX_CUDA_ERROR on this host thread happened (a CUDA error
+// name, or a short text for driver-API failures).
+thread_local const char* t_last_cuda_error = "none";
 std::atomic<int64_t> g_launches{0};
 std::atomic<int> g_sm_count[64] = {};
 
@@ -94,7 +97,20 @@ void note_launch(const char* name) {
   g_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
-int check_launch() { return cudaGetLastError() == cudaSuccess ? CUOPX_SUCCESS : CUOPX_CUDA_ERROR; }
+int check_launch() {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CUOPX_SUCCESS : cuda_failure(e);
+}
+
+int cuda_failure(cudaError_t e) {
+  t_last_cuda_error = cudaGetErrorName(e);
+  return CUOPX_CUDA_ERROR;
+}
+
+int cuda_failure_text(const char* what) {
+  t_last_cuda_error = what;
+  return CUOPX_CUDA_ERROR;
+}
 
 size_t vector_workspace_size_impl();
 int vector_reduce(int op, int64_t n, const float* x, int64_t incx, const float* y, int64_t incy, float* fres,
@@ -217,6 +233,7 @@ int cuopx_set_fp32_gemm_mode(int mode) {
 int cuopx_get_fp32_gemm_mode(void) { return g_fp32_mode.load(); }
 
 const char* cuopx_last_kernel(void) { return t_last_kernel; }
+const char* cuopx_last_cuda_error(void) { return t_last_cuda_error; }
 
 int64_t cuopx_launch_count(void) { return g_launches.load(); }
 

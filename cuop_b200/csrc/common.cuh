@@ -153,6 +153,12 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// Named barrier `id` (1..15; 0 is __syncthreads) over `threads` threads
+// (a multiple of 32; whole warps).
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 // The two halves of cluster_sync_all, for a barrier whose arrival comes
 // early and whose wait comes much later (each thread does both, in order).
 __device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }

@@ -20,6 +20,10 @@ void note_launch(const char* name);
 
 // cudaGetLastError -> CUOPX_SUCCESS / CUOPX_CUDA_ERROR.
 int check_launch();
+// Record why a call fails with CUOPX_CUDA_ERROR (cuopx_last_cuda_error) and
+// return CUOPX_CUDA_ERROR.
+int cuda_failure(cudaError_t e);
+int cuda_failure_text(const char* what);
 // Process-wide fp32 arithmetic mode (cuopx_set_fp32_gemm_mode).
 int fp32_mode();
 

@@ -537,7 +537,10 @@ bool make_map_es(CUtensorMap* map, CUtensorMapDataType dt, int es, const void* b
                  int64_t batch, int64_t ld, int64_t bstride, int box_inner, int box_rows,
                  CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto enc = get_encode_fn();
-  if (!enc) return false;
+  if (!enc) {
+    cuda_failure_text("cuTensorMapEncodeTiled unavailable");
+    return false;
+  }
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows),
                         static_cast<cuuint64_t>(batch)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld * es),
@@ -547,6 +550,7 @@ bool make_map_es(CUtensorMap* map, CUtensorMapDataType dt, int es, const void* b
   CUresult r = enc(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) cuda_failure_text("cuTensorMapEncodeTiled failed");
   return r == CUDA_SUCCESS;
 }
 
@@ -618,10 +622,11 @@ int launch_tc(const GemmProblem& p, cudaStream_t stream, const char* name, void*
   // One CTA per tile; running CTAs take over unlaunched ones' tiles.  The
   // launch may overlap the previous kernel's tail (programmatic dependent
   // launch; the kernel waits before touching global memory).
-  if (launch_pdl(kern, dim3(static_cast<unsigned>(prm.num_tiles)), dim3(NUM_THREADS), L::ALLOC, stream, mA, mB, mC,
-                 prm) != cudaSuccess) {
+  const cudaError_t lerr =
+      launch_pdl(kern, dim3(static_cast<unsigned>(prm.num_tiles)), dim3(NUM_THREADS), L::ALLOC, stream, mA, mB, mC, prm);
+  if (lerr != cudaSuccess) {
     cudaGetLastError();
-    return CUOPX_CUDA_ERROR;
+    return cuda_failure(lerr);
   }
   note_launch(name);
   return check_launch();

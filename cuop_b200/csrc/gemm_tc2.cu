@@ -625,10 +625,11 @@ int launch_tc2(const GemmProblem& p, cudaStream_t stream, const char* name, void
     attr_set[dev].store(true, std::memory_order_relaxed);
   }
   // One cluster per pair tile; running clusters take over unlaunched ones.
-  if (launch_pdl(kern, dim3(static_cast<unsigned>(prm.num_tiles * 2)), dim3(P_THREADS), L::ALLOC, stream, mA, mB, mC,
-                 prm) != cudaSuccess) {
+  const cudaError_t lerr = launch_pdl(kern, dim3(static_cast<unsigned>(prm.num_tiles * 2)), dim3(P_THREADS), L::ALLOC,
+                                     stream, mA, mB, mC, prm);
+  if (lerr != cudaSuccess) {
     cudaGetLastError();
-    return CUOPX_CUDA_ERROR;
+    return cuda_failure(lerr);
   }
   note_launch(name);
   return check_launch();

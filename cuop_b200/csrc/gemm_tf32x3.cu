@@ -618,7 +618,7 @@ int launch_x3(const GemmProblem& p, cudaStream_t stream, const char* name) {
   }
   if (err != cudaSuccess) {
     cudaGetLastError();
-    return CUOPX_CUDA_ERROR;
+    return cuda_failure(err);
   }
   note_launch(name);
   return check_launch();
@@ -660,11 +660,19 @@ int launch_x3_layout(const GemmProblem& p, cudaStream_t stream, const char* name
 //               staged B half; arrive on the even CTA's `conv` barrier
 // K-major A only (A in TMEM); B either layout.  No TMA multicast.
 constexpr int XP_BN = 128;     // pair tile columns (64 of B per CTA)
-constexpr int XP_STAGES = 6;   // TMEM: 128 accumulator columns + 6 x 64 of A = 512
+// A stage is XP_SUB sub-blocks of 32 K (one 128-byte swizzle row each): the
+// MMA thread waits once per 24 MMAs.  A wait whose result the issuing thread
+// consumes leaves the tensor pipe idle for part of it (the pipe queues about
+// one 64-cycle MMA ahead), so fewer, larger stages lose less.
+constexpr int XP_SUB = 2;
+constexpr int XP_BK = XP_SUB * X3_BK;  // 64
+constexpr int XP_STAGES = 3;   // TMEM: 128 accumulator columns + 3 x 128 of A = 512
 
 struct XPSmem {
-  static constexpr int A_BYTES = X3_BM * X3_BK * 4;        // 16 KB
-  static constexpr int B_BYTES = (XP_BN / 2) * X3_BK * 4;  // 8 KB: this CTA's half
+  static constexpr int A_SUB = X3_BM * X3_BK * 4;          // 16 KB: one 32-deep sub-block of A
+  static constexpr int B_SUB = (XP_BN / 2) * X3_BK * 4;    // 8 KB: this CTA's half of B, one sub-block
+  static constexpr int A_BYTES = XP_SUB * A_SUB;
+  static constexpr int B_BYTES = XP_SUB * B_SUB;
   static constexpr int STAGE = A_BYTES + 2 * B_BYTES;      // A, B (its own hi), B lo
   static constexpr int C_STAGE = 32 * X3_CHUNK * 4;        // 4 KB
   static constexpr int OWN = XP_BN / 2;                    // columns each K half finishes
@@ -681,9 +689,14 @@ struct XPSmem {
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int ALLOC = OFF_MISC + 16 + 1024;
   static_assert(ALLOC <= 232448, "shared memory budget exceeded");
-  __device__ static unsigned char* a(unsigned char* s, int st) { return s + st * STAGE; }
-  __device__ static unsigned char* b_hi(unsigned char* s, int st) { return s + st * STAGE + A_BYTES; }
-  __device__ static unsigned char* b_lo(unsigned char* s, int st) { return s + st * STAGE + A_BYTES + B_BYTES; }
+  // Sub-block j of stage st.
+  __device__ static unsigned char* a(unsigned char* s, int st, int j) { return s + st * STAGE + j * A_SUB; }
+  __device__ static unsigned char* b_hi(unsigned char* s, int st, int j) {
+    return s + st * STAGE + A_BYTES + j * B_SUB;
+  }
+  __device__ static unsigned char* b_lo(unsigned char* s, int st, int j) {
+    return s + st * STAGE + A_BYTES + B_BYTES + j * B_SUB;
+  }
 };
 
 template <bool B_MN, int CG>
@@ -696,7 +709,7 @@ __global__ void __launch_bounds__(x3_threads(CG), 1)
   constexpr uint32_t CHUNK_BYTES = 32 * X3_BK * 4;  // one 32 x 32 fp32 box = 4 KB
   constexpr uint32_t TMEM_COLS = 512;
   constexpr uint32_t A_COL0 = XP_BN;  // accumulator: columns [0, 128)
-  static_assert(A_COL0 + XP_STAGES * 2 * X3_BK <= TMEM_COLS, "TMEM budget");
+  static_assert(A_COL0 + XP_STAGES * 2 * XP_BK <= TMEM_COLS, "TMEM budget");
   constexpr int OWN = L::OWN;
   constexpr int CPO = OWN / X3_CHUNK;  // store chunks per K half
   constexpr int W = X3_CONV_PER_GROUP;
@@ -742,20 +755,26 @@ __global__ void __launch_bounds__(x3_threads(CG), 1)
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
   }
+  __syncthreads();  // barrier inits visible in the CTA
+  // The producer starts loading at once; the pair's TMEM allocation (which
+  // the other roles need) runs meanwhile, published to them on named
+  // barrier 1.
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(TMEM_COLS)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    tc_fence_before_sync();
   }
-  tc_fence_before_sync();
-  __syncthreads();
+  if (warp != 0) {
+    named_bar_sync(1, x3_threads(CG) - 32);
+    tc_fence_after_sync();
+  }
   // Barrier inits and TMEM allocations are published to the cluster here and
   // waited for just before each role's first cross-CTA operation, so the
   // first loads overlap the cluster barrier.
   cluster_arrive();
-  tc_fence_after_sync();
-  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t tmem_base = warp != 0 ? *tmem_slot : 0u;
   grid_dependency_wait();
 
   if (warp == 0) {
@@ -772,14 +791,18 @@ __global__ void __launch_bounds__(x3_threads(CG), 1)
           break;
         }
         mbar_arrive_expect_tx(&full[stage], STAGE_TX);
-        const int k0 = kb * X3_BK;
-        tma_load_3d(L::a(smem, stage), &tmA, &full[stage], k0, m0, b);
-        unsigned char* sb = L::b_hi(smem, stage);
-        if constexpr (B_MN) {
 #pragma unroll
-          for (int j = 0; j < (XP_BN / 2) / 32; ++j) tma_load_3d(sb + j * CHUNK_BYTES, &tmB, &full[stage], nb + 32 * j, k0, b);
-        } else {
-          tma_load_3d(sb, &tmB, &full[stage], k0, nb, b);
+        for (int j = 0; j < XP_SUB; ++j) {
+          const int k0 = kb * XP_BK + j * X3_BK;  // past K: the TMA fills zeros
+          tma_load_3d(L::a(smem, stage, j), &tmA, &full[stage], k0, m0, b);
+          unsigned char* sb = L::b_hi(smem, stage, j);
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int c = 0; c < (XP_BN / 2) / 32; ++c)
+              tma_load_3d(sb + c * CHUNK_BYTES, &tmB, &full[stage], nb + 32 * c, k0, b);
+          } else {
+            tma_load_3d(sb, &tmB, &full[stage], k0, nb, b);
+          }
         }
         issued_mask |= 1u << stage;
         phase_mask = (phase_mask & ~(1u << stage)) | (phase << stage);
@@ -822,28 +845,34 @@ __global__ void __launch_bounds__(x3_threads(CG), 1)
     for (int kb = kb0; kb < kb1; ++kb, ++seq) {
       if (seq % CG == grp) {
         if (!mbar_wait_bounded(&full[stage], phase, kDevErrWaitTimeoutFull, abort_flag)) break;
-        // Row r of the A stage (128 swizzled bytes) -> hi, lo into TMEM.
-        const unsigned char* arow = L::a(smem, stage) + r * 128;
-        uint32_t hi[2][16], lo[2][16];
+        // Row r of each A sub-block (128 swizzled bytes) -> hi, lo into
+        // TMEM: sub-block sb at stage columns [64 sb, 64 sb + 32) (hi) and
+        // [64 sb + 32, 64 sb + 64) (lo).
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const float4 v = *reinterpret_cast<const float4*>(arow + ((c ^ (r & 7)) << 4));
-          const float e[4] = {v.x, v.y, v.z, v.w};
+        for (int sb = 0; sb < XP_SUB; ++sb) {
+          const unsigned char* arow = L::a(smem, stage, sb) + r * 128;
+          uint32_t hi[2][16], lo[2][16];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int j = 4 * c + i;
-            hi[j / 16][j % 16] = to_tf32_rna(e[i]);
-            lo[j / 16][j % 16] = __float_as_uint(__fsub_rn(e[i], __uint_as_float(hi[j / 16][j % 16])));
+          for (int c = 0; c < 8; ++c) {
+            const float4 v = *reinterpret_cast<const float4*>(arow + ((c ^ (r & 7)) << 4));
+            const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int j = 4 * c + i;
+              hi[j / 16][j % 16] = to_tf32_rna(e[i]);
+              lo[j / 16][j % 16] = __float_as_uint(__fsub_rn(e[i], __uint_as_float(hi[j / 16][j % 16])));
+            }
+          }
+          const uint32_t tcol = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + A_COL0 +
+                                static_cast<uint32_t>(stage * 2 * XP_BK + sb * 2 * X3_BK);
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            tmem_st_32x32b_x16(tcol + 16 * u, hi[u]);
+            tmem_st_32x32b_x16(tcol + X3_BK + 16 * u, lo[u]);
           }
         }
-        const uint32_t tcol =
-            tmem_base + (static_cast<uint32_t>(32 * q) << 16) + A_COL0 + static_cast<uint32_t>(stage * 2 * X3_BK);
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          tmem_st_32x32b_x16(tcol + 16 * u, hi[u]);
-          tmem_st_32x32b_x16(tcol + X3_BK + 16 * u, lo[u]);
-        }
-        split_tf32_lo<L::B_BYTES, W * 32>(L::b_hi(smem, stage), L::b_lo(smem, stage), gtid);
+        // The B sub-blocks are contiguous, and so are their lo parts.
+        split_tf32_lo<L::B_BYTES, W * 32>(L::b_hi(smem, stage, 0), L::b_lo(smem, stage, 0), gtid);
         tmem_wait_st();
         tc_fence_before_sync();
         fence_proxy_async_shared();  // generic-proxy writes -> visible to the tensor cores
@@ -869,20 +898,25 @@ __global__ void __launch_bounds__(x3_threads(CG), 1)
         const int next = stage + 1 == XP_STAGES ? 0 : stage + 1;
         const uint32_t next_phase = next == 0 ? phase ^ 1u : phase;
         ready = false;
-        const uint32_t bh = smem_u32(L::b_hi(smem, stage)), bl = smem_u32(L::b_lo(smem, stage));
 #pragma unroll
-        for (int kk = 0; kk < X3_BK / 8; ++kk) {
-          // Test the next stage while this one's last MMAs are issued.
-          if (kk == X3_BK / 8 - 1 && kb + 1 < kb1) ready = mbar_test_wait_cluster(smem_u32(&conv[next]), next_phase);
-          const uint32_t bo = B_MN ? kk * 1024 : kk * 32;
-          const uint64_t dbh = B_MN ? make_smem_desc_sw128_32b(bh + bo, CHUNK_BYTES, 512)
-                                    : make_smem_desc_sw128(bh + bo, 16, 1024);
-          const uint64_t dbl = B_MN ? make_smem_desc_sw128_32b(bl + bo, CHUNK_BYTES, 512)
-                                    : make_smem_desc_sw128(bl + bo, 16, 1024);
-          const uint32_t ta = tmem_base + A_COL0 + static_cast<uint32_t>(stage * 2 * X3_BK + kk * 8);
-          umma_tf32_pair_a_tmem(tmem_base, ta + X3_BK, dbh, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);  // lo*hi first
-          umma_tf32_pair_a_tmem(tmem_base, ta, dbl, IDESC, 1u);
-          umma_tf32_pair_a_tmem(tmem_base, ta, dbh, IDESC, 1u);
+        for (int sb = 0; sb < XP_SUB; ++sb) {
+          const uint32_t bh = smem_u32(L::b_hi(smem, stage, sb)), bl = smem_u32(L::b_lo(smem, stage, sb));
+#pragma unroll
+          for (int kk = 0; kk < X3_BK / 8; ++kk) {
+            // Test the next stage while this one's last MMAs are issued.
+            if (sb == XP_SUB - 1 && kk == X3_BK / 8 - 1 && kb + 1 < kb1)
+              ready = mbar_test_wait_cluster(smem_u32(&conv[next]), next_phase);
+            const uint32_t bo = B_MN ? kk * 1024 : kk * 32;
+            const uint64_t dbh = B_MN ? make_smem_desc_sw128_32b(bh + bo, CHUNK_BYTES, 512)
+                                      : make_smem_desc_sw128(bh + bo, 16, 1024);
+            const uint64_t dbl = B_MN ? make_smem_desc_sw128_32b(bl + bo, CHUNK_BYTES, 512)
+                                      : make_smem_desc_sw128(bl + bo, 16, 1024);
+            const uint32_t ta =
+                tmem_base + A_COL0 + static_cast<uint32_t>(stage * 2 * XP_BK + sb * 2 * X3_BK + kk * 8);
+            umma_tf32_pair_a_tmem(tmem_base, ta + X3_BK, dbh, IDESC, (kb > kb0 || sb > 0 || kk > 0) ? 1u : 0u);
+            umma_tf32_pair_a_tmem(tmem_base, ta, dbl, IDESC, 1u);  // lo*hi first, then hi*lo, hi*hi
+            umma_tf32_pair_a_tmem(tmem_base, ta, dbh, IDESC, 1u);
+          }
         }
         issued = true;
         umma_commit_pair_mask(&empty[stage], pair_mask);
@@ -936,12 +970,6 @@ __global__ void __launch_bounds__(x3_threads(CG), 1)
     if (lane == 0)
       bulk_copy_to_cluster(map_to_rank(smem + L::OFF_RECV + 32 * q * OWN * 4, dst),
                            smem + L::OFF_SEND + 32 * q * OWN * 4, 32u * OWN * 4u, map_to_rank(recv, dst));
-    uint32_t own[CPO][32];
-    if (got) {
-#pragma unroll
-      for (int c = 0; c < CPO; ++c) tmem_ld_32x32b_x32(t_row + (kh * CPO + c) * X3_CHUNK, own[c]);
-      tmem_wait_ld();
-    }
     const bool landed = mbar_wait_bounded(recv, 0, kDevErrWaitTimeoutFull, abort_flag);
     if (got && landed) {
       const unsigned char* rrow = smem + L::OFF_RECV + row_in_tile * OWN * 4;
@@ -950,9 +978,12 @@ __global__ void __launch_bounds__(x3_threads(CG), 1)
       for (int c = 0; c < CPO; ++c) {
         // Two K halves: p0 + p1 is one IEEE addition (commutative), the
         // same on both sides; the result does not depend on timing.
+        uint32_t own[32];
+        tmem_ld_32x32b_x32(t_row + (kh * CPO + c) * X3_CHUNK, own);
+        tmem_wait_ld();
         float v[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(own[c][i]);
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(own[i]);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const float4 f = *reinterpret_cast<const float4*>(rrow + ((static_cast<uint32_t>(c * 8 + j) ^ rsw) << 4));
@@ -1041,7 +1072,7 @@ int launch_x3_pair(const GemmProblem& p, cudaStream_t stream, const char* name) 
   prm.tiles_m = static_cast<int>((p.M + 2 * X3_BM - 1) / (2 * X3_BM));
   prm.tiles_n = static_cast<int>((p.N + XP_BN - 1) / XP_BN);
   prm.num_tiles = prm.tiles_m * prm.tiles_n * prm.batch;
-  prm.k_blocks = static_cast<int>((p.K + X3_BK - 1) / X3_BK);
+  prm.k_blocks = static_cast<int>((p.K + XP_BK - 1) / XP_BK);  // 64-deep stages
   prm.alpha = static_cast<float>(p.alpha);
   prm.beta = static_cast<float>(p.beta);
   prm.C_in = static_cast<const float*>(p.C);
@@ -1064,7 +1095,7 @@ int launch_x3_pair(const GemmProblem& p, cudaStream_t stream, const char* name) 
                                              L::ALLOC, stream, 4, mA, mB, prm);
   if (err != cudaSuccess) {
     cudaGetLastError();
-    return CUOPX_CUDA_ERROR;
+    return cuda_failure(err);
   }
   note_launch(name);
   return check_launch();
@@ -1105,10 +1136,10 @@ int gemm_tf32x3(const GemmProblem& p, cudaStream_t stream, int bn) {
       bn = (p.N > 64 && tiles128 * 3 >= sms * 2) ? 128 : 64;
     }
   }
-  // Each K half needs at least one K block of its own; the pair kernel
-  // takes K-major A only.
-  if (bn == kTf32x3PairSplitK2 && p.transA) bn = kTf32x3SplitK2;
-  if ((bn == kTf32x3SplitK2 || bn == kTf32x3PairSplitK2) && (p.K + X3_BK - 1) / X3_BK < 2) bn = 128;
+  // Each K half needs at least one K block of its own (64 deep in the pair
+  // kernel); the pair kernel takes K-major A only.
+  if (bn == kTf32x3PairSplitK2 && (p.transA || (p.K + XP_BK - 1) / XP_BK < 2)) bn = kTf32x3SplitK2;
+  if (bn == kTf32x3SplitK2 && (p.K + X3_BK - 1) / X3_BK < 2) bn = 128;
   if (bn == kTf32x3PairSplitK2)
     return p.transB ? launch_x3_pair<false>(p, stream, "gemm_tf32x3_256x128_pair_k2")
                     : launch_x3_pair<true>(p, stream, "gemm_tf32x3_256x128_pair_k2");

@@ -427,17 +427,18 @@ int launch_gemv_stream(int trans, int64_t M, int64_t N, double alpha_d, const vo
     }
     if (e != cudaSuccess) {
       cudaGetLastError();
-      return CUOPX_CUDA_ERROR;
+      return cuda_failure(e);
     }
     note_launch("gemv_n_xreg");
   } else {
     unsigned int* counters = reinterpret_cast<unsigned int*>(ws);
     Acc* partials = reinterpret_cast<Acc*>(static_cast<char*>(ws) + counter_bytes);
     const dim3 grid(static_cast<unsigned>(p.strips), static_cast<unsigned>(p.splits));
-    if (launch_pdl(gemv_t_lsu<T>, grid, dim3(GS_THREADS), 0, stream, M, N, alpha, A, lda, x, beta, y,
-                   p.rows_per_split, partials, counters) != cudaSuccess) {
+    const cudaError_t e = launch_pdl(gemv_t_lsu<T>, grid, dim3(GS_THREADS), 0, stream, M, N, alpha, A, lda, x, beta,
+                                     y, p.rows_per_split, partials, counters);
+    if (e != cudaSuccess) {
       cudaGetLastError();
-      return CUOPX_CUDA_ERROR;
+      return cuda_failure(e);
     }
     note_launch("gemv_t_lsu");
   }

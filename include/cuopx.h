@@ -59,6 +59,10 @@ int cuopx_version(void);
 /* Name of the kernel variant the last successful call on this host thread
  * launched (e.g. "gemm_tc_128x256", "gemv_t_splitk").  Never NULL. */
 const char* cuopx_last_kernel(void);
+/* Why the last call on this host thread that returned CUOPX_CUDA_ERROR
+ * failed: the CUDA runtime error name (e.g. "cudaErrorLaunchOutOfResources")
+ * or a short text for a driver-API failure; "none" before any.  Never NULL. */
+const char* cuopx_last_cuda_error(void);
 /* Number of cuopx kernels launched by this process so far. */
 int64_t cuopx_launch_count(void);
 /* First error code recorded by a device-side bounded wait (0 = none).
