@@ -161,3 +161,15 @@ def test_call_log_is_opt_in():
     off = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=120)
     assert off.returncode == 0 and "cuopx:" not in off.stderr
 
+
+
+def test_last_cuda_error_starts_empty():
+    """cuopx_last_cuda_error names the CUDA error behind a CUOPX_CUDA_ERROR;
+    before any such failure on this thread it is "none" (no GPU needed)."""
+    import threading
+
+    seen = []
+    t = threading.Thread(target=lambda: seen.append(cx.lib().cuopx_last_cuda_error().decode()))
+    t.start()
+    t.join()
+    assert seen == ["none"]
