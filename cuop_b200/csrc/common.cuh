@@ -163,6 +163,12 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
 // early and whose wait comes much later (each thread does both, in order).
 __device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+// Arrival without release semantics (~1 k cycles cheaper than the release
+// form, measured): for threads that publish nothing, or whose mbarrier
+// initialisations were published by fence.mbarrier_init.release.cluster.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
 
 // Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned)
 // from this CTA's shared memory to `dst` in another CTA of the cluster (a

@@ -206,8 +206,9 @@ __global__ void __launch_bounds__(x3_threads(CG), 1)
   __syncthreads();
   tc_fence_after_sync();
   // Split K: the barriers of every CTA of the cluster are initialised before
-  // any rank copies into another (the wait is taken just before that copy).
-  if constexpr (KSPLIT > 1) cluster_arrive();
+  // any rank copies into another (the wait is taken just before that copy;
+  // the inits were released by fence.mbarrier_init).
+  if constexpr (KSPLIT > 1) cluster_arrive_relaxed();
   const uint32_t tmem_base = *tmem_slot;
   // Global memory only after the previous kernel on the stream has completed
   // (programmatic dependent launch).
@@ -772,8 +773,11 @@ __global__ void __launch_bounds__(x3_threads(CG), 1)
   }
   // Barrier inits and TMEM allocations are published to the cluster here and
   // waited for just before each role's first cross-CTA operation, so the
-  // first loads overlap the cluster barrier.
-  cluster_arrive();
+  // first loads overlap the cluster barrier.  Only warp 1 (the TMEM
+  // allocation) needs a releasing arrival; the barrier inits were released by
+  // fence.mbarrier_init.
+  if (warp == 1) cluster_arrive();
+  else cluster_arrive_relaxed();
   const uint32_t tmem_base = warp != 0 ? *tmem_slot : 0u;
   grid_dependency_wait();
 
