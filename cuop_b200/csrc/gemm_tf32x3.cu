@@ -744,7 +744,7 @@ __global__ void __launch_bounds__(x3_threads(CG), 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < XP_STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&conv[s], 2 * W);
+      mbar_init(&conv[s], 2 * CG * W);  // every converter warp of both CTAs
       mbar_init(&empty[s], 1);
     }
     mbar_init(acc_full, 1);
@@ -843,46 +843,42 @@ __global__ void __launch_bounds__(x3_threads(CG), 1)
     const int gtid = threadIdx.x - (6 + grp * W) * 32;
     const int q = warp & 3;  // TMEM lane quarter of this warp
     const int r = 32 * q + lane;
+    // Group g splits sub-block g of every stage (A rows into TMEM, B's lo),
+    // so a stage is ready after half the split work of one group alone.
+    static_assert(CG == XP_SUB, "one converter group per sub-block");
+    const int sb = grp;
     int stage = 0;
     uint32_t phase = 0;
-    int seq = 0;
-    for (int kb = kb0; kb < kb1; ++kb, ++seq) {
-      if (seq % CG == grp) {
-        if (!mbar_wait_bounded(&full[stage], phase, kDevErrWaitTimeoutFull, abort_flag)) break;
-        // Row r of each A sub-block (128 swizzled bytes) -> hi, lo into
-        // TMEM: sub-block sb at stage columns [64 sb, 64 sb + 32) (hi) and
-        // [64 sb + 32, 64 sb + 64) (lo).
+    for (int kb = kb0; kb < kb1; ++kb) {
+      if (!mbar_wait_bounded(&full[stage], phase, kDevErrWaitTimeoutFull, abort_flag)) break;
+      // Row r of A sub-block sb (128 swizzled bytes) -> hi, lo into TMEM
+      // stage columns [64 sb, 64 sb + 32) (hi) and [64 sb + 32, 64 sb + 64) (lo).
+      const unsigned char* arow = L::a(smem, stage, sb) + r * 128;
+      uint32_t hi[2][16], lo[2][16];
 #pragma unroll
-        for (int sb = 0; sb < XP_SUB; ++sb) {
-          const unsigned char* arow = L::a(smem, stage, sb) + r * 128;
-          uint32_t hi[2][16], lo[2][16];
+      for (int c = 0; c < 8; ++c) {
+        const float4 v = *reinterpret_cast<const float4*>(arow + ((c ^ (r & 7)) << 4));
+        const float e[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const float4 v = *reinterpret_cast<const float4*>(arow + ((c ^ (r & 7)) << 4));
-            const float e[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int j = 4 * c + i;
-              hi[j / 16][j % 16] = to_tf32_rna(e[i]);
-              lo[j / 16][j % 16] = __float_as_uint(__fsub_rn(e[i], __uint_as_float(hi[j / 16][j % 16])));
-            }
-          }
-          const uint32_t tcol = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + A_COL0 +
-                                static_cast<uint32_t>(stage * 2 * XP_BK + sb * 2 * X3_BK);
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            tmem_st_32x32b_x16(tcol + 16 * u, hi[u]);
-            tmem_st_32x32b_x16(tcol + X3_BK + 16 * u, lo[u]);
-          }
+        for (int i = 0; i < 4; ++i) {
+          const int j = 4 * c + i;
+          hi[j / 16][j % 16] = to_tf32_rna(e[i]);
+          lo[j / 16][j % 16] = __float_as_uint(__fsub_rn(e[i], __uint_as_float(hi[j / 16][j % 16])));
         }
-        // The B sub-blocks are contiguous, and so are their lo parts.
-        split_tf32_lo<L::B_BYTES, W * 32>(L::b_hi(smem, stage, 0), L::b_lo(smem, stage, 0), gtid);
-        tmem_wait_st();
-        tc_fence_before_sync();
-        fence_proxy_async_shared();  // generic-proxy writes -> visible to the tensor cores
-        __syncwarp();
-        if (lane == 0) mbar_arrive_remote(map_to_rank(&conv[stage], even));
       }
+      const uint32_t tcol = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + A_COL0 +
+                            static_cast<uint32_t>(stage * 2 * XP_BK + sb * 2 * X3_BK);
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        tmem_st_32x32b_x16(tcol + 16 * u, hi[u]);
+        tmem_st_32x32b_x16(tcol + X3_BK + 16 * u, lo[u]);
+      }
+      split_tf32_lo<L::B_SUB, W * 32>(L::b_hi(smem, stage, sb), L::b_lo(smem, stage, sb), gtid);
+      tmem_wait_st();
+      tc_fence_before_sync();
+      fence_proxy_async_shared();  // generic-proxy writes -> visible to the tensor cores
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(map_to_rank(&conv[stage], even));
       if (++stage == XP_STAGES) stage = 0, phase ^= 1u;
     }
   } else if (warp == 1) {
