@@ -656,9 +656,13 @@ int launch_x3_layout(const GemmProblem& p, cudaStream_t stream, const char* name
 //   warps 2..5  epilogue: as the one-CTA split — CTA r of half h finishes
 //               output columns [64h, 64h+64) of its 128 rows, after one bulk
 //               copy per warp has brought the other half's partial sums of
-//               them (from cluster rank r ^ 2) into its `recv` area
-//   warps 6..   converters: A rows into this CTA's TMEM, B lo next to the
-//               staged B half; arrive on the even CTA's `conv` barrier
+//               them (from cluster rank r ^ 2) into its `recv` area; the
+//               outputs leave through a swizzled staging buffer as plain
+//               coalesced stores
+//   warps 6..   converters, one group of four per 32-deep sub-block of a
+//               stage: A rows into this CTA's TMEM, B lo next to the staged
+//               B half; every converter warp arrives on the even CTA's
+//               `conv` barrier
 // K-major A only (A in TMEM); B either layout.  No TMA multicast.
 constexpr int XP_BN = 128;     // pair tile columns (64 of B per CTA)
 // A stage is XP_SUB sub-blocks of 32 K (one 128-byte swizzle row each): the
