@@ -199,17 +199,19 @@ def batched_gemm_host(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, *, alph
     per_batch = (M * K + K * B.size(2) + M * B.size(2)) * A.element_size()
     if chunk is None:  # about 8 chunks, each moving at least 8 MiB (measured best on B200 over PCIe 5)
         chunk = max(1, min(batch, max((8 << 20) // per_batch, -(-batch // 8))))
-    # Chunk boundaries: the first and the last chunk are half size, so that
-    # the copy-in before the first GEMM and the copy-out after the last one,
-    # which nothing overlaps, are short.
+    # Chunk boundaries: the first and the last chunk are a quarter size, so
+    # that the copy-in before the first GEMM and the copy-out after the last
+    # one, which nothing overlaps, are short.  (Measured on a C4 step over
+    # PCIe 5: the copy-in direction is busy throughout at ~42 GB/s while the
+    # copy-out runs beside it; quarter-size edges gain ~1 % over half-size.)
     bounds = []
     b0 = 0
-    first = max(1, chunk // 2)
+    edge = max(1, chunk // 4)
     while b0 < batch:
         rest = batch - b0
-        n = first if b0 == 0 else chunk
-        if b0 > 0 and rest <= chunk + chunk // 2:  # tail: split what is left into two, the last half size
-            n = rest - chunk // 2 if rest > chunk // 2 and chunk // 2 > 0 else rest
+        n = edge if b0 == 0 else chunk
+        if b0 > 0 and rest <= chunk + edge:  # tail: split what is left into two, the last one edge-sized
+            n = rest - edge if rest > edge else rest
         n = min(n, rest)
         bounds.append((b0, b0 + n))
         b0 += n
